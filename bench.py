@@ -1,0 +1,445 @@
+"""Benchmark of the paged KV hot path on B200: BASELINE config 2 (Llama-3.1-8B decode-attention shape).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (KV-head sharding, NCCL all-gather)
+
+Workload (config 2): bf16, 32 query heads, 8 KV heads, head_dim 128, block_size 16, batch 64, context
+lengths U[512, 4096] (seeded), block tables a seeded shuffle of a pool sized 1.25x the blocks needed,
+K/V ~ 0.5 N(0,1), Q ~ N(0,1).  One STEP = one decode step of all 32 layers: per layer, append one token
+per sequence (K1) and run paged attention over the context (K2a + K2b), each layer on its own pool
+(32 x 740 MB: every layer's reads are far larger than the 126 MB L2, so no flush is needed).
+Synthetic data (no checkpoint or dataset): the kernels' cost depends only on shapes and lengths.
+
+Metric: KV-read GB/s = algorithmic K+V bytes the attention must read (sum of contexts x 2 x Hkv x Dh x 2 B,
+every layer) / step time, summed over ranks (value), with seqs/s and append GB/s alongside.  The
+`reference` arm times the reference's CPU algorithm (the oracle port of paged_torch_ref.py) on the
+host cores with the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+PACKAGE = "mini-llm-inference-server_b200"
+H, HKV, DH, BS = 32, 8, 128, 16
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ----------------------------------------------------------------------------- workload
+
+
+def config2(batch: int, seed: int = 1234):
+    """Seeded config-2 step: contexts (after the append), block tables, pool size."""
+    r = np.random.default_rng(seed)
+    ctx = r.integers(512, 4097, size=batch).astype(np.int64)
+    pages = -(-ctx // BS)
+    nb = int(math.ceil(1.25 * int(pages.sum())))
+    perm = r.permutation(nb)
+    offs = np.concatenate([[0], np.cumsum(pages)])
+    blocks = [perm[offs[i]:offs[i + 1]].tolist() for i in range(batch)]
+    return ctx, blocks, nb
+
+
+def kv_bytes(ctx, hkv: int, elt: int = 2) -> int:
+    return int(np.sum(ctx)) * 2 * hkv * DH * elt
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.idx = device_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.idx)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.25)
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- helpers
+
+
+def measured_peak() -> tuple[float, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic() -> int | None:
+    """DRAM bytes per attention launch from the committed ncu summary (None until one is captured)."""
+    p = REPO / "profiles" / "paged_attention_cfg2.md"
+    if not p.exists():
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", p.read_text())
+    return int(m.group(1)) if m else None
+
+
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------------------- CPU reference leg
+
+
+def cpu_reference_step(ctx, blocks, nb_sample_seqs: int, seed: int = 7):
+    """Build the oracle's inputs for a bounded sample of the config-2 step (first `nb_sample_seqs`
+    sequences, one layer, pool holding just their blocks) and return a callable that runs one step."""
+    sys.path.insert(0, str(REPO))
+    import oracle  # the reference's CPU algorithm (paged_torch_ref.py restated): the baseline, not the product
+
+    sel = list(range(nb_sample_seqs))
+    sctx = [int(ctx[i]) for i in sel]
+    sblocks, nxt = [], 0
+    for i in sel:  # renumber the sample's blocks densely: a small pool, same access pattern per sequence
+        sblocks.append(list(range(nxt, nxt + len(blocks[i]))))
+        nxt += len(blocks[i])
+    g = torch.Generator().manual_seed(seed)
+    k_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    v_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    q = torch.randn(len(sel), H, DH, generator=g).to(torch.bfloat16)
+    k = (torch.randn(len(sel), HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(len(sel), HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    meta = oracle.build_metadata([(c - 1, 1, b) for c, b in zip(sctx, sblocks)], BS)
+
+    def step():
+        oracle.forward(q, k, v, k_pool, v_pool, meta, compute_dtype=None)  # the reference's own dtype: bf16
+
+    return step, kv_bytes(sctx, HKV), f"{len(sel)} of 64 sequences (sum ctx {sum(sctx)}), 1 layer, bf16"
+
+
+def run_cpu_baseline(ctx, blocks, seqs: int, reps: int, warmup: int = 1) -> dict:
+    step, nbytes, sample = cpu_reference_step(ctx, blocks, seqs)
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        step()
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": sample + f", {reps} reps", "ms_per_step": round(dt * 1e3, 2)}
+
+
+def run_reference_arm(args) -> None:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return  # the CPU arm runs once, on rank 0 only
+    torch.set_num_threads(os.cpu_count() or 1)
+    ctx, blocks, _ = config2(args.batch)
+    step, nbytes, sample = cpu_reference_step(ctx, blocks, args.cpu_sample_seqs)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = nbytes / dt / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config 2: Llama-3.1-8B decode attention, B64 ctx U[512,4096], bf16",
+                   "sample": sample},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+METRIC = "Llama-3.1-8B paged decode attn: KV-read GB/s vs HBM peak, seqs/s; append GB/s"
+
+
+# ----------------------------------------------------------------------------- our arm
+
+
+def run_ours(args) -> None:
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    mlb = importlib.import_module(PACKAGE)
+    sharding = importlib.import_module(PACKAGE + ".sharding")
+    ops = mlb.ops
+
+    hkv_l, h_l = HKV // world, H // world
+    ctx, blocks, nb = config2(args.batch)
+    seqs = [mlb.SeqStep(int(c) - 1, 1, b) for c, b in zip(ctx, blocks)]
+    layers = args.layers
+
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    k_pools, v_pools = [], []
+    for _ in range(layers):
+        for pools in (k_pools, v_pools):
+            p = torch.empty(nb, BS, hkv_l, DH, device=dev, dtype=torch.bfloat16)
+            p.normal_(0.0, 0.5, generator=g)
+            pools.append(p)
+    gq = torch.Generator(device=dev).manual_seed(7)  # the same full q/k/v on every rank
+    q = torch.randn(args.batch, H, DH, device=dev, generator=gq).to(torch.bfloat16)
+    k = (torch.randn(args.batch, HKV, DH, device=dev, generator=gq) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(args.batch, HKV, DH, device=dev, generator=gq) * 0.5).to(torch.bfloat16)
+    qs = sharding.head_range(rank, world, H)
+    ks = sharding.head_range(rank, world, HKV)
+    q_l, k_l, v_l = q[:, qs], k[:, ks], v[:, ks]
+
+    meta = mlb.AttentionMetadata.build(seqs, BS, dev)
+    backend = mlb.B200Backend()
+    plan = backend.plan(meta, h_l, hkv_l, dev)
+    ws = ops.Workspace()
+    out_l = torch.empty(args.batch, h_l, DH, device=dev, dtype=torch.bfloat16)
+    gathered = torch.empty(world * args.batch, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 else None
+    launches_per_layer = 2 + (1 if plan.num_partial_rows else 0)
+
+    def layer_step(l, ev=None):
+        ops.kv_append(k_pools[l], v_pools[l], meta.slot_mapping, k_l, v_l)
+        if ev is not None:
+            ev[0].record()
+        ops.attention_partials(q_l, k_pools[l], v_pools[l], meta.block_tables_i32, meta.seq_lens_i32,
+                               meta.qo_indptr, plan, ws, out_l)
+        if ev is not None:
+            ev[1].record()
+        ops.splitk_reduce(plan, ws, out_l)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(gathered, out_l)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # --- device-resident timing (value) with per-launch events around the attention kernel
+    for _ in range(args.warmup):
+        for l in range(layers):
+            layer_step(l)
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
+           for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        start.record()
+        for s in range(args.steps):
+            for l in range(layers):
+                layer_step(l, evs[s][l])
+        end.record()
+        barrier()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end), world, dev)
+    attn_ms = [e0.elapsed_time(e1) for step in evs for (e0, e1) in step]
+    attn_avg_ms = max_over_ranks(statistics.mean(attn_ms), world, dev)
+    ms_per_step = elapsed_ms / args.steps
+
+    bytes_rank_layer = kv_bytes(ctx, hkv_l)
+    bytes_step_total = bytes_rank_layer * layers * world
+    value = bytes_step_total / (ms_per_step * 1e-3) / 1e9
+
+    # --- append kernel alone (append GB/s): K1 across the 32 pools
+    ap_s, ap_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ap_s.record()
+    reps = 5
+    for _ in range(reps):
+        for l in range(layers):
+            ops.kv_append(k_pools[l], v_pools[l], meta.slot_mapping, k_l, v_l)
+    ap_e.record()
+    barrier()
+    append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
+    append_bytes = 2 * 2 * args.batch * hkv_l * DH * 2  # K and V rows read + written, bf16
+
+    # --- end to end through the public API with host buffers (metadata build + H2D in, D2H out)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx)
+
+    peak, peak_kind = measured_peak()
+    achieved = bytes_rank_layer / (attn_avg_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        cpu = run_cpu_baseline(ctx, blocks, args.cpu_sample_seqs, reps=args.cpu_reps)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 2: Llama-3.1-8B decode attention (H32/Hkv8/Dh128, bs16), batch 64, "
+                                   "ctx U[512,4096], 32 layer pools, append 1 token/seq + paged attention",
+                       "layers": layers, "batch": args.batch, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
+                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "l2": "no flush: every layer reads 604 MB of KV, > 126 MB L2",
+                       "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
+                       "partial_rows": plan.num_partial_rows},
+            "seqs_per_s": round(args.batch / (ms_per_step * 1e-3 / layers), 1),
+            "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 2),
+            "append_us": round(append_ms * 1e3, 2),
+            "attention_us": round(attn_avg_ms * 1e3, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "traffic": profiled_traffic(), "algorithmic_bytes": bytes_rank_layer,
+                         "kernel": "paged_attn_mma_kernel<bf16,128,3>"},
+            "gpu_launches": launches_per_layer * layers * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx) -> dict:
+    """Each step: AttentionMetadata.build (host -> device), then per layer the q/k/v rows copied from pinned
+    host memory, the public backend's forward, and the output copied back to pinned host memory."""
+    layers = len(k_pools)
+    qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    backend = sharding.KVHeadShardedBackend() if world > 1 else mlb.B200Backend()
+
+    def step():
+        meta = mlb.AttentionMetadata.build(seqs, BS, dev)
+        for l in range(layers):
+            qd.copy_(qh, non_blocking=True)
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
+            out = backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)
+            outs[l].copy_(out, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e), world, dev) / args.steps
+    total = kv_bytes(ctx, HKV) * layers
+    meta_bytes = _meta_bytes(mlb, seqs)
+    h2d = layers * (q.numel() + k.numel() + v.numel()) * q.element_size() + meta_bytes
+    d2h = layers * q.numel() * q.element_size()
+    return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "path": ("KVHeadShardedBackend" if world > 1 else "B200Backend") + ".forward per layer, pinned host I/O"}
+
+
+def _meta_bytes(mlb, seqs) -> int:
+    m = mlb.AttentionMetadata.build(seqs, BS, "cpu")
+    return sum(t.numel() * t.element_size() for t in (m.positions, m.slot_mapping, m.block_tables, m.logits_index,
+                                                      m.qo_indptr, m.seq_lens_i32, m.block_tables_i32, m.kv_indptr,
+                                                      m.kv_indices, m.kv_last_page_len))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--cpu-sample-seqs", type=int, default=16)
+    ap.add_argument("--cpu-reps", type=int, default=10)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours" and args.layers == 32:
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

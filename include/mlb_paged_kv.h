@@ -1,0 +1,148 @@
+/*
+ * mlb_paged_kv.h — C ABI of the B200 (sm_100a) paged KV-cache hot path.
+ *
+ * Drop-in boundary for the paged path of prakhar-iit/mini-llm-inference-server.  Every entry point
+ * below replaces one piece of the reference's Python/torch hot path (cited as file:line inside that
+ * project).  Conventions shared by all of them:
+ *   - pointers are raw device pointers (or host pointers where stated), sizes are element counts and
+ *     strides are in ELEMENTS of the tensor they describe; the innermost (head_dim) stride is 1;
+ *   - `stream` is a cudaStream_t passed as void* (0 = the legacy default stream);
+ *   - the return value is MLB_OK (0) or an MLB_E* code; mlb_last_error() describes the last failure of
+ *     the calling thread.  No C++ exception crosses this boundary;
+ *   - the library allocates no device memory: pools, metadata, outputs and split-K workspace all
+ *     belong to the caller (torch in the Python package);
+ *   - `err_word` (optional, may be NULL) is a device int32 into which kernels OR an MLB_DEV_* bit when
+ *     they meet an out-of-range slot / block id or a wait that never completes; the offending access
+ *     is skipped instead of faulting.
+ */
+#ifndef MLB_PAGED_KV_H
+#define MLB_PAGED_KV_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MLB_API __attribute__((visibility("default")))
+#else
+#define MLB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of rows and pools */
+enum { MLB_F32 = 0, MLB_F16 = 1, MLB_BF16 = 2 };
+
+/* status codes */
+enum { MLB_OK = 0, MLB_EINVAL = 1, MLB_EUNSUPPORTED = 2, MLB_ECUDA = 3, MLB_ENOSPACE = 4 };
+
+/* bits a kernel ORs into *err_word */
+enum {
+  MLB_DEV_SLOT_RANGE = 1,   /* slot_mapping entry outside [0, num_blocks * block_size): row not written */
+  MLB_DEV_BLOCK_RANGE = 2,  /* block_tables entry outside [0, num_blocks): page treated as empty        */
+  MLB_DEV_WAIT_TIMEOUT = 4, /* a bounded wait on a page copy gave up: output of that unit is invalid    */
+  MLB_DEV_COPY_RANGE = 8    /* block-copy pair outside [0, num_blocks): pair skipped                    */
+};
+
+/* Description of the last failing call on this thread ("" if none). */
+MLB_API const char* mlb_last_error(void);
+
+/* ABI version (bumped on any signature change). */
+MLB_API int mlb_abi_version(void);
+
+/*
+ * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three
+ * reference backends (torch_ref.py:47, flashinfer_backend.py:43, flash_attn_backend.py:44):
+ *     k_cache.view(-1, Hkv, Dh)[slot_mapping[i]] = k[i].to(k_cache.dtype)   (and the same for v)
+ * k, v: [num_tokens, num_kv_heads, head_dim] of in_dtype with strides (tok, head) in elements;
+ * pools: [num_blocks, block_size, num_kv_heads, head_dim] of cache_dtype, contiguous;
+ * slot_mapping: device int64 [num_tokens] (metadata.py:94).  Casts round to nearest even; bf16 NaN is
+ * stored as 0xFFFF and fp16 NaN as sign|0x7E00 (the reference's CPU cast).  Slots must be distinct.
+ */
+MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
+                  const int64_t* slot_mapping, const void* k, int64_t k_stride_tok, int64_t k_stride_head,
+                  const void* v, int64_t v_stride_tok, int64_t v_stride_head, int in_dtype,
+                  int64_t num_tokens, int num_kv_heads, int head_dim, int32_t* err_word, void* stream);
+
+/*
+ * One unit of paged-attention work: query tile `q_tile` of sequence `seq` over the pages
+ * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads).
+ * part_row < 0: the unit covers the whole context and writes `out` itself; otherwise it writes
+ * normalised fp32 partial rows part_row + t (t = token within the tile) for the split-K reduction.
+ */
+typedef struct {
+  int32_t seq;
+  int32_t q_tile;
+  int32_t page_begin;
+  int32_t page_end;
+  int32_t part_row;
+  int32_t reserved[3];
+} mlb_work_unit;
+
+/*
+ * Host-side planner (host pointers).  Plays the role of FlashInfer's per-step plan() that the reference
+ * runs once per AttentionMetadata and reuses across layers (flashinfer_backend.py:44-45, :48-64).
+ * Inputs: qo_indptr [num_seqs + 1] and seq_lens [num_seqs] exactly as AttentionMetadata holds them
+ * (metadata.py:39-40, :97-98); max_blocks_per_seq = block_tables width (validates seq_lens).
+ * pages_per_unit = 0 picks a split size from the total work and num_sms.
+ * Outputs: units[*num_units] (capacity units_capacity; MLB_ENOSPACE with the needed count in
+ * *num_units if too small), per token reduce_rows / reduce_chunks [num_tokens] (chunks <= 1: no
+ * reduction for that token) and the number of fp32 partial rows the workspace must hold.
+ * Query tokens per tile = max(1, 8 / (num_heads / num_kv_heads)).
+ */
+MLB_API int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int max_blocks_per_seq,
+                       int num_heads, int num_kv_heads, int block_size, int num_sms, int pages_per_unit,
+                       mlb_work_unit* units, int64_t units_capacity, int64_t* num_units,
+                       int32_t* reduce_rows, int32_t* reduce_chunks, int64_t num_tokens,
+                       int64_t* num_partial_rows);
+
+/* Upper bound on the units mlb_plan_attention can emit for these sequences (host pointers). */
+MLB_API int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int num_heads,
+                          int num_kv_heads, int block_size);
+
+/*
+ * Paged attention over block tables (decode rows and multi-token rows with the causal mask aligned to
+ * the end of each context).  Replaces paged_attention (src/minillm/attention/paged_torch_ref.py:40-74)
+ * and the FlashInfer decode/prefill wrappers' run() (flashinfer_backend.py:46).
+ * q: [N, num_heads, head_dim] (strides in elements); pools as above, dtype == q's; block_tables:
+ * device int32 [num_seqs, bt_stride] (metadata.py:48); seq_lens: device int32 [num_seqs];
+ * qo_indptr: device int32 [num_seqs + 1]; units: device copy of the plan.  Scale is usually
+ * 1/sqrt(head_dim).  partial_o [num_partial_rows, num_heads, head_dim] and partial_lse
+ * [num_partial_rows, num_heads] (fp32, caller-owned) may be NULL when the plan has no partial rows.
+ * out: [N, num_heads, head_dim] of q's dtype.  Supported: head_dim 64/128/256, block_size 16,
+ * num_heads / num_kv_heads <= 8; f16/bf16 pools use tensor-core tiles, f32 pools CUDA cores.
+ */
+MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache, int dtype, int64_t num_blocks, int block_size,
+                        int num_heads, int num_kv_heads, int head_dim, float scale,
+                        const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
+                        const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
+                        float* partial_o, float* partial_lse, int64_t num_partial_rows,
+                        void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        int32_t* err_word, void* stream);
+
+/*
+ * Split-K reduction: for every token whose reduce_chunks > 1, combine its rows
+ * reduce_rows[t] + c * tokens_per_tile (c < reduce_chunks[t]) by their log-sum-exp weights and write
+ * out[t].  Completes mlb_paged_attention; no reference counterpart (the reference never splits).
+ */
+MLB_API int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                      const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,
+                      int64_t num_tokens, int num_heads, int head_dim,
+                      void* out, int64_t out_stride_tok, int64_t out_stride_head, int out_dtype, void* stream);
+
+/*
+ * Block copy for prefix-cache copy-on-write and compaction: pool[dst[i]] = pool[src[i]] for every pool
+ * in `pools` (a DEVICE array of num_pools base pointers: every layer's K and V).  block_bytes = one
+ * block of one pool (block_size * Hkv * Dh * elt).  The destination set must be disjoint from the
+ * source set.  No reference counterpart: the reference has no COW or compaction; its compaction by
+ * copy is SlotKVCache.move (src/minillm/cache/slot.py:41-46), which this generalises to blocks.
+ */
+MLB_API int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
+                   const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err_word, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLB_PAGED_KV_H */

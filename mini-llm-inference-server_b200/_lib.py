@@ -1,0 +1,86 @@
+"""ctypes binding of the C ABI in `include/mlb_paged_kv.h` (the in-tree `_mlb_paged_kv.so`).
+
+The library is required: there is no fallback.  If it is missing, `lib()` raises with the command that
+builds it.  Argument and result types are declared once so ctypes converts Python ints exactly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).with_name("_mlb_paged_kv.so")
+
+# dtype codes and status codes (mlb_paged_kv.h)
+MLB_F32, MLB_F16, MLB_BF16 = 0, 1, 2
+MLB_OK, MLB_EINVAL, MLB_EUNSUPPORTED, MLB_ECUDA, MLB_ENOSPACE = 0, 1, 2, 3, 4
+# bits kernels OR into the device error word
+DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
+
+EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_plan_capacity",
+           "mlb_paged_attention", "mlb_splitk_reduce", "mlb_block_copy")
+
+
+class WorkUnit(ctypes.Structure):
+    """mlb_work_unit: one (sequence, query tile, page range) of paged-attention work."""
+
+    _fields_ = [("seq", c_int32), ("q_tile", c_int32), ("page_begin", c_int32), ("page_end", c_int32),
+                ("part_row", c_int32), ("reserved", c_int32 * 3)]
+
+
+WORK_UNIT_INT32S = ctypes.sizeof(WorkUnit) // 4
+
+_I32P, _I64P = POINTER(c_int32), POINTER(c_int64)
+_SIGNATURES = {
+    "mlb_last_error": (c_char_p, []),
+    "mlb_abi_version": (c_int, []),
+    "mlb_kv_append": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64,
+                              c_void_p, c_int64, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p]),
+    "mlb_plan_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                   c_int64, _I64P, c_void_p, c_void_p, c_int64, _I64P]),
+    "mlb_plan_capacity": (c_int64, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]),
+    "mlb_paged_attention": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
+                                    c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
+                                    c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+                                    c_void_p]),
+    "mlb_splitk_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
+                                  c_void_p, c_int64, c_int64, c_int, c_void_p]),
+    "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+                               c_void_p]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+class MlbError(RuntimeError):
+    """A CUDA-side failure reported by the library (MLB_ECUDA / MLB_ENOSPACE)."""
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH.name} is not built: run `python {LIB_PATH.parent.name}/build.py` "
+                              "(nvcc, sm_100a); the paged-KV ops have no fallback")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def last_error() -> str:
+    return lib().mlb_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    """Turn a status code into the exception the reference raises for the same fault."""
+    if rc == MLB_OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc in (MLB_EINVAL, MLB_EUNSUPPORTED):
+        raise ValueError(msg)
+    raise MlbError(msg)

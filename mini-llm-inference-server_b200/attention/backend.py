@@ -1,0 +1,100 @@
+"""`B200Backend`: the reference's `AttentionBackend` (attention/base.py:16-45) on sm_100a kernels.
+
+`forward` per layer (the engine calls it 32 times per step for Llama-3.1-8B):
+1. K1 `kv_append`: this step's k/v rows into the pools through `meta.slot_mapping` (replaces write_kv,
+   paged_torch_ref.py:23-28, which all three reference backends share);
+2. the step's split plan, built on the first layer that sees a new `meta` and reused by the rest, as the
+   FlashInfer backend caches its plan() (flashinfer_backend.py:44-45);
+3. K2a paged attention over `meta.block_tables_i32` + K2b split-K reduction (replaces paged_attention,
+   paged_torch_ref.py:40-74, and FlashInfer's run(), flashinfer_backend.py:46).
+No host synchronisation happens inside `forward`; every launch goes on torch's current stream.
+
+`prefill` (the contiguous, non-paged path of generate.py and the correctness tests) is not part of the
+paged hot path; like the reference's CUDA backends (flashinfer_backend.py:39-40) it is plain SDPA.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from .. import _lib
+from ..ops import AttentionPlan, Workspace, kv_append, paged_attention, plan_attention
+from .base import AttentionBackend
+
+
+class DeviceFault(RuntimeError):
+    """A kernel met an out-of-range slot / block id (skipped) or gave up a bounded wait."""
+
+
+class B200Backend(AttentionBackend):
+    name = "b200"
+
+    def __init__(self, pages_per_unit: int = 0, num_sms: int | None = None, check_errors: bool = False) -> None:
+        """pages_per_unit: split-K size in pages (0 = chosen per step from the work and the SM count).
+        check_errors: after every forward, synchronise and raise `DeviceFault` if a kernel flagged a range
+        fault (debugging aid; it costs a host sync per layer)."""
+        _lib.lib()  # the CUDA library is required: fail here, not on the first step
+        self.pages_per_unit = pages_per_unit
+        self.num_sms = num_sms
+        self.check_errors = check_errors
+        self._planned = None  # the AttentionMetadata the plan was built for
+        self._plan_key: tuple | None = None
+        self._plan: AttentionPlan | None = None
+        self._workspace = Workspace()
+        self._err: torch.Tensor | None = None
+
+    # ------------------------------------------------------------------ contiguous path
+    def prefill(self, q, k, v, key_valid=None, **kwargs):
+        tq, tk = q.shape[2], k.shape[2]
+        if key_valid is None and tq in (1, tk):  # decode step sees every key; a fresh prompt is plain causal
+            return F.scaled_dot_product_attention(q, k, v, is_causal=tq > 1, enable_gqa=True)
+        # query i (position tk - tq + i) sees keys 0 .. tk - tq + i
+        mask = torch.ones(tq, tk, dtype=torch.bool, device=q.device).tril(diagonal=tk - tq)
+        if key_valid is not None:
+            mask = mask & key_valid[:, None, None, :]
+            # a query with no real key may see its own position (softmax over nothing would be NaN)
+            own = torch.zeros(tq, tk, dtype=torch.bool, device=q.device)
+            own[torch.arange(tq), torch.arange(tq) + tk - tq] = True
+            mask = mask | (own & ~mask.any(dim=-1, keepdim=True))
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True)
+
+    # ------------------------------------------------------------------ paged path
+    def plan(self, meta, num_heads: int, num_kv_heads: int, device: torch.device) -> AttentionPlan:
+        key = (num_heads, num_kv_heads, device)
+        if self._planned is not meta or self._plan_key != key:
+            self._plan = plan_attention(meta.query_start_loc, meta.seq_lens, meta.block_tables_i32.shape[1],
+                                        num_heads, num_kv_heads, device, meta.block_size, self.num_sms,
+                                        self.pages_per_unit)
+            self._planned, self._plan_key = meta, key
+        return self._plan
+
+    def forward(self, q, k, v, k_cache, v_cache, meta):
+        if k_cache.shape[1] != meta.block_size:
+            raise ValueError(f"pool block size {k_cache.shape[1]} != metadata block size {meta.block_size}")
+        err = self._error_word(q.device) if self.check_errors else None
+        kv_append(k_cache, v_cache, meta.slot_mapping, k, v, err)
+        plan = self.plan(meta, q.shape[1], k_cache.shape[2], q.device)
+        out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
+                              self._workspace, err=err)
+        if self.check_errors:
+            self.raise_device_errors()
+        return out
+
+    # ------------------------------------------------------------------ device error word
+    def _error_word(self, device: torch.device) -> torch.Tensor:
+        if self._err is None or self._err.device != device:
+            self._err = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._err
+
+    def raise_device_errors(self) -> None:
+        if self._err is None:
+            return
+        bits = int(self._err.item())
+        if bits:
+            self._err.zero_()
+            names = [n for b, n in ((_lib.DEV_SLOT_RANGE, "slot out of range"),
+                                    (_lib.DEV_BLOCK_RANGE, "block id out of range"),
+                                    (_lib.DEV_WAIT_TIMEOUT, "page copy wait timed out"),
+                                    (_lib.DEV_COPY_RANGE, "block-copy pair out of range")) if bits & b]
+            raise DeviceFault("device fault flags: " + ", ".join(names))

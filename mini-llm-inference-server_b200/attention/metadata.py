@@ -1,0 +1,119 @@
+"""Per-step attention metadata for paged KV, the reference's `AttentionMetadata` (metadata.py:27-103) with
+the same fields, built without a per-token Python loop.
+
+The reference's `build` walks every new token in Python (metadata.py:72-81) and makes eleven separate
+host-to-device tensors.  Here the step is described with numpy array arithmetic and all device tensors
+are views into two buffers (int64 and int32) that cross to the device in two copies from pinned
+memory, once per step; every layer reuses them.
+
+Example (block size 16): sequence 0 has 3 tokens cached and adds 1; sequence 1 is a fresh 5-token prompt.
+    query_start_loc = [0, 1, 6]; seq_lens = [4, 5]; positions = [3, 0, 1, 2, 3, 4]
+    slot_mapping    = [b0*16 + 3, b1*16 + 0, ..., b1*16 + 4]
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+
+@dataclass
+class SeqStep:
+    """One sequence in a step: `num_cached` tokens already in the pool, `num_new` added now (metadata.py:27-33)."""
+
+    num_cached: int
+    num_new: int
+    block_ids: list[int]  # covers num_cached + num_new tokens
+
+
+@dataclass
+class AttentionMetadata:
+    block_size: int
+    query_start_loc: list[int]  # host, len S + 1
+    seq_lens: list[int]  # host: context length per sequence, this step's tokens included
+    positions: torch.Tensor  # [N] int64
+    slot_mapping: torch.Tensor  # [N] int64 flat pool slot of each new token
+    block_tables: torch.Tensor  # [S, max_blocks] int64, padded with block 0
+    logits_index: torch.Tensor  # [S] int64 index of each sequence's last new token
+    qo_indptr: torch.Tensor  # [S + 1] int32
+    seq_lens_i32: torch.Tensor  # [S] int32
+    block_tables_i32: torch.Tensor  # [S, max_blocks] int32
+    kv_indptr: torch.Tensor  # [S + 1] int32 offsets into kv_indices
+    kv_indices: torch.Tensor  # int32: the pages each sequence uses, concatenated
+    kv_last_page_len: torch.Tensor  # [S] int32
+
+    @property
+    def max_query_len(self) -> int:
+        return max(self.num_new)
+
+    @property
+    def max_seq_len(self) -> int:
+        return max(self.seq_lens)
+
+    @property
+    def num_seqs(self) -> int:
+        return len(self.seq_lens)
+
+    @property
+    def num_new(self) -> list[int]:
+        q = self.query_start_loc
+        return [q[i + 1] - q[i] for i in range(len(q) - 1)]
+
+    @classmethod
+    def build(cls, seqs: list[SeqStep], block_size: int, device: torch.device | str) -> AttentionMetadata:
+        device = torch.device(device)
+        s = len(seqs)
+        cached = np.fromiter((q.num_cached for q in seqs), dtype=np.int64, count=s)
+        new = np.fromiter((q.num_new for q in seqs), dtype=np.int64, count=s)
+        nblk = np.fromiter((len(q.block_ids) for q in seqs), dtype=np.int64, count=s)
+        ends = cached + new
+        short = np.nonzero(nblk * block_size < ends)[0]
+        if short.size:
+            i = int(short[0])
+            raise ValueError(f"{int(nblk[i])} blocks can't hold {int(ends[i])} tokens")
+        width = int(nblk.max()) if s else 0
+        table = np.zeros((s, width), dtype=np.int64)
+        for i, q in enumerate(seqs):
+            table[i, :len(q.block_ids)] = q.block_ids
+        starts = np.zeros(s + 1, dtype=np.int64)
+        np.cumsum(new, out=starts[1:])
+        n = int(starts[-1])
+        owner = np.repeat(np.arange(s), new)  # sequence of each new token
+        positions = np.arange(n, dtype=np.int64) - starts[owner] + cached[owner]
+        slots = table[owner, positions // block_size] * block_size + positions % block_size
+        used = -(-ends // block_size)  # pages holding context
+        kv_indptr = np.zeros(s + 1, dtype=np.int64)
+        np.cumsum(used, out=kv_indptr[1:])
+        kv_indices = table[np.arange(width)[None, :] < used[:, None]]  # row-major: sequence by sequence
+        last_len = ends - (used - 1) * block_size
+
+        # two transfers: every int64 tensor in one buffer, every int32 tensor in another
+        i64 = np.concatenate([positions, slots, table.reshape(-1), starts[1:] - 1])
+        i32 = np.concatenate([starts, ends, table.reshape(-1), kv_indptr, kv_indices, last_len]).astype(np.int32)
+        d64, d32 = _to_device(i64, device), _to_device(i32, device)
+        o64 = np.cumsum([0, n, n, s * width, s])
+        o32 = np.cumsum([0, s + 1, s, s * width, s + 1, kv_indices.size, s])
+        return cls(
+            block_size=block_size,
+            query_start_loc=starts.tolist(),
+            seq_lens=ends.tolist(),
+            positions=d64[o64[0]:o64[1]],
+            slot_mapping=d64[o64[1]:o64[2]],
+            block_tables=d64[o64[2]:o64[3]].view(s, width),
+            logits_index=d64[o64[3]:o64[4]],
+            qo_indptr=d32[o32[0]:o32[1]],
+            seq_lens_i32=d32[o32[1]:o32[2]],
+            block_tables_i32=d32[o32[2]:o32[3]].view(s, width),
+            kv_indptr=d32[o32[3]:o32[4]],
+            kv_indices=d32[o32[4]:o32[5]],
+            kv_last_page_len=d32[o32[5]:o32[6]],
+        )
+
+
+def _to_device(a: np.ndarray, device: torch.device) -> torch.Tensor:
+    host = torch.from_numpy(np.ascontiguousarray(a))
+    if device.type == "cuda":
+        return host.pin_memory().to(device, non_blocking=True)
+    return host.clone() if device.type == "cpu" else host.to(device)

@@ -1,0 +1,286 @@
+// The extern "C" boundary (include/mlb_paged_kv.h): argument validation, the host-side split planner,
+// dispatch to the kernels, and error reporting by status code + mlb_last_error().  No exception and no
+// device allocation crosses or happens behind this boundary.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+#include <vector>
+
+#include "attn_args.cuh"
+
+namespace mlb {
+cudaError_t launch_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_slots, const int64_t* slots,
+                             const void* k, int64_t k_st, int64_t k_sh, const void* v, int64_t v_st, int64_t v_sh,
+                             int in_dtype, int64_t num_tokens, int hkv, int dh, bool vec, int32_t* err,
+                             cudaStream_t s);
+cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
+cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
+                                 int tpt, int64_t ntok, int h, int dh, char* out, int64_t o_st, int64_t o_sh,
+                                 int out_dtype, cudaStream_t s);
+cudaError_t launch_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
+                              const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err, int num_sms,
+                              cudaStream_t s);
+}  // namespace mlb
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MLB_OK;
+  return fail(MLB_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int elt_bytes(int dtype) { return dtype == MLB_F32 ? 4 : (dtype == MLB_F16 || dtype == MLB_BF16) ? 2 : 0; }
+bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
+constexpr int kCtasPerSm = 2;        // resident paged-attention CTAs per SM (shared memory bound)
+constexpr int kWaves = 4;            // CTA waves the auto split aims for (tail balance vs partial rows)
+constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
+
+int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+struct Group {
+  int seq, tile, pages;
+};
+
+// Enumerate (sequence, query tile) groups and the pages each must read; validates the step.
+int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_blocks, int h, int hkv, int bs,
+                std::vector<Group>& groups, int64_t* total_pages) {
+  const int tpt = tokens_per_tile(h, hkv);
+  *total_pages = 0;
+  groups.clear();
+  for (int s = 0; s < num_seqs; ++s) {
+    const int n = qo[s + 1] - qo[s], L = lens[s];
+    if (n < 0) return fail(MLB_EINVAL, "qo_indptr must be non-decreasing (sequence %d)", s);
+    if (L < n) return fail(MLB_EINVAL, "sequence %d: seq_len %d < %d new tokens", s, L, n);
+    if (max_blocks >= 0 && static_cast<int64_t>(L) > static_cast<int64_t>(max_blocks) * bs)
+      return fail(MLB_EINVAL, "sequence %d: %d blocks can't hold %d tokens", s, max_blocks, L);
+    for (int t = 0; t * tpt < n; ++t) {
+      const int last = std::min((t + 1) * tpt, n) - 1;
+      const int extent = L - n + last + 1;
+      const int pages = (extent + bs - 1) / bs;
+      groups.push_back({s, t, pages});
+      *total_pages += pages;
+    }
+  }
+  return MLB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mlb_last_error(void) { return g_last_error.c_str(); }
+
+int mlb_abi_version(void) { return 1; }
+
+int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
+                  const int64_t* slot_mapping, const void* k, int64_t k_stride_tok, int64_t k_stride_head,
+                  const void* v, int64_t v_stride_tok, int64_t v_stride_head, int in_dtype, int64_t num_tokens,
+                  int num_kv_heads, int head_dim, int32_t* err_word, void* stream) {
+  const int ob = elt_bytes(cache_dtype), ib = elt_bytes(in_dtype);
+  if (!ob || !ib) return fail(MLB_EINVAL, "kv_append: unknown dtype (cache %d, rows %d)", cache_dtype, in_dtype);
+  if (num_tokens < 0 || num_kv_heads <= 0 || head_dim <= 0 || num_blocks <= 0 || block_size <= 0)
+    return fail(MLB_EINVAL, "kv_append: bad sizes");
+  if ((head_dim * ob) % 16 != 0)
+    return fail(MLB_EUNSUPPORTED, "kv_append: head_dim * element size must be a multiple of 16 bytes");
+  if (num_tokens == 0) return MLB_OK;
+  if (!k_cache || !v_cache || !slot_mapping || !k || !v) return fail(MLB_EINVAL, "kv_append: null pointer");
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16))
+    return fail(MLB_EINVAL, "kv_append: pools must be 16-byte aligned");
+  // Wide loads need every vector of every input row aligned to the load width.
+  const int in_vec = ob == ib ? 16 : 8;
+  const int64_t per_vec_bytes = static_cast<int64_t>(16 / ob) * ib;
+  const bool vec = aligned(k, in_vec) && aligned(v, in_vec) && per_vec_bytes % in_vec == 0 &&
+                   (k_stride_tok * ib) % in_vec == 0 && (k_stride_head * ib) % in_vec == 0 &&
+                   (v_stride_tok * ib) % in_vec == 0 && (v_stride_head * ib) % in_vec == 0;
+  return cuda_status(mlb::launch_kv_append(k_cache, v_cache, cache_dtype, num_blocks * block_size, slot_mapping, k,
+                                           k_stride_tok, k_stride_head, v, v_stride_tok, v_stride_head, in_dtype,
+                                           num_tokens, num_kv_heads, head_dim, vec, err_word,
+                                           static_cast<cudaStream_t>(stream)),
+                     "kv_append launch");
+}
+
+int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int num_heads,
+                          int num_kv_heads, int block_size) {
+  if (num_kv_heads <= 0 || num_heads % num_kv_heads || block_size <= 0) return -1;
+  std::vector<Group> groups;
+  int64_t total = 0;
+  if (plan_groups(qo_indptr, seq_lens, num_seqs, -1, num_heads, num_kv_heads, block_size, groups, &total) != MLB_OK)
+    return -1;
+  int64_t cap = 0;
+  for (const Group& g : groups) cap += (g.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit;
+  return cap;
+}
+
+int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int max_blocks_per_seq,
+                       int num_heads, int num_kv_heads, int block_size, int num_sms, int pages_per_unit,
+                       mlb_work_unit* units, int64_t units_capacity, int64_t* num_units, int32_t* reduce_rows,
+                       int32_t* reduce_chunks, int64_t num_tokens, int64_t* num_partial_rows) {
+  if (!qo_indptr || !seq_lens || !num_units || !num_partial_rows || num_seqs < 0)
+    return fail(MLB_EINVAL, "plan: null pointer or negative sequence count");
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
+    return fail(MLB_EINVAL, "plan: num_heads (%d) must be a positive multiple of num_kv_heads (%d)", num_heads,
+                num_kv_heads);
+  if (block_size <= 0 || num_sms <= 0) return fail(MLB_EINVAL, "plan: bad block_size or num_sms");
+  if (num_seqs > 0 && qo_indptr[num_seqs] > num_tokens)
+    return fail(MLB_EINVAL, "plan: qo_indptr ends at %d > num_tokens %lld", qo_indptr[num_seqs],
+                static_cast<long long>(num_tokens));
+  std::vector<Group> groups;
+  int64_t total = 0;
+  int rc = plan_groups(qo_indptr, seq_lens, num_seqs, max_blocks_per_seq, num_heads, num_kv_heads, block_size, groups,
+                       &total);
+  if (rc != MLB_OK) return rc;
+  const int tpt = tokens_per_tile(num_heads, num_kv_heads);
+  int64_t chunk = pages_per_unit;
+  if (chunk <= 0) {
+    const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaves;
+    chunk = std::max<int64_t>(kMinPagesPerUnit, (total * num_kv_heads + target_ctas - 1) / target_ctas);
+  }
+  std::vector<mlb_work_unit> out;
+  out.reserve(groups.size());
+  if (reduce_rows && reduce_chunks)
+    for (int64_t t = 0; t < num_tokens; ++t) reduce_rows[t] = -1, reduce_chunks[t] = 0;
+  int64_t rows = 0;
+  for (const Group& g : groups) {
+    const int64_t nch = std::max<int64_t>(1, (g.pages + chunk - 1) / chunk);
+    const int64_t per = (g.pages + nch - 1) / nch;
+    const int64_t base = nch > 1 ? rows : -1;
+    if (nch > 1) rows += nch * tpt;
+    for (int64_t c = 0; c < nch; ++c) {
+      mlb_work_unit u{};
+      u.seq = g.seq;
+      u.q_tile = g.tile;
+      u.page_begin = static_cast<int32_t>(c * per);
+      u.page_end = static_cast<int32_t>(std::min<int64_t>((c + 1) * per, g.pages));
+      u.part_row = nch > 1 ? static_cast<int32_t>(base + c * tpt) : -1;
+      if (u.page_end > u.page_begin || g.pages == 0) out.push_back(u);
+    }
+    if (reduce_rows && reduce_chunks) {
+      const int n = qo_indptr[g.seq + 1] - qo_indptr[g.seq];
+      for (int i = 0; i < tpt && g.tile * tpt + i < n; ++i) {
+        const int64_t tok = qo_indptr[g.seq] + static_cast<int64_t>(g.tile) * tpt + i;
+        reduce_rows[tok] = nch > 1 ? static_cast<int32_t>(base + i) : -1;
+        reduce_chunks[tok] = static_cast<int32_t>(nch);
+      }
+    }
+  }
+  if (rows > INT32_MAX) return fail(MLB_EINVAL, "plan: too many partial rows");
+  // Largest units first, so the short tail units fill in behind them.
+  std::stable_sort(out.begin(), out.end(), [](const mlb_work_unit& x, const mlb_work_unit& y) {
+    return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);
+  });
+  *num_units = static_cast<int64_t>(out.size());
+  *num_partial_rows = rows;
+  if (!units) return MLB_OK;  // count only
+  if (static_cast<int64_t>(out.size()) > units_capacity)
+    return fail(MLB_ENOSPACE, "plan: %zu units > capacity %lld", out.size(), static_cast<long long>(units_capacity));
+  std::copy(out.begin(), out.end(), units);
+  return MLB_OK;
+}
+
+int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k_cache,
+                        const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
+                        int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
+                        const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
+                        int64_t num_units, float* partial_o, float* partial_lse, int64_t num_partial_rows, void* out,
+                        int64_t out_stride_tok, int64_t out_stride_head, int32_t* err_word, void* stream) {
+  if (!elt_bytes(dtype)) return fail(MLB_EINVAL, "paged_attention: unknown dtype %d", dtype);
+  if (block_size != mlb::kBlockSize)
+    return fail(MLB_EUNSUPPORTED, "paged_attention: block_size %d (kernels are built for 16)", block_size);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(MLB_EUNSUPPORTED, "paged_attention: head_dim %d (supported: 64, 128, 256)", head_dim);
+  if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
+    return fail(MLB_EINVAL, "paged_attention: num_heads %d not a multiple of num_kv_heads %d", num_heads,
+                num_kv_heads);
+  if (num_heads / num_kv_heads > 8)
+    return fail(MLB_EUNSUPPORTED, "paged_attention: %d query heads per KV head (at most 8)",
+                num_heads / num_kv_heads);
+  if (num_units < 0 || num_seqs < 0 || num_blocks <= 0) return fail(MLB_EINVAL, "paged_attention: bad sizes");
+  if (num_units == 0) return MLB_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !seq_lens || !qo_indptr || !units || !out)
+    return fail(MLB_EINVAL, "paged_attention: null pointer");
+  if (num_partial_rows > 0 && (!partial_o || !partial_lse))
+    return fail(MLB_EINVAL, "paged_attention: the plan has %lld partial rows but no workspace",
+                static_cast<long long>(num_partial_rows));
+  if (!aligned(k_cache, 16) || !aligned(v_cache, 16))
+    return fail(MLB_EINVAL, "paged_attention: pools must be 16-byte aligned");
+  if (num_units * num_kv_heads > INT32_MAX) return fail(MLB_EINVAL, "paged_attention: grid too large");
+  mlb::AttnArgs a{};
+  a.q = static_cast<const char*>(q);
+  a.q_st = q_stride_tok;
+  a.q_sh = q_stride_head;
+  a.k_cache = static_cast<const char*>(k_cache);
+  a.v_cache = static_cast<const char*>(v_cache);
+  a.num_blocks = num_blocks;
+  a.h = num_heads;
+  a.hkv = num_kv_heads;
+  a.group = num_heads / num_kv_heads;
+  a.tile_tokens = tokens_per_tile(num_heads, num_kv_heads);
+  a.sl2 = scale * mlb::kLog2e;
+  a.bt = block_tables;
+  a.bt_stride = bt_stride;
+  a.seq_lens = seq_lens;
+  a.qo = qo_indptr;
+  a.units = units;
+  a.part_o = partial_o;
+  a.part_lse = partial_lse;
+  a.out = static_cast<char*>(out);
+  a.o_st = out_stride_tok;
+  a.o_sh = out_stride_head;
+  a.err = err_word;
+  a.wait_ns = kWaitNs;
+  return cuda_status(mlb::launch_paged_attention(a, dtype, head_dim, num_units, static_cast<cudaStream_t>(stream)),
+                     "paged_attention launch");
+}
+
+int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                      const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile_,
+                      int64_t num_tokens, int num_heads, int head_dim, void* out, int64_t out_stride_tok,
+                      int64_t out_stride_head, int out_dtype, void* stream) {
+  if (!elt_bytes(out_dtype)) return fail(MLB_EINVAL, "splitk_reduce: unknown dtype %d", out_dtype);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(MLB_EUNSUPPORTED, "splitk_reduce: head_dim %d", head_dim);
+  if (num_tokens < 0 || num_heads <= 0 || tokens_per_tile_ <= 0) return fail(MLB_EINVAL, "splitk_reduce: bad sizes");
+  if (num_tokens == 0 || num_partial_rows == 0) return MLB_OK;
+  if (!partial_o || !partial_lse || !reduce_rows || !reduce_chunks || !out)
+    return fail(MLB_EINVAL, "splitk_reduce: null pointer");
+  return cuda_status(mlb::launch_splitk_reduce(partial_o, partial_lse, reduce_rows, reduce_chunks, tokens_per_tile_,
+                                               num_tokens, num_heads, head_dim, static_cast<char*>(out),
+                                               out_stride_tok, out_stride_head, out_dtype,
+                                               static_cast<cudaStream_t>(stream)),
+                     "splitk_reduce launch");
+}
+
+int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes, const int32_t* src,
+                   const int32_t* dst, int64_t num_pairs, int32_t* err_word, void* stream) {
+  if (num_pools < 0 || num_pairs < 0 || num_blocks <= 0 || block_bytes <= 0)
+    return fail(MLB_EINVAL, "block_copy: bad sizes");
+  if (block_bytes % 16) return fail(MLB_EUNSUPPORTED, "block_copy: block_bytes must be a multiple of 16");
+  if (num_pools == 0 || num_pairs == 0) return MLB_OK;
+  if (!pools || !src || !dst) return fail(MLB_EINVAL, "block_copy: null pointer");
+  return cuda_status(mlb::launch_block_copy(pools, num_pools, num_blocks, block_bytes, src, dst, num_pairs, err_word,
+                                            sm_count(), static_cast<cudaStream_t>(stream)),
+                     "block_copy launch");
+}
+
+}  // extern "C"

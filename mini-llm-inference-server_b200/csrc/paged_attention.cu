@@ -1,0 +1,555 @@
+// K2a — paged attention over block tables, split-K partials; K2b — the split-K reduction.
+//
+// Replaces paged_attention (src/minillm/attention/paged_torch_ref.py:40-74), which gathers every
+// sequence's context into a contiguous copy and runs SDPA, and the FlashInfer decode wrapper the
+// reference's CUDA backend calls (attention/flashinfer_backend.py:46).  Here the pages are read in place.
+//
+// Work decomposition (one CTA = one work unit x one KV head):
+//   unit = (sequence, query tile, page range).  A query tile is up to 8 "columns" = (query token,
+//   query head) pairs that share this KV head; a decode row of GQA group 4 is 4 columns.
+//   The CTA's 4 warps take the unit's pages round robin.  Each warp streams its pages through a private
+//   ring of STAGES shared-memory slots filled by the TMA engine: 32 one-dimensional bulk copies per
+//   page (16 K rows + 16 V rows of this head, one per lane) complete on the slot's mbarrier.  Shared
+//   rows are padded by 16 bytes so ldmatrix reads are free of bank conflicts.
+//   Per page and warp: S^T[16 tok x 8 col] = K[16 x Dh] . Q^T (m16n8k16 MMAs, fp32 accumulate),
+//   online softmax per column (exp2 domain), P^T goes back to a B fragment with movmatrix.trans, and
+//   O^T[Dh x 8] += V^T . P^T.  The 4 warps' (m, l, O) are merged through shared memory at the end.
+// f32 pools take a CUDA-core path with the same decomposition (fp32 accuracy, 1e-5).
+#include "attn_args.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr float kNegInf = -__builtin_huge_valf();
+
+struct UnitInfo {
+  int seq, q0, n_new, L, t0, ncols, pb, pe, part_row;
+};
+
+__device__ __forceinline__ UnitInfo unit_info(const AttnArgs& a, int unit_idx) {
+  const mlb_work_unit u = a.units[unit_idx];
+  UnitInfo r;
+  r.seq = u.seq;
+  r.q0 = a.qo[u.seq];
+  r.n_new = a.qo[u.seq + 1] - r.q0;
+  r.L = a.seq_lens[u.seq];
+  r.t0 = u.q_tile * a.tile_tokens;
+  r.ncols = min(a.tile_tokens, r.n_new - r.t0) * a.group;
+  r.pb = u.page_begin;
+  r.pe = u.page_end;
+  r.part_row = u.part_row;
+  return r;
+}
+
+// Exclusive key limit of column j: its query token sits at position L - n_new + qi and sees keys up to
+// and including itself (causal, aligned to the end of the context; a decode row sees all L keys).
+__device__ __forceinline__ int column_limit(const AttnArgs& a, const UnitInfo& ui, int j) {
+  if (j >= ui.ncols) return 0;
+  return ui.L - ui.n_new + ui.t0 + j / a.group + 1;
+}
+
+// Merge the warps' (m, l, O[col][dim]) states and write the unit's result: the final row when the unit
+// covers the whole context, else a normalised fp32 partial row plus its log2-sum-exp.
+template <int DH, int OUT_DT>
+__device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInfo& ui, int kvh,
+                                                const float* const* so, const float* const* sm,
+                                                const float* const* sl) {
+  for (int idx = threadIdx.x; idx < ui.ncols * DH; idx += blockDim.x) {
+    const int j = idx / DH, d = idx % DH;
+    float M = kNegInf;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm[w][j]);
+    float lsum = 0.f, acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float mw = sm[w][j];
+      const float e = mw == kNegInf ? 0.f : fast_exp2(mw - M);
+      lsum += e * sl[w][j];
+      acc += e * so[w][j * DH + d];
+    }
+    const float val = lsum > 0.f ? acc / lsum : 0.f;
+    const int qi = ui.t0 + j / a.group;
+    const int head = kvh * a.group + j % a.group;
+    if (ui.part_row < 0) {
+      char* o = a.out + ((static_cast<int64_t>(ui.q0 + qi) * a.o_st + static_cast<int64_t>(head) * a.o_sh + d) *
+                         Elt<OUT_DT>::bytes);
+      store_f32<OUT_DT>(o, val);
+    } else {
+      const int64_t row = ui.part_row + j / a.group;
+      a.part_o[(row * a.h + head) * DH + d] = val;
+      if (d == 0) a.part_lse[row * a.h + head] = lsum > 0.f ? M + log2f(lsum) : kNegInf;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ 16-bit pools: tensor-core tiles
+
+template <int DT, int DH, int STAGES>
+__global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_mma_kernel(AttnArgs a) {
+  using T = typename Elt<DT>::T;
+  constexpr int ROWB = DH * 2 + 16;  // padded shared row: 8 consecutive rows hit 8 distinct 16B bank groups
+  constexpr int TILE = 16 * ROWB;    // one page of one head, K or V
+  constexpr int STAGE = 2 * TILE;
+  constexpr int KSTEPS = DH / 16;
+  constexpr uint32_t PAGE_BYTES = 2u * 16u * DH * 2u;  // K + V rows of one head of one page
+  static_assert(8 * DH * 4 + 64 <= STAGES * STAGE, "merge state must fit in a warp's ring");
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bars[kWarps][STAGES];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x % a.hkv;
+  const UnitInfo ui = unit_info(a, blockIdx.x / a.hkv);
+  uint8_t* ring = smem + warp * STAGES * STAGE;
+
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[warp][s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+
+  const int pb = ui.pb + warp;
+  const int npages = pb < ui.pe ? (ui.pe - pb + kWarps - 1) / kWarps : 0;
+  const int32_t* table = a.bt + static_cast<int64_t>(ui.seq) * a.bt_stride;
+
+  // Block ids of this warp's pages, 32 at a time (lane i holds page i of the window); the next window
+  // is loaded one window ahead so its latency hides behind the current one.
+  auto load_window = [&](int w) -> int {
+    const int i = w * 32 + lane;
+    return i < npages ? __ldg(table + pb + i * kWarps) : 0;
+  };
+  int ids_cur = load_window(0), ids_nxt = load_window(1), win = 0;
+  uint32_t bad_mask = 0;  // bit s: the page in slot s had a block id outside the pool
+
+  auto issue = [&](int j) {
+    if ((j >> 5) != win) {
+      ++win;
+      ids_cur = ids_nxt;
+      ids_nxt = load_window(win + 1);
+    }
+    const int bid = __shfl_sync(0xffffffffu, ids_cur, j & 31);
+    const int s = j % STAGES;
+    uint64_t* bar = &bars[warp][s];
+    const bool ok = bid >= 0 && bid < a.num_blocks;
+    bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
+    if (lane == 0) {
+      if (!ok) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+      mbar_arrive_expect_tx(bar, ok ? PAGE_BYTES : 0u);
+    }
+    __syncwarp();
+    if (ok) {
+      const int row = lane & 15;
+      const bool isv = lane >= 16;
+      const char* src = (isv ? a.v_cache : a.k_cache) +
+                        ((static_cast<int64_t>(bid) * kBlockSize + row) * a.hkv + kvh) * (DH * 2);
+      bulk_g2s(ring + s * STAGE + (isv ? TILE : 0) + row * ROWB, src, DH * 2, bar);
+    }
+  };
+
+  for (int j = 0; j < STAGES && j < npages; ++j) issue(j);
+
+  // Q^T as B fragments (column n = lane / 4, dims 2 * (lane % 4) + {0, 1} (+8)), loaded once.
+  uint32_t qb[KSTEPS][2];
+  {
+    const int n = lane >> 2, c2 = (lane & 3) * 2;
+    const bool live = n < ui.ncols;
+    const int tok = ui.q0 + ui.t0 + (live ? n / a.group : 0);
+    const int head = kvh * a.group + (live ? n % a.group : 0);
+    const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
+                           static_cast<int64_t>(head) * a.q_sh;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      if (live) {
+        const int d = ks * 16 + c2;
+        qb[ks][0] = static_cast<uint32_t>(__ldg(qrow + d)) | (static_cast<uint32_t>(__ldg(qrow + d + 1)) << 16);
+        qb[ks][1] = static_cast<uint32_t>(__ldg(qrow + d + 8)) | (static_cast<uint32_t>(__ldg(qrow + d + 9)) << 16);
+      } else {
+        qb[ks][0] = qb[ks][1] = 0u;
+      }
+    }
+  }
+
+  const int r0 = lane >> 2;
+  const int j0 = (lane & 3) * 2, j1 = j0 + 1;
+  const int lim0 = column_limit(a, ui, j0), lim1 = column_limit(a, ui, j1);
+  float o[DH / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+
+  // lane-constant parts of the ldmatrix addresses
+  const uint32_t ring_u32 = smem_u32(ring);
+  const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
+  const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
+
+  bool timed_out = false;
+  for (int i = 0; i < npages; ++i) {
+    const int s = i % STAGES;
+    const uint32_t parity = (i / STAGES) & 1;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[warp][s], parity, a.wait_ns))) {
+      // A copy that never lands: record it, drain the other slots in flight (bounded) and stop.
+      if (lane == 0) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
+      for (int k = i + 1; k < npages && k < i + STAGES; ++k)
+        mbar_wait_bounded(&bars[warp][k % STAGES], (k / STAGES) & 1, a.wait_ns);
+      timed_out = true;
+      break;
+    }
+    if (!((bad_mask >> s) & 1u)) {
+      const int tok_base = (pb + i * kWarps) * kBlockSize;
+      uint8_t* vt = ring + s * STAGE + TILE;
+      const int live_rows = ui.L - tok_base;
+      if (live_rows < 16) {
+        // Rows past the context end hold another request's data or junk; P is 0 there, but 0 * NaN
+        // would still poison O, so clear those V rows.
+        const int r_begin = live_rows < 0 ? 0 : live_rows;
+        constexpr int VEC_PER_ROW = DH * 2 / 16;
+        for (int e = lane; e < (16 - r_begin) * VEC_PER_ROW; e += 32) {
+          const int r = r_begin + e / VEC_PER_ROW, c = e % VEC_PER_ROW;
+          *reinterpret_cast<uint4*>(vt + r * ROWB + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+      }
+
+      // S^T = K . Q^T, two accumulators to halve the dependent-MMA chain
+      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t kaddr = ring_u32 + s * STAGE + k_off;
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        uint32_t x0, x1, x2, x3;
+        ldsm_x4(kaddr + ks * 32, x0, x1, x2, x3);
+        mma16816<DT>((ks & 1) ? sb : sa, x0, x1, x2, x3, qb[ks][0], qb[ks][1]);
+      }
+      const int tk0 = tok_base + r0, tk1 = tk0 + 8;
+      const float x0 = tk0 < lim0 ? (sa[0] + sb[0]) * a.sl2 : kNegInf;
+      const float x1 = tk0 < lim1 ? (sa[1] + sb[1]) * a.sl2 : kNegInf;
+      const float x2 = tk1 < lim0 ? (sa[2] + sb[2]) * a.sl2 : kNegInf;
+      const float x3 = tk1 < lim1 ? (sa[3] + sb[3]) * a.sl2 : kNegInf;
+
+      // online softmax per column; columns j0, j1 are shared by the 8 lanes with equal lane % 4
+      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+      }
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
+      const float al0 = fast_exp2(m0 - b0), al1 = fast_exp2(m1 - b1);
+      const float p0 = fast_exp2(x0 - b0), p2 = fast_exp2(x2 - b0);
+      const float p1 = fast_exp2(x1 - b1), p3 = fast_exp2(x3 - b1);
+      l0 = l0 * al0 + p0 + p2;
+      l1 = l1 * al1 + p1 + p3;
+      m0 = mn0;
+      m1 = mn1;
+#pragma unroll
+      for (int mt = 0; mt < DH / 16; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
+      }
+      // P (C layout: token rows, column pairs) -> P^T as the B operand (token = k, column = n)
+      const uint32_t pb0 = movm_t(pack2<DT>(p0, p1));
+      const uint32_t pb1 = movm_t(pack2<DT>(p2, p3));
+      const uint32_t vaddr = ring_u32 + s * STAGE + TILE + v_off;
+#pragma unroll
+      for (int mt = 0; mt < DH / 16; ++mt) {
+        uint32_t y0, y1, y2, y3;
+        ldsm_x4_t(vaddr + mt * 32, y0, y1, y2, y3);
+        mma16816<DT>(o[mt], y0, y1, y2, y3, pb0, pb1);
+      }
+    }
+    __syncwarp();
+    if (i + STAGES < npages) {
+      fence_proxy_async();  // order this slot's generic reads/writes before the next async-proxy fill
+      issue(i + STAGES);
+    }
+  }
+
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  if (timed_out) {
+    m0 = m1 = kNegInf;
+    l0 = l1 = 0.f;
+  }
+  // Stash this warp's state in its own ring: every copy into it has landed and been consumed.
+  __syncwarp();
+  float* so = reinterpret_cast<float*>(ring);
+  float* sm = so + 8 * DH;
+  float* sl = sm + 8;
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) {
+    const int d = mt * 16 + r0;
+    so[j0 * DH + d] = o[mt][0];
+    so[j1 * DH + d] = o[mt][1];
+    so[j0 * DH + d + 8] = o[mt][2];
+    so[j1 * DH + d + 8] = o[mt][3];
+  }
+  if (lane < 4) {
+    sm[j0] = m0;
+    sm[j1] = m1;
+    sl[j0] = l0;
+    sl[j1] = l1;
+  }
+  __syncthreads();
+  const float* so_w[kWarps];
+  const float* sm_w[kWarps];
+  const float* sl_w[kWarps];
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    so_w[w] = reinterpret_cast<const float*>(smem + w * STAGES * STAGE);
+    sm_w[w] = so_w[w] + 8 * DH;
+    sl_w[w] = sm_w[w] + 8;
+  }
+  merge_and_store<DH, DT>(a, ui, kvh, so_w, sm_w, sl_w);
+}
+
+// ------------------------------------------------------------------ f32 pools: CUDA cores
+
+template <int DH>
+__global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a) {
+  constexpr int HALF = DH / 2;
+  constexpr int DPL = DH / 32;  // dims per lane in the P.V product
+  constexpr int MSTRIDE = 8 * DH + 16;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* qs = reinterpret_cast<float*>(smem);  // [8][DH]
+  float* ms = qs + 8 * DH;                     // [warps][8 * DH + 16]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x % a.hkv;
+  const UnitInfo ui = unit_info(a, blockIdx.x / a.hkv);
+  const float* q = reinterpret_cast<const float*>(a.q);
+  for (int idx = threadIdx.x; idx < 8 * DH; idx += blockDim.x) {
+    const int j = idx / DH, d = idx % DH;
+    float x = 0.f;
+    if (j < ui.ncols) {
+      const int tok = ui.q0 + ui.t0 + j / a.group, head = kvh * a.group + j % a.group;
+      x = q[static_cast<int64_t>(tok) * a.q_st + static_cast<int64_t>(head) * a.q_sh + d];
+    }
+    qs[idx] = x;
+  }
+  __syncthreads();
+
+  int lim[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) lim[j] = column_limit(a, ui, j);
+  float o[8][DPL], m[8], l[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    m[j] = kNegInf;
+    l[j] = 0.f;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) o[j][i] = 0.f;
+  }
+  const int t = lane & 15, half = lane >> 4;
+  const int32_t* table = a.bt + static_cast<int64_t>(ui.seq) * a.bt_stride;
+  const float* kc = reinterpret_cast<const float*>(a.k_cache);
+  const float* vc = reinterpret_cast<const float*>(a.v_cache);
+
+  for (int page = ui.pb + warp; page < ui.pe; page += kWarps) {
+    const int bid = __ldg(table + page);
+    if (bid < 0 || bid >= a.num_blocks) {
+      if (lane == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+      continue;
+    }
+    const int tok = page * kBlockSize + t;
+    const float* krow = kc + ((static_cast<int64_t>(bid) * kBlockSize + t) * a.hkv + kvh) * DH + half * HALF;
+    float sc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < HALF; c += 4) {
+      const float4 kv = __ldg(reinterpret_cast<const float4*>(krow + c));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < ui.ncols) {
+          const float4 qv = *reinterpret_cast<const float4*>(qs + j * DH + half * HALF + c);
+          sc[j] = fmaf(kv.x, qv.x, fmaf(kv.y, qv.y, fmaf(kv.z, qv.z, fmaf(kv.w, qv.w, sc[j]))));
+        }
+      }
+    }
+    float p[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= ui.ncols) {
+        p[j] = 0.f;
+        continue;
+      }
+      const float s = sc[j] + __shfl_xor_sync(0xffffffffu, sc[j], 16);
+      const float x = tok < lim[j] ? s * a.sl2 : kNegInf;
+      float mx = x;
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[j], mx);
+      const float b = mn == kNegInf ? 0.f : mn;
+      const float al = fast_exp2(m[j] - b);
+      p[j] = fast_exp2(x - b);
+      float ps = p[j];
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l[j] = l[j] * al + ps;
+      m[j] = mn;
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) o[j][i] *= al;
+    }
+    const int live = min(kBlockSize, ui.L - page * kBlockSize);  // rows past the context end are skipped
+    for (int r = 0; r < live; ++r) {
+      const float* vrow = vc + ((static_cast<int64_t>(bid) * kBlockSize + r) * a.hkv + kvh) * DH;
+      float vv[DPL];
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) vv[i] = __ldg(vrow + lane + 32 * i);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (j < ui.ncols) {
+          const float pj = __shfl_sync(0xffffffffu, p[j], r);
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) o[j][i] = fmaf(pj, vv[i], o[j][i]);
+        }
+      }
+    }
+  }
+
+  float* so = ms + warp * MSTRIDE;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) so[j * DH + lane + 32 * i] = o[j][i];
+  if (lane == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      so[8 * DH + j] = m[j];
+      so[8 * DH + 8 + j] = l[j];
+    }
+  }
+  __syncthreads();
+  const float* so_w[kWarps];
+  const float* sm_w[kWarps];
+  const float* sl_w[kWarps];
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    so_w[w] = ms + w * MSTRIDE;
+    sm_w[w] = so_w[w] + 8 * DH;
+    sl_w[w] = sm_w[w] + 8;
+  }
+  merge_and_store<DH, MLB_F32>(a, ui, kvh, so_w, sm_w, sl_w);
+}
+
+// ------------------------------------------------------------------ split-K reduction
+
+template <int DH, int OUT_DT>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* po, const float* plse,
+                                                            const int32_t* rrows, const int32_t* rchunks, int tpt,
+                                                            int64_t ntok, int h, char* out, int64_t o_st,
+                                                            int64_t o_sh) {
+  constexpr int DPL = DH / 32;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= ntok * h) return;
+  const int64_t tok = wid / h;
+  const int head = static_cast<int>(wid % h);
+  const int nc = rchunks[tok];
+  if (nc <= 1) return;
+  const int64_t r0 = rrows[tok];
+  float M = kNegInf;
+  for (int c = lane; c < nc; c += 32) M = fmaxf(M, plse[(r0 + static_cast<int64_t>(c) * tpt) * h + head]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  float acc[DPL];
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
+  float lw = 0.f;
+  for (int c = 0; c < nc; ++c) {
+    const int64_t row = r0 + static_cast<int64_t>(c) * tpt;
+    const float lse = plse[row * h + head];
+    const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
+    lw += w;
+    const float* src = po + (row * h + head) * DH;
+#pragma unroll
+    for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, src[lane + 32 * i], acc[i]);
+  }
+  const float inv = lw > 0.f ? 1.f / lw : 0.f;
+  char* o = out + (tok * o_st + static_cast<int64_t>(head) * o_sh) * Elt<OUT_DT>::bytes;
+#pragma unroll
+  for (int i = 0; i < DPL; ++i) store_f32<OUT_DT>(o + (lane + 32 * i) * Elt<OUT_DT>::bytes, acc[i] * inv);
+}
+
+// Opt in to > 48 KB of dynamic shared memory once per kernel instance and device (`done` is the
+// caller's per-instance bit set of device ordinals < 64).
+template <typename K>
+cudaError_t set_smem(K kernel, int bytes, unsigned long long& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && (done >> dev) & 1ull) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev < 64) __atomic_fetch_or(&done, 1ull << dev, __ATOMIC_RELAXED);
+  return e;
+}
+
+template <int DT, int DH, int STAGES>
+cudaError_t launch_mma(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
+  constexpr int bytes = kWarps * STAGES * 2 * 16 * (DH * 2 + 16);
+  static unsigned long long done = 0;
+  auto k = paged_attn_mma_kernel<DT, DH, STAGES>;
+  cudaError_t e = set_smem(k, bytes, done);
+  if (e != cudaSuccess) return e;
+  k<<<static_cast<unsigned>(ctas), kWarps * 32, bytes, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int DH>
+cudaError_t launch_f32(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
+  constexpr int bytes = (8 * DH + kWarps * (8 * DH + 16)) * 4;
+  static unsigned long long done = 0;
+  auto k = paged_attn_f32_kernel<DH>;
+  cudaError_t e = set_smem(k, bytes, done);
+  if (e != cudaSuccess) return e;
+  k<<<static_cast<unsigned>(ctas), kWarps * 32, bytes, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
+  const int64_t ctas = num_units * a.hkv;
+  if (dtype == MLB_BF16) {
+    if (dh == 64) return launch_mma<MLB_BF16, 64, 4>(a, ctas, s);
+    if (dh == 128) return launch_mma<MLB_BF16, 128, 3>(a, ctas, s);
+    if (dh == 256) return launch_mma<MLB_BF16, 256, 2>(a, ctas, s);
+  } else if (dtype == MLB_F16) {
+    if (dh == 64) return launch_mma<MLB_F16, 64, 4>(a, ctas, s);
+    if (dh == 128) return launch_mma<MLB_F16, 128, 3>(a, ctas, s);
+    if (dh == 256) return launch_mma<MLB_F16, 256, 2>(a, ctas, s);
+  } else if (dtype == MLB_F32) {
+    if (dh == 64) return launch_f32<64>(a, ctas, s);
+    if (dh == 128) return launch_f32<128>(a, ctas, s);
+    if (dh == 256) return launch_f32<256>(a, ctas, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
+                                 int tpt, int64_t ntok, int h, int dh, char* out, int64_t o_st, int64_t o_sh,
+                                 int out_dtype, cudaStream_t s) {
+  const int64_t warps = ntok * h;
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+#define MLB_RED(D, O)                                                                                    \
+  if (dh == D && out_dtype == O) {                                                                       \
+    splitk_reduce_kernel<D, O><<<blocks, 256, 0, s>>>(po, plse, rrows, rchunks, tpt, ntok, h, out, o_st, \
+                                                      o_sh);                                             \
+    return cudaGetLastError();                                                                           \
+  }
+  MLB_RED(64, MLB_F32) MLB_RED(64, MLB_F16) MLB_RED(64, MLB_BF16)
+  MLB_RED(128, MLB_F32) MLB_RED(128, MLB_F16) MLB_RED(128, MLB_BF16)
+  MLB_RED(256, MLB_F32) MLB_RED(256, MLB_F16) MLB_RED(256, MLB_BF16)
+#undef MLB_RED
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace mlb

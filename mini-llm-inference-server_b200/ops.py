@@ -1,0 +1,274 @@
+"""Torch-facing wrappers of the C ABI: tensors in, raw pointers + strides + the current CUDA stream out.
+
+Every function validates what the kernels rely on (shapes, dtypes, devices, contiguity of the pools)
+and raises `ValueError` like the reference does for malformed input (metadata.py:75-76); device-side
+range faults (a bad slot or block id) are skipped by the kernels and recorded in an optional int32
+error word instead of faulting the GPU.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import WORK_UNIT_INT32S, check, lib
+
+DTYPE_CODE = {torch.float32: _lib.MLB_F32, torch.float16: _lib.MLB_F16, torch.bfloat16: _lib.MLB_BF16}
+BLOCK_SIZE = 16
+
+
+def _code(t: torch.Tensor, what: str) -> int:
+    try:
+        return DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise ValueError(f"{what}: dtype {t.dtype} not supported (float32, float16, bfloat16)") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _check_pool(pool: torch.Tensor, what: str) -> None:
+    if pool.dim() != 4 or not pool.is_contiguous():
+        raise ValueError(f"{what}: pools are contiguous [num_blocks, block_size, Hkv, Dh], got {tuple(pool.shape)}")
+    if not pool.is_cuda:
+        raise ValueError(f"{what}: pools must be CUDA tensors")
+
+
+def _check_rows(x: torch.Tensor, hkv: int, dh: int, what: str) -> None:
+    if x.dim() != 3 or x.shape[1:] != (hkv, dh) or (x.shape[0] and x.stride(2) != 1):
+        raise ValueError(f"{what}: rows must be [N, {hkv}, {dh}] with unit stride on the last dim, "
+                         f"got {tuple(x.shape)} strides {x.stride()}")
+
+
+# ---------------------------------------------------------------- K1: append
+
+
+def kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, slot_mapping: torch.Tensor, k: torch.Tensor,
+              v: torch.Tensor, err: torch.Tensor | None = None) -> None:
+    """write_kv (paged_torch_ref.py:23-28) on the GPU: pools[slot_mapping[i]] = k[i] / v[i], cast to the
+    pool dtype (round to nearest even).  k, v may be strided views [N, Hkv, Dh]."""
+    _check_pool(k_cache, "kv_append")
+    _check_pool(v_cache, "kv_append")
+    nb, bs, hkv, dh = k_cache.shape
+    if v_cache.shape != k_cache.shape or v_cache.dtype != k_cache.dtype:
+        raise ValueError("kv_append: k_cache and v_cache differ")
+    _check_rows(k, hkv, dh, "kv_append k")
+    _check_rows(v, hkv, dh, "kv_append v")
+    n = k.shape[0]
+    if v.shape[0] != n or slot_mapping.shape != (n,):
+        raise ValueError(f"kv_append: {n} k rows, {v.shape[0]} v rows, slot_mapping {tuple(slot_mapping.shape)}")
+    if slot_mapping.dtype != torch.long or not slot_mapping.is_contiguous():
+        raise ValueError("kv_append: slot_mapping must be a contiguous int64 tensor")
+    if k.dtype != v.dtype:
+        raise ValueError("kv_append: k and v dtypes differ")
+    for t in (v_cache, slot_mapping, k, v):
+        if t.device != k_cache.device:
+            raise ValueError("kv_append: all tensors must be on the pools' device")
+    if n == 0:
+        return
+    rc = lib().mlb_kv_append(k_cache.data_ptr(), v_cache.data_ptr(), _code(k_cache, "kv_append"), nb, bs,
+                             slot_mapping.data_ptr(), k.data_ptr(), k.stride(0), k.stride(1), v.data_ptr(),
+                             v.stride(0), v.stride(1), _code(k, "kv_append"), n, hkv, dh, _ptr(err),
+                             _stream(k_cache.device))
+    check(rc, "kv_append")
+
+
+# ---------------------------------------------------------------- K2: plan, attention, reduction
+
+
+@dataclass
+class AttentionPlan:
+    """A step's split of paged-attention work (built once per AttentionMetadata, reused by every layer)."""
+
+    units: torch.Tensor  # device int32 [num_units, 8]: mlb_work_unit records
+    num_units: int
+    reduce_rows: torch.Tensor  # device int32 [N]
+    reduce_chunks: torch.Tensor  # device int32 [N]
+    num_partial_rows: int
+    tokens_per_tile: int
+    num_heads: int
+    num_kv_heads: int
+    num_tokens: int
+    units_host: np.ndarray  # the same records on the host (inspection and tests)
+    reduce_chunks_host: np.ndarray  # [N] splits per token on the host
+
+
+def _i32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32))
+
+
+def plan_attention(qo_indptr: list[int], seq_lens: list[int], max_blocks: int, num_heads: int, num_kv_heads: int,
+                   device: torch.device | str, block_size: int = BLOCK_SIZE, num_sms: int | None = None,
+                   pages_per_unit: int = 0) -> AttentionPlan:
+    """Split the step into units (host work, like FlashInfer's plan(); flashinfer_backend.py:48-64).
+
+    qo_indptr / seq_lens are the host lists AttentionMetadata keeps (metadata.py:39-40), so planning
+    needs no device round trip.  The plan is copied to the device in one transfer.
+    """
+    device = torch.device(device)
+    qo, lens = _i32(qo_indptr), _i32(seq_lens)
+    s = len(lens)
+    if qo.shape != (s + 1,):
+        raise ValueError(f"plan: qo_indptr has {qo.shape[0]} entries for {s} sequences")
+    n_tok = int(qo[-1]) if s else 0
+    if num_sms is None:
+        num_sms = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 148
+    L = lib()
+    cap = L.mlb_plan_capacity(qo.ctypes.data, lens.ctypes.data, s, num_heads, num_kv_heads, block_size)
+    if cap < 0:
+        cap = 0  # invalid input: the planner itself reports why
+    units = np.zeros((max(cap, 1), WORK_UNIT_INT32S), dtype=np.int32)
+    rows = np.empty(max(n_tok, 1), dtype=np.int32)
+    chunks = np.empty(max(n_tok, 1), dtype=np.int32)
+    nu, npart = ctypes.c_int64(0), ctypes.c_int64(0)
+
+    def run() -> int:
+        return L.mlb_plan_attention(qo.ctypes.data, lens.ctypes.data, s, max_blocks, num_heads, num_kv_heads,
+                                    block_size, num_sms, pages_per_unit, units.ctypes.data, units.shape[0],
+                                    ctypes.byref(nu), rows.ctypes.data, chunks.ctypes.data, n_tok,
+                                    ctypes.byref(npart))
+
+    rc = run()
+    if rc == _lib.MLB_ENOSPACE:  # an explicit pages_per_unit below the capacity estimate's minimum
+        units = np.zeros((nu.value, WORK_UNIT_INT32S), dtype=np.int32)
+        rc = run()
+    check(rc, "plan_attention")
+    n_units = nu.value
+    # one host -> device copy for the whole plan
+    packed = np.concatenate([units[:n_units].reshape(-1), rows[:n_tok], chunks[:n_tok]])
+    host = torch.from_numpy(packed)
+    dev = host.pin_memory().to(device, non_blocking=True) if device.type == "cuda" else host.clone()
+    u = n_units * WORK_UNIT_INT32S
+    plan = AttentionPlan(dev[:u].view(n_units, WORK_UNIT_INT32S), n_units, dev[u:u + n_tok],
+                         dev[u + n_tok:u + 2 * n_tok], npart.value, max(1, 8 // (num_heads // num_kv_heads)),
+                         num_heads, num_kv_heads, n_tok, units[:n_units].copy(), chunks[:n_tok].copy())
+    return plan
+
+
+class Workspace:
+    """Split-K scratch (fp32 partial rows + their log-sum-exp), grown on demand and reused across calls."""
+
+    def __init__(self) -> None:
+        self._o: torch.Tensor | None = None
+        self._lse: torch.Tensor | None = None
+
+    def get(self, rows: int, heads: int, dh: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        need_o, need_l = rows * heads * dh, rows * heads
+        if self._o is None or self._o.device != device or self._o.numel() < need_o:
+            self._o = torch.empty(max(need_o, 1), dtype=torch.float32, device=device)
+        if self._lse is None or self._lse.device != device or self._lse.numel() < need_l:
+            self._lse = torch.empty(max(need_l, 1), dtype=torch.float32, device=device)
+        return self._o, self._lse
+
+
+def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                    seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan,
+                    workspace: Workspace | None = None, out: torch.Tensor | None = None, scale: float | None = None,
+                    err: torch.Tensor | None = None) -> torch.Tensor:
+    """paged_attention (paged_torch_ref.py:40-74) on the GPU: q [N, H, Dh] -> [N, H, Dh] in q's dtype.
+
+    block_tables int32 [S, W], seq_lens int32 [S], qo_indptr int32 [S + 1] are AttentionMetadata's
+    device tensors (block_tables_i32, seq_lens_i32, qo_indptr).  The pools must already hold this
+    step's k/v (kv_append first).  Launches the attention kernel, then the split-K reduction when the
+    plan split any sequence.
+    """
+    workspace = workspace or Workspace()
+    out = attention_partials(q, k_cache, v_cache, block_tables, seq_lens, qo_indptr, plan, workspace, out, scale,
+                             err)
+    splitk_reduce(plan, workspace, out)
+    return out
+
+
+def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                       seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan, workspace: Workspace,
+                       out: torch.Tensor | None = None, scale: float | None = None,
+                       err: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention kernel alone (K2a): unsplit sequences are final in `out`; split ones leave fp32 partial
+    rows in `workspace` for `splitk_reduce`."""
+    _check_pool(k_cache, "paged_attention")
+    _check_pool(v_cache, "paged_attention")
+    nb, bs, hkv, dh = k_cache.shape
+    if q.dim() != 3 or q.shape[2] != dh or (q.shape[0] and q.stride(2) != 1):
+        raise ValueError(f"paged_attention: q must be [N, H, {dh}] with unit last stride, got {tuple(q.shape)}")
+    n, h = q.shape[0], q.shape[1]
+    if q.dtype != k_cache.dtype or v_cache.dtype != k_cache.dtype or v_cache.shape != k_cache.shape:
+        raise ValueError(f"paged_attention: q {q.dtype} and pools {k_cache.dtype}/{v_cache.dtype} must agree")
+    if (plan.num_heads, plan.num_kv_heads, plan.num_tokens) != (h, hkv, n):
+        raise ValueError("paged_attention: the plan was built for another shape")
+    for t, name in ((block_tables, "block_tables"), (seq_lens, "seq_lens"), (qo_indptr, "qo_indptr")):
+        if t.dtype != torch.int32 or not t.is_contiguous() or t.device != q.device:
+            raise ValueError(f"paged_attention: {name} must be a contiguous int32 tensor on {q.device}")
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1:
+        raise ValueError("paged_attention: out must match q")
+    if n == 0 or plan.num_units == 0:
+        return out
+    scale = 1.0 / math.sqrt(dh) if scale is None else float(scale)
+    po = plse = None
+    if plan.num_partial_rows:
+        po, plse = workspace.get(plan.num_partial_rows, h, dh, q.device)
+    rc = lib().mlb_paged_attention(q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+                                   _code(q, "paged_attention"), nb, bs, h, hkv, dh, scale, block_tables.data_ptr(),
+                                   block_tables.stride(0), seq_lens.data_ptr(), qo_indptr.data_ptr(),
+                                   seq_lens.shape[0], plan.units.data_ptr(), plan.num_units, _ptr(po), _ptr(plse),
+                                   plan.num_partial_rows, out.data_ptr(), out.stride(0), out.stride(1), _ptr(err),
+                                   _stream(q.device))
+    check(rc, "paged_attention")
+    return out
+
+
+def splitk_reduce(plan: AttentionPlan, workspace: Workspace, out: torch.Tensor) -> None:
+    """K2b: combine the split sequences' partial rows into `out` (no-op when the plan split nothing)."""
+    if not plan.num_partial_rows or plan.num_tokens == 0:
+        return
+    n, h, dh = out.shape
+    po, plse = workspace.get(plan.num_partial_rows, h, dh, out.device)
+    rc = lib().mlb_splitk_reduce(po.data_ptr(), plse.data_ptr(), plan.num_partial_rows, plan.reduce_rows.data_ptr(),
+                                 plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, n, h, dh, out.data_ptr(),
+                                 out.stride(0), out.stride(1), _code(out, "splitk_reduce"), _stream(out.device))
+    check(rc, "splitk_reduce")
+
+
+# ---------------------------------------------------------------- K3: block copy
+
+
+def pool_pointer_table(pools: list[torch.Tensor]) -> torch.Tensor:
+    """Device int64 array of pool base addresses (every layer's K and V), the block copy's `pools`."""
+    if not pools:
+        raise ValueError("block_copy: no pools")
+    first = pools[0]
+    for p in pools:
+        _check_pool(p, "block_copy")
+        if p.shape != first.shape or p.dtype != first.dtype or p.device != first.device:
+            raise ValueError("block_copy: every pool must have the same shape, dtype and device")
+    ptrs = torch.tensor([p.data_ptr() for p in pools], dtype=torch.int64)
+    return ptrs.to(first.device)
+
+
+def block_copy(pool_ptrs: torch.Tensor, template: torch.Tensor, src: torch.Tensor, dst: torch.Tensor,
+               err: torch.Tensor | None = None) -> None:
+    """pool[dst[i]] = pool[src[i]] for every pool in `pool_ptrs` (see `pool_pointer_table`); `template` is
+    any one of the pools (it fixes num_blocks and the block size in bytes).  src / dst: device int32."""
+    if src.shape != dst.shape or src.dim() != 1:
+        raise ValueError("block_copy: src and dst must be 1-D and of equal length")
+    for t, name in ((src, "src"), (dst, "dst")):
+        if t.dtype != torch.int32 or not t.is_contiguous() or t.device != template.device:
+            raise ValueError(f"block_copy: {name} must be a contiguous int32 tensor on {template.device}")
+    if src.numel() == 0:
+        return
+    nb = template.shape[0]
+    block_bytes = template[0].numel() * template.element_size()
+    rc = lib().mlb_block_copy(pool_ptrs.data_ptr(), pool_ptrs.numel(), nb, block_bytes, src.data_ptr(),
+                              dst.data_ptr(), src.numel(), _ptr(err), _stream(template.device))
+    check(rc, "block_copy")

@@ -1,0 +1,120 @@
+"""B200Backend as a drop-in AttentionBackend, in the shape of the reference's own kernel tests
+(tests/test_kernels.py:29-72: a mixed ragged step and a decode-only step, pool writes bit-identical,
+outputs within 2e-2), plus plan reuse across layers and a multi-step decode loop."""
+
+from __future__ import annotations
+
+import random
+
+import pytest
+import torch
+
+import oracle
+from paged_helpers import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def mixed_step(mlb, dev, h=8, hkv=2, dh=128, bs=16, dtype=torch.bfloat16):
+    """tests/test_kernels.py:29-48: fresh prompt, decode, prompt on top of cache, 1-token prompt, decode."""
+    torch.manual_seed(0)
+    steps = [(0, 37), (90, 1), (40, 25), (0, 1), (300, 1)]
+    k_pool = torch.randn(64, bs, hkv, dh, device=dev, dtype=dtype)
+    v_pool = torch.randn_like(k_pool)
+    free = list(range(64))
+    random.Random(3).shuffle(free)
+    seqs = []
+    for cached, new in steps:
+        n = cached + new
+        seqs.append(mlb.SeqStep(cached, new, [free.pop() for _ in range(-(-n // bs))]))
+    meta = mlb.AttentionMetadata.build(seqs, bs, dev)
+    n = meta.query_start_loc[-1]
+    q = torch.randn(n, h, dh, device=dev, dtype=dtype)
+    k = torch.randn(n, hkv, dh, device=dev, dtype=dtype)
+    v = torch.randn(n, hkv, dh, device=dev, dtype=dtype)
+    return q, k, v, k_pool, v_pool, meta, seqs
+
+
+def reference(q, k, v, k_pool, v_pool, seqs):
+    om = oracle.build_metadata([(s.num_cached, s.num_new, s.block_ids) for s in seqs], 16)
+    kp, vp = k_pool.cpu(), v_pool.cpu()
+    out = oracle.forward(q.cpu(), k.cpu(), v.cpu(), kp, vp, om)
+    return out, kp, vp
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+def test_backend_matches_reference_on_a_mixed_step(mlb, cuda, dtype):
+    q, k, v, k_pool, v_pool, meta, seqs = mixed_step(mlb, cuda, dtype=dtype)
+    expected, ref_k, ref_v = reference(q, k, v, k_pool, v_pool, seqs)
+    backend = mlb.get_backend("b200")
+    got = backend.forward(q, k, v, k_pool, v_pool, meta)
+    assert torch.equal(k_pool.cpu(), ref_k) and torch.equal(v_pool.cpu(), ref_v)  # identical writes
+    assert got.dtype == q.dtype and got.shape == q.shape
+    torch.testing.assert_close(got.float().cpu(), expected, atol=2e-2, rtol=2e-2)
+
+
+def test_backend_on_a_decode_only_step(mlb, cuda):
+    q, k, v, k_pool, v_pool, _, _ = mixed_step(mlb, cuda)
+    seqs = [mlb.SeqStep(c, 1, list(range(i * 4, i * 4 + 4))) for i, c in enumerate([5, 63, 17])]
+    meta = mlb.AttentionMetadata.build(seqs, 16, cuda)
+    q, k, v = q[:3], k[:3], v[:3]
+    expected, _, _ = reference(q, k, v, k_pool, v_pool, seqs)
+    got = mlb.B200Backend().forward(q, k, v, k_pool, v_pool, meta)
+    torch.testing.assert_close(got.float().cpu(), expected, atol=2e-2, rtol=2e-2)
+
+
+def test_plan_is_built_once_per_step_and_reused_by_every_layer(mlb, cuda):
+    q, k, v, k_pool, v_pool, meta, seqs = mixed_step(mlb, cuda, h=32, hkv=8)
+    layers = [(k_pool.clone(), v_pool.clone()) for _ in range(4)]
+    backend = mlb.B200Backend()
+    outs, plans = [], []
+    for kp, vp in layers:
+        outs.append(backend.forward(q, k, v, kp, vp, meta))
+        plans.append(backend._plan)
+    assert all(p is plans[0] for p in plans)
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    meta2 = mlb.AttentionMetadata.build(seqs, 16, cuda)  # a new step gets a new plan
+    backend.forward(q, k, v, *layers[0], meta2)
+    assert backend._plan is not plans[0]
+
+
+def test_decode_loop_matches_reference_every_step(mlb, cuda):
+    """Several engine steps: sequences grow one token per step, taking a new block at each boundary."""
+    h, hkv, dh, nb = 32, 8, 128, 128
+    g = torch.Generator(device=cuda).manual_seed(11)
+    k_pool = torch.randn(nb, 16, hkv, dh, device=cuda, generator=g).to(torch.bfloat16)
+    v_pool = torch.randn(nb, 16, hkv, dh, device=cuda, generator=g).to(torch.bfloat16)
+    bm = mlb.BlockManager(nb, 16)
+    cached = [14, 31, 1, 47, 100]
+    tables = [bm.allocate(-(-c // 16)) for c in cached]
+    backend = mlb.B200Backend()
+    for _ in range(5):
+        for i, c in enumerate(cached):
+            if c + 1 > len(tables[i]) * 16:
+                tables[i] += bm.allocate(1)
+        seqs = [mlb.SeqStep(c, 1, list(t)) for c, t in zip(cached, tables)]
+        meta = mlb.AttentionMetadata.build(seqs, 16, cuda)
+        n = len(seqs)
+        q = torch.randn(n, h, dh, device=cuda, generator=g).to(torch.bfloat16)
+        k = torch.randn(n, hkv, dh, device=cuda, generator=g).to(torch.bfloat16)
+        v = torch.randn(n, hkv, dh, device=cuda, generator=g).to(torch.bfloat16)
+        expected, ref_k, _ = reference(q, k, v, k_pool, v_pool, seqs)
+        got = backend.forward(q, k, v, k_pool, v_pool, meta)
+        assert torch.equal(k_pool.cpu(), ref_k)
+        assert_close(got, expected, torch.bfloat16)
+        cached = [c + 1 for c in cached]
+    bm.check(tables)
+
+
+def test_forward_is_stream_ordered_without_host_syncs(mlb, cuda):
+    """Everything goes on torch's current stream: running on a side stream gives the same answer."""
+    q, k, v, k_pool, v_pool, meta, _ = mixed_step(mlb, cuda, h=32, hkv=8)
+    kp2, vp2 = k_pool.clone(), v_pool.clone()
+    base = mlb.B200Backend().forward(q, k, v, k_pool, v_pool, meta)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        got = mlb.B200Backend().forward(q, k, v, kp2, vp2, meta)
+    torch.cuda.current_stream().wait_stream(side)
+    assert torch.equal(got, base)

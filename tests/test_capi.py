@@ -1,0 +1,128 @@
+"""The C-ABI library without a GPU: it loads, exports exactly what include/*.h declares, and its host-side
+entry points (the planner, argument validation) behave.  No call here launches a kernel."""
+
+from __future__ import annotations
+
+import ctypes
+import random
+import re
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def declared_symbols() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"MLB_API\s+[\w\s\*]+?\b(mlb_\w+)\s*\(", text))
+    return names
+
+
+@pytest.fixture(scope="module")
+def L(mlb):
+    from importlib import import_module
+
+    return import_module(mlb.__name__ + "._lib")
+
+
+def test_library_exports_every_declared_symbol(L):
+    declared = declared_symbols()
+    assert declared, "no MLB_API declarations found"
+    lib = L.lib()
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert declared == set(L.EXPORTS)
+    assert lib.mlb_abi_version() == 1
+
+
+def test_work_unit_layout_matches_header(L):
+    assert ctypes.sizeof(L.WorkUnit) == 32 and L.WORK_UNIT_INT32S == 8
+
+
+def test_invalid_arguments_return_status_without_launching(L):
+    lib = L.lib()
+    # unknown dtype, null pointers: rejected on the host with a message
+    rc = lib.mlb_kv_append(None, None, 7, 10, 16, None, None, 0, 0, None, 0, 0, 2, 1, 2, 64, None, None)
+    assert rc == L.MLB_EINVAL and "dtype" in L.last_error()
+    rc = lib.mlb_kv_append(None, None, 2, 10, 16, None, None, 0, 0, None, 0, 0, 2, 1, 2, 64, None, None)
+    assert rc == L.MLB_EINVAL and "null" in L.last_error()
+    rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 32, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
+                                 None, None, 0, None, 0, 0, None, None)
+    assert rc == L.MLB_EUNSUPPORTED and "block_size" in L.last_error()
+    rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 16, 32, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
+                                 None, None, 0, None, 0, 0, None, None)
+    assert rc == L.MLB_EUNSUPPORTED and "query heads per KV head" in L.last_error()
+    rc = lib.mlb_block_copy(None, 2, 10, 100, None, None, 3, None, None)
+    assert rc == L.MLB_EUNSUPPORTED
+    rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 8, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
+                                 None, None, 0, None, 0, 0, None, None)
+    with pytest.raises(ValueError, match="block_size"):  # status codes become the reference's ValueError
+        L.check(rc, "paged_attention")
+    # zero work is a successful no-op
+    assert lib.mlb_block_copy(None, 0, 10, 64, None, None, 0, None, None) == L.MLB_OK
+
+
+def plan(mlb, steps, h=32, hkv=8, ppu=0, sms=148, width=None):
+    qo = [0]
+    lens = []
+    for cached, new in steps:
+        qo.append(qo[-1] + new)
+        lens.append(cached + new)
+    width = width or max(-(-n // 16) for n in lens)
+    return mlb.plan_attention(qo, lens, width, h, hkv, "cpu", num_sms=sms, pages_per_unit=ppu), qo, lens
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("h,hkv,ppu", [(32, 8, 0), (32, 8, 3), (8, 2, 1), (8, 8, 0), (16, 2, 2), (12, 4, 5)])
+def test_planner_covers_every_page_once(mlb, seed, h, hkv, ppu):
+    r = random.Random(seed)
+    steps = [(r.randint(0, 3000), r.choice([1, 1, 1, r.randint(1, 40)])) for _ in range(r.randint(1, 20))]
+    p, qo, lens = plan(mlb, steps, h, hkv, ppu)
+    g = h // hkv
+    tpt = max(1, 8 // g)
+    assert p.tokens_per_tile == tpt
+    u = p.units_host
+    sizes = u[:, 3] - u[:, 2]
+    assert (np.diff(sizes) <= 0).all(), "largest units first"
+    # per (seq, tile) the units tile the pages the tile's last query can see, exactly once
+    cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
+    for seq, tile, pb, pe, prow, *_ in u.tolist():
+        cover.setdefault((seq, tile), []).append((pb, pe, prow))
+    for s, (cached, new) in enumerate(steps):
+        for t in range(-(-new // tpt)):
+            last = min((t + 1) * tpt, new) - 1
+            pages = -(-(cached + last + 1) // 16)
+            got = sorted(cover.pop((s, t)))
+            assert got[0][0] == 0 and got[-1][1] == pages
+            assert all(a[1] == b[0] for a, b in zip(got, got[1:]))
+            if len(got) == 1:
+                assert got[0][2] == -1
+            else:
+                rows = [x[2] for x in got]
+                assert rows == [rows[0] + c * tpt for c in range(len(got))]
+                for i in range(min(tpt, new - t * tpt)):
+                    tok = qo[s] + t * tpt + i
+                    assert p.reduce_chunks_host[tok] == len(got)
+    assert not cover
+
+
+def test_planner_rejects_a_table_that_cannot_hold_the_context(mlb):
+    with pytest.raises(ValueError, match="can't hold"):
+        plan(mlb, [(40, 1)], width=2)
+    with pytest.raises(ValueError, match="multiple"):
+        plan(mlb, [(4, 1)], h=6, hkv=4)
+
+
+def test_planner_auto_split_targets_waves_of_ctas(mlb):
+    # 64 decode rows, context U[512, 4096]: enough units for several waves on 148 SMs
+    r = random.Random(0)
+    steps = [(r.randint(512, 4096) - 1, 1) for _ in range(64)]
+    p, _, _ = plan(mlb, steps)
+    ctas = p.num_units * 8
+    assert 148 * 2 * 2 <= ctas <= 148 * 2 * 8
+    assert p.num_partial_rows > 0
