@@ -69,6 +69,8 @@ MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t
  * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads).
  * part_row < 0: the unit covers the whole context and writes `out` itself; otherwise it writes
  * normalised fp32 partial rows part_row + t (t = token within the tile) for the split-K reduction.
+ * q0 / num_new / seq_len repeat the sequence's qo_indptr[seq], new-token count and context length so
+ * a CTA starts from one 32-byte record.
  */
 typedef struct {
   int32_t seq;
@@ -76,7 +78,9 @@ typedef struct {
   int32_t page_begin;
   int32_t page_end;
   int32_t part_row;
-  int32_t reserved[3];
+  int32_t q0;
+  int32_t num_new;
+  int32_t seq_len;
 } mlb_work_unit;
 
 /*

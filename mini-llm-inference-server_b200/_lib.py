@@ -26,7 +26,7 @@ class WorkUnit(ctypes.Structure):
     """mlb_work_unit: one (sequence, query tile, page range) of paged-attention work."""
 
     _fields_ = [("seq", c_int32), ("q_tile", c_int32), ("page_begin", c_int32), ("page_end", c_int32),
-                ("part_row", c_int32), ("reserved", c_int32 * 3)]
+                ("part_row", c_int32), ("q0", c_int32), ("num_new", c_int32), ("seq_len", c_int32)]
 
 
 WORK_UNIT_INT32S = ctypes.sizeof(WorkUnit) // 4

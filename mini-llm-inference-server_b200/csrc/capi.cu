@@ -46,8 +46,8 @@ int elt_bytes(int dtype) { return dtype == MLB_F32 ? 4 : (dtype == MLB_F16 || dt
 bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
-constexpr int kCtasPerSm = 2;        // resident paged-attention CTAs per SM (shared memory bound)
-constexpr int kWaves = 4;            // CTA waves the auto split aims for (tail balance vs partial rows)
+constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
+constexpr int kWaveTenths = 15;      // the auto split aims for 1.5 waves of resident CTAs (measured best)
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
 
 int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
@@ -153,7 +153,7 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   const int tpt = tokens_per_tile(num_heads, num_kv_heads);
   int64_t chunk = pages_per_unit;
   if (chunk <= 0) {
-    const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaves;
+    const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaveTenths / 10;
     chunk = std::max<int64_t>(kMinPagesPerUnit, (total * num_kv_heads + target_ctas - 1) / target_ctas);
   }
   std::vector<mlb_work_unit> out;
@@ -173,6 +173,9 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
       u.page_begin = static_cast<int32_t>(c * per);
       u.page_end = static_cast<int32_t>(std::min<int64_t>((c + 1) * per, g.pages));
       u.part_row = nch > 1 ? static_cast<int32_t>(base + c * tpt) : -1;
+      u.q0 = qo_indptr[g.seq];
+      u.num_new = qo_indptr[g.seq + 1] - qo_indptr[g.seq];
+      u.seq_len = seq_lens[g.seq];
       if (u.page_end > u.page_begin || g.pages == 0) out.push_back(u);
     }
     if (reduce_rows && reduce_chunks) {

@@ -19,9 +19,18 @@
 
 namespace mlb {
 
+// Ring shape of the 16-bit kernel (head_dim 64 / 128): warps per CTA and slots per warp.  Two slots of
+// 8.5 KB per warp keep 3 CTAs resident per SM; these are the values measured best on B200.
+#ifndef MLB_ATTN_STAGES
+#define MLB_ATTN_STAGES 2
+#endif
+#ifndef MLB_ATTN_WARPS
+#define MLB_ATTN_WARPS 4
+#endif
+
 namespace {
 
-constexpr int kWarps = 4;
+constexpr int kWarps = 4;  // warps per CTA of the f32 kernel
 constexpr float kNegInf = -__builtin_huge_valf();
 
 struct UnitInfo {
@@ -29,12 +38,16 @@ struct UnitInfo {
 };
 
 __device__ __forceinline__ UnitInfo unit_info(const AttnArgs& a, int unit_idx) {
-  const mlb_work_unit u = a.units[unit_idx];
+  const int4* rec = reinterpret_cast<const int4*>(a.units + unit_idx);  // one 32-byte record, two loads
+  const int4 x = __ldg(rec), y = __ldg(rec + 1);
+  mlb_work_unit u;
+  u.seq = x.x, u.q_tile = x.y, u.page_begin = x.z, u.page_end = x.w;
+  u.part_row = y.x, u.q0 = y.y, u.num_new = y.z, u.seq_len = y.w;
   UnitInfo r;
   r.seq = u.seq;
-  r.q0 = a.qo[u.seq];
-  r.n_new = a.qo[u.seq + 1] - r.q0;
-  r.L = a.seq_lens[u.seq];
+  r.q0 = u.q0;
+  r.n_new = u.num_new;
+  r.L = u.seq_len;
   r.t0 = u.q_tile * a.tile_tokens;
   r.ncols = min(a.tile_tokens, r.n_new - r.t0) * a.group;
   r.pb = u.page_begin;
@@ -52,7 +65,7 @@ __device__ __forceinline__ int column_limit(const AttnArgs& a, const UnitInfo& u
 
 // Merge the warps' (m, l, O[col][dim]) states and write the unit's result: the final row when the unit
 // covers the whole context, else a normalised fp32 partial row plus its log2-sum-exp.
-template <int DH, int OUT_DT>
+template <int DH, int OUT_DT, int NW>
 __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInfo& ui, int kvh,
                                                 const float* const* so, const float* const* sm,
                                                 const float* const* sl) {
@@ -60,10 +73,10 @@ __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInf
     const int j = idx / DH, d = idx % DH;
     float M = kNegInf;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm[w][j]);
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, sm[w][j]);
     float lsum = 0.f, acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
+    for (int w = 0; w < NW; ++w) {
       const float mw = sm[w][j];
       const float e = mw == kNegInf ? 0.f : fast_exp2(mw - M);
       lsum += e * sl[w][j];
@@ -86,70 +99,72 @@ __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInf
 
 // ------------------------------------------------------------------ 16-bit pools: tensor-core tiles
 
-template <int DT, int DH, int STAGES>
-__global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_mma_kernel(AttnArgs a) {
-  using T = typename Elt<DT>::T;
+// NW warps per CTA, each streaming its pages through a private ring of STAGES shared-memory slots.
+template <int DT, int DH, int STAGES, int NW>
+__global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
   constexpr int ROWB = DH * 2 + 16;  // padded shared row: 8 consecutive rows hit 8 distinct 16B bank groups
   constexpr int TILE = 16 * ROWB;    // one page of one head, K or V
   constexpr int STAGE = 2 * TILE;
   constexpr int KSTEPS = DH / 16;
-  constexpr uint32_t PAGE_BYTES = 2u * 16u * DH * 2u;  // K + V rows of one head of one page
+  constexpr int CH_ROW = DH * 2 / 16;         // 16-byte chunks per row
+  constexpr int CH_LANE = 2 * 16 * CH_ROW / 32;  // chunks each lane copies per page (K and V)
   static_assert(8 * DH * 4 + 64 <= STAGES * STAGE, "merge state must fit in a warp's ring");
+  static_assert(32 % CH_ROW == 0 || CH_ROW % 32 == 0, "row chunks must tile a warp");
 
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t bars[kWarps][STAGES];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x % a.hkv;
   const UnitInfo ui = unit_info(a, blockIdx.x / a.hkv);
   uint8_t* ring = smem + warp * STAGES * STAGE;
 
-  if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[warp][s], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-
   const int pb = ui.pb + warp;
-  const int npages = pb < ui.pe ? (ui.pe - pb + kWarps - 1) / kWarps : 0;
+  const int npages = pb < ui.pe ? (ui.pe - pb + NW - 1) / NW : 0;
   const int32_t* table = a.bt + static_cast<int64_t>(ui.seq) * a.bt_stride;
 
   // Block ids of this warp's pages, 32 at a time (lane i holds page i of the window); the next window
   // is loaded one window ahead so its latency hides behind the current one.
   auto load_window = [&](int w) -> int {
     const int i = w * 32 + lane;
-    return i < npages ? __ldg(table + pb + i * kWarps) : 0;
+    return i < npages ? __ldg(table + pb + i * NW) : 0;
   };
   int ids_cur = load_window(0), ids_nxt = load_window(1), win = 0;
   uint32_t bad_mask = 0;  // bit s: the page in slot s had a block id outside the pool
 
+  // Copy page j (this warp's j-th) into slot j % STAGES with 16-byte cp.async: chunk e = c * 32 + lane of
+  // the page's 2 x 16 rows, consecutive lanes on consecutive chunks of a row (coalesced).  Every call
+  // commits one group (possibly empty) so the group count stays in step with the page count.
+  const int64_t row_stride = static_cast<int64_t>(a.hkv) * DH * 2;  // bytes between tokens of one head
   auto issue = [&](int j) {
-    if ((j >> 5) != win) {
-      ++win;
-      ids_cur = ids_nxt;
-      ids_nxt = load_window(win + 1);
+    if (j < npages) {
+      if ((j >> 5) != win) {
+        ++win;
+        ids_cur = ids_nxt;
+        ids_nxt = load_window(win + 1);
+      }
+      const int bid = __shfl_sync(0xffffffffu, ids_cur, j & 31);
+      const int s = j % STAGES;
+      const bool ok = bid >= 0 && bid < a.num_blocks;
+      bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
+      if (!ok) {
+        if (lane == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+      } else {
+        const int64_t page_off = (static_cast<int64_t>(bid) * kBlockSize * a.hkv + kvh) * (DH * 2);
+        uint8_t* slot = ring + s * STAGE;
+#pragma unroll
+        for (int c = 0; c < CH_LANE; ++c) {
+          const int e = c * 32 + lane;
+          const int kv = e / (16 * CH_ROW), row = (e / CH_ROW) % 16, ch = e % CH_ROW;
+          const char* src = (kv ? a.v_cache : a.k_cache) + page_off + row * row_stride + ch * 16;
+          cp_async16(slot + kv * TILE + row * ROWB + ch * 16, src);
+        }
+      }
     }
-    const int bid = __shfl_sync(0xffffffffu, ids_cur, j & 31);
-    const int s = j % STAGES;
-    uint64_t* bar = &bars[warp][s];
-    const bool ok = bid >= 0 && bid < a.num_blocks;
-    bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
-    if (lane == 0) {
-      if (!ok) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-      mbar_arrive_expect_tx(bar, ok ? PAGE_BYTES : 0u);
-    }
-    __syncwarp();
-    if (ok) {
-      const int row = lane & 15;
-      const bool isv = lane >= 16;
-      const char* src = (isv ? a.v_cache : a.k_cache) +
-                        ((static_cast<int64_t>(bid) * kBlockSize + row) * a.hkv + kvh) * (DH * 2);
-      bulk_g2s(ring + s * STAGE + (isv ? TILE : 0) + row * ROWB, src, DH * 2, bar);
-    }
+    cp_async_commit();
   };
 
-  for (int j = 0; j < STAGES && j < npages; ++j) issue(j);
+#pragma unroll
+  for (int j = 0; j < STAGES - 1; ++j) issue(j);
 
   // Q^T as B fragments (column n = lane / 4, dims 2 * (lane % 4) + {0, 1} (+8)), loaded once.
   uint32_t qb[KSTEPS][2];
@@ -185,29 +200,21 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_mma_kernel(AttnArgs
   const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
   const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
 
-  bool timed_out = false;
   for (int i = 0; i < npages; ++i) {
+    issue(i + STAGES - 1);           // refill the slot page i - 1 used
+    cp_async_wait<STAGES - 1>();     // this lane's copies of page i have landed
+    __syncwarp();                    // ... and every other lane's
     const int s = i % STAGES;
-    const uint32_t parity = (i / STAGES) & 1;
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&bars[warp][s], parity, a.wait_ns))) {
-      // A copy that never lands: record it, drain the other slots in flight (bounded) and stop.
-      if (lane == 0) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
-      for (int k = i + 1; k < npages && k < i + STAGES; ++k)
-        mbar_wait_bounded(&bars[warp][k % STAGES], (k / STAGES) & 1, a.wait_ns);
-      timed_out = true;
-      break;
-    }
     if (!((bad_mask >> s) & 1u)) {
-      const int tok_base = (pb + i * kWarps) * kBlockSize;
+      const int tok_base = (pb + i * NW) * kBlockSize;
       uint8_t* vt = ring + s * STAGE + TILE;
       const int live_rows = ui.L - tok_base;
       if (live_rows < 16) {
         // Rows past the context end hold another request's data or junk; P is 0 there, but 0 * NaN
         // would still poison O, so clear those V rows.
         const int r_begin = live_rows < 0 ? 0 : live_rows;
-        constexpr int VEC_PER_ROW = DH * 2 / 16;
-        for (int e = lane; e < (16 - r_begin) * VEC_PER_ROW; e += 32) {
-          const int r = r_begin + e / VEC_PER_ROW, c = e % VEC_PER_ROW;
+        for (int e = lane; e < (16 - r_begin) * CH_ROW; e += 32) {
+          const int r = r_begin + e / CH_ROW, c = e % CH_ROW;
           *reinterpret_cast<uint4*>(vt + r * ROWB + c * 16) = make_uint4(0u, 0u, 0u, 0u);
         }
         __syncwarp();
@@ -262,21 +269,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_mma_kernel(AttnArgs
         mma16816<DT>(o[mt], y0, y1, y2, y3, pb0, pb1);
       }
     }
-    __syncwarp();
-    if (i + STAGES < npages) {
-      fence_proxy_async();  // order this slot's generic reads/writes before the next async-proxy fill
-      issue(i + STAGES);
-    }
+    __syncwarp();  // every lane is done with slot s before the next iteration refills it
   }
+  cp_async_wait<0>();
 
 #pragma unroll
   for (int off = 4; off < 32; off <<= 1) {
     l0 += __shfl_xor_sync(0xffffffffu, l0, off);
     l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-  }
-  if (timed_out) {
-    m0 = m1 = kNegInf;
-    l0 = l1 = 0.f;
   }
   // Stash this warp's state in its own ring: every copy into it has landed and been consumed.
   __syncwarp();
@@ -298,16 +298,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2) paged_attn_mma_kernel(AttnArgs
     sl[j1] = l1;
   }
   __syncthreads();
-  const float* so_w[kWarps];
-  const float* sm_w[kWarps];
-  const float* sl_w[kWarps];
+  const float* so_w[NW];
+  const float* sm_w[NW];
+  const float* sl_w[NW];
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
+  for (int w = 0; w < NW; ++w) {
     so_w[w] = reinterpret_cast<const float*>(smem + w * STAGES * STAGE);
     sm_w[w] = so_w[w] + 8 * DH;
     sl_w[w] = sm_w[w] + 8;
   }
-  merge_and_store<DH, DT>(a, ui, kvh, so_w, sm_w, sl_w);
+  merge_and_store<DH, DT, NW>(a, ui, kvh, so_w, sm_w, sl_w);
 }
 
 // ------------------------------------------------------------------ f32 pools: CUDA cores
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a)
     sm_w[w] = so_w[w] + 8 * DH;
     sl_w[w] = sm_w[w] + 8;
   }
-  merge_and_store<DH, MLB_F32>(a, ui, kvh, so_w, sm_w, sl_w);
+  merge_and_store<DH, MLB_F32, kWarps>(a, ui, kvh, so_w, sm_w, sl_w);
 }
 
 // ------------------------------------------------------------------ split-K reduction
@@ -492,14 +492,14 @@ cudaError_t set_smem(K kernel, int bytes, unsigned long long& done) {
   return e;
 }
 
-template <int DT, int DH, int STAGES>
+template <int DT, int DH, int STAGES, int NW>
 cudaError_t launch_mma(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
-  constexpr int bytes = kWarps * STAGES * 2 * 16 * (DH * 2 + 16);
+  constexpr int bytes = NW * STAGES * 2 * 16 * (DH * 2 + 16);
   static unsigned long long done = 0;
-  auto k = paged_attn_mma_kernel<DT, DH, STAGES>;
+  auto k = paged_attn_mma_kernel<DT, DH, STAGES, NW>;
   cudaError_t e = set_smem(k, bytes, done);
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(ctas), kWarps * 32, bytes, s>>>(a);
+  k<<<static_cast<unsigned>(ctas), NW * 32, bytes, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -519,13 +519,13 @@ cudaError_t launch_f32(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
   const int64_t ctas = num_units * a.hkv;
   if (dtype == MLB_BF16) {
-    if (dh == 64) return launch_mma<MLB_BF16, 64, 4>(a, ctas, s);
-    if (dh == 128) return launch_mma<MLB_BF16, 128, 3>(a, ctas, s);
-    if (dh == 256) return launch_mma<MLB_BF16, 256, 2>(a, ctas, s);
+    if (dh == 64) return launch_mma<MLB_BF16, 64, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);
+    if (dh == 128) return launch_mma<MLB_BF16, 128, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);
+    if (dh == 256) return launch_mma<MLB_BF16, 256, 2, 4>(a, ctas, s);
   } else if (dtype == MLB_F16) {
-    if (dh == 64) return launch_mma<MLB_F16, 64, 4>(a, ctas, s);
-    if (dh == 128) return launch_mma<MLB_F16, 128, 3>(a, ctas, s);
-    if (dh == 256) return launch_mma<MLB_F16, 256, 2>(a, ctas, s);
+    if (dh == 64) return launch_mma<MLB_F16, 64, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);
+    if (dh == 128) return launch_mma<MLB_F16, 128, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);
+    if (dh == 256) return launch_mma<MLB_F16, 256, 2, 4>(a, ctas, s);
   } else if (dtype == MLB_F32) {
     if (dh == 64) return launch_f32<64>(a, ctas, s);
     if (dh == 128) return launch_f32<128>(a, ctas, s);

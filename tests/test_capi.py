@@ -124,5 +124,5 @@ def test_planner_auto_split_targets_waves_of_ctas(mlb):
     steps = [(r.randint(512, 4096) - 1, 1) for _ in range(64)]
     p, _, _ = plan(mlb, steps)
     ctas = p.num_units * 8
-    assert 148 * 2 * 2 <= ctas <= 148 * 2 * 8
+    assert 148 * 3 <= ctas <= 148 * 3 * 4
     assert p.num_partial_rows > 0

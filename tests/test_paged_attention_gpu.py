@@ -67,11 +67,15 @@ def test_nan_junk_past_the_context_does_not_leak(mlb, cuda, dtype):
     for (cached, _), blocks in zip(case.steps, case.blocks):
         for p in range(cached):
             used[blocks[p // 16] * 16 + p % 16] = True
+    # The reference's batched decode gathers every row to the longest context and lets SDPA weight the
+    # masked tail by 0, and 0 * NaN = NaN: with non-finite junk it returns NaN for the shorter rows.  The
+    # kernels read only each sequence's own tokens, so the answer is the oracle's on zeroed junk.
+    expected = oracle_forward(case, dtype)[0]
     for pool in (case.k_pool, case.v_pool):
         pool.view(-1, case.hkv, case.dh)[~used] = float("nan")
     out, _, _ = run_backend(mlb, case, dtype, cuda, ppu=1)
     assert torch.isfinite(out).all()
-    assert_close(out, oracle_forward(case, dtype)[0], dtype)
+    assert_close(out, expected, dtype)
 
 
 def test_out_of_range_block_ids_are_flagged_not_read(mlb, cuda):
