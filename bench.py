@@ -367,7 +367,7 @@ def run_ours(args) -> None:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "traffic": profiled_traffic(), "algorithmic_bytes": bytes_rank_layer,
-                         "kernel": "paged_attn_mma_kernel<bf16,128,3>"},
+                         "kernel": "paged_attn_mma_kernel<bf16, Dh 128, 2 slots, 4 warps>"},
             "gpu_launches": launches_per_layer * layers * args.steps,
             "clocks": clocks.summary(),
         }
