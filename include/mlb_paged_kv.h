@@ -145,6 +145,29 @@ MLB_API int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, 
 MLB_API int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
                    const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err_word, void* stream);
 
+/*
+ * Paged attention that allocates nothing.  No counterpart in the reference: it is this library's answer to
+ * callers that cannot allocate device memory when they attend, e.g. an engine that gave nearly all free
+ * device memory to the KV pool at start-up (as the reference sizes its pool, engine/process.py:91-115), or a
+ * non-PyTorch serving loop with no device allocator and no room for cudaMalloc's implicit synchronisation.
+ * Same arguments and results as mlb_paged_attention followed by mlb_splitk_reduce (out gets q's dtype),
+ * with the split-K partial rows kept in a static device array of MLB_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading the library holds until exit.  Plans whose partial rows need more than that (rows x num_heads x
+ * (head_dim + 1) x 4 bytes, each part 256-byte aligned) return MLB_ENOSPACE.  All calls share the array and
+ * it keeps the last call's contents; calls that overlap on the GPU race.  The first call on a device looks
+ * up the array's device address (cudaGetSymbolAddress) with that device current: make it before any stream
+ * capture.  reduce_rows / reduce_chunks / num_tokens are the plan's (mlb_plan_attention).
+ */
+#define MLB_NOALLOC_SCRATCH_BYTES (8u << 20)
+MLB_API int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache, int dtype, int64_t num_blocks, int block_size,
+                        int num_heads, int num_kv_heads, int head_dim, float scale,
+                        const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
+                        const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
+                        int64_t num_partial_rows, const int32_t* reduce_rows, const int32_t* reduce_chunks,
+                        int64_t num_tokens, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        int32_t* err_word, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

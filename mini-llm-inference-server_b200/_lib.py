@@ -19,7 +19,8 @@ MLB_OK, MLB_EINVAL, MLB_EUNSUPPORTED, MLB_ECUDA, MLB_ENOSPACE = 0, 1, 2, 3, 4
 DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
 
 EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_plan_capacity",
-           "mlb_paged_attention", "mlb_splitk_reduce", "mlb_block_copy")
+           "mlb_paged_attention", "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc")
+NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 
 
 class WorkUnit(ctypes.Structure):
@@ -48,6 +49,10 @@ _SIGNATURES = {
                                   c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                                c_void_p]),
+    "mlb_paged_attention_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
+                                            c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p,
+                                            c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                                            c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

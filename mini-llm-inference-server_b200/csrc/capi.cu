@@ -87,6 +87,10 @@ int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_bl
 
 }  // namespace
 
+namespace mlb {
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace mlb
+
 extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
