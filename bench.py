@@ -288,25 +288,42 @@ def run_ours(args) -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # --- device-resident timing (value) with per-launch events around the attention kernel
+    # --- warm-up (eager): NCCL communicators, kernel attributes, the workspace
     for _ in range(args.warmup):
         for l in range(layers):
             layer_step(l)
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
-           for _ in range(args.steps)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
+
+    # --- value: the whole step (every layer's append, attention, reduction [, all-gather]) as one CUDA
+    # graph, replayed; device time between events, max over ranks.  A decode step is what serving engines
+    # capture in a graph, and it keeps the device time from hiding behind Python launch overhead.
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph):
+        for l in range(layers):
+            layer_step(l)
+    step_graph.replay()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         start.record()
-        for s in range(args.steps):
-            for l in range(layers):
-                layer_step(l, evs[s][l])
+        for _ in range(args.steps):
+            step_graph.replay()
         end.record()
         barrier()
     elapsed_ms = max_over_ranks(start.elapsed_time(end), world, dev)
+    ms_per_step = elapsed_ms / args.steps
+
+    # --- roofline of the dominant kernel: every attention launch of eager steps bracketed by events on
+    # the launching stream
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
+           for _ in range(args.kernel_steps)]
+    barrier()
+    for s in range(args.kernel_steps):
+        for l in range(layers):
+            layer_step(l, evs[s][l])
+    barrier()
     attn_ms = [e0.elapsed_time(e1) for step in evs for (e0, e1) in step]
     attn_avg_ms = max_over_ranks(statistics.mean(attn_ms), world, dev)
-    ms_per_step = elapsed_ms / args.steps
 
     bytes_rank_layer = kv_bytes(ctx, hkv_l)
     bytes_step_total = bytes_rank_layer * layers * world
@@ -332,9 +349,15 @@ def run_ours(args) -> None:
         graph.replay()
     ap_e.record()
     barrier()
-    del graph
+    del graph, step_graph  # graphs holding NCCL work go before the process group
     append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
     append_bytes = 2 * 2 * args.batch * hkv_l * DH * 2  # K and V rows read + written, bf16
+
+    # --- optional GPU comparison: FlashInfer's paged decode on the same pools, called as the reference's
+    # FlashInfer backend calls it (attention/flashinfer_backend.py:48-58: NHD, plan once, run per layer)
+    flashinfer = None
+    if args.flashinfer and world == 1:
+        flashinfer = run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, args.kernel_steps, dev)
 
     # --- end to end through the public API with host buffers (metadata build + H2D in, D2H out)
     e2e = None
@@ -369,10 +392,13 @@ def run_ours(args) -> None:
                          "traffic": profiled_traffic(), "algorithmic_bytes": bytes_rank_layer,
                          "kernel": "paged_attn_mma_kernel<bf16, Dh 128, 2 slots, 4 warps>"},
             "gpu_launches": launches_per_layer * layers * args.steps,
+            "timing": "value: CUDA-graph replays of the 32-layer step; roofline: event-timed eager attention launches",
             "clocks": clocks.summary(),
         }
         if e2e:
             line["e2e"] = e2e
+        if flashinfer:
+            line["flashinfer_decode"] = flashinfer
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -424,6 +450,33 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
             "path": ("KVHeadShardedBackend" if world > 1 else "B200Backend") + ".forward per layer, pinned host I/O"}
 
 
+def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:
+    """FlashInfer BatchDecodeWithPagedKVCacheWrapper on the same pages (the reference's CUDA backend)."""
+    try:
+        import flashinfer
+    except ImportError as e:
+        return {"unavailable": f"flashinfer not importable: {e}"}
+    ws = torch.empty(128 * 2**20, dtype=torch.uint8, device=dev)
+    w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout="NHD")
+    w.plan(meta.kv_indptr, meta.kv_indices, meta.kv_last_page_len, H, HKV, DH, BS, pos_encoding_mode="NONE",
+           q_data_type=q.dtype, kv_data_type=k_pools[0].dtype)
+    out = w.run(q, (k_pools[0], v_pools[0]))
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        for l in range(layers):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            w.run(q, (k_pools[l], v_pools[l]), out=out)
+            e1.record()
+            evs.append((e0, e1))
+    torch.cuda.synchronize()
+    us = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
+    nbytes = kv_bytes(ctx, HKV)
+    return {"attention_us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "version": flashinfer.__version__,
+            "call": "BatchDecodeWithPagedKVCacheWrapper(NHD).plan(kv_indptr, kv_indices, kv_last_page_len, ...).run"}
+
+
 def _meta_bytes(mlb, seqs) -> int:
     m = mlb.AttentionMetadata.build(seqs, BS, "cpu")
     return sum(t.numel() * t.element_size() for t in (m.positions, m.slot_mapping, m.block_tables, m.logits_index,
@@ -438,10 +491,12 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--kernel-steps", type=int, default=10, help="eager steps whose attention launches are timed")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--cpu-reps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours" and args.layers == 32:
