@@ -1,7 +1,11 @@
 """Benchmark of the paged KV hot path on B200: BASELINE config 2 (Llama-3.1-8B decode-attention shape).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
     torchrun --nproc-per-node N bench.py --gpus N ...      (KV-head sharding, NCCL all-gather)
+
+The default (config 2) is the headline line.  --config 3/4/5 print the same kind of line for BASELINE's
+mixed continuous-batching step, prefix-sharing step (copy-on-write) and long-context eviction step
+(compaction), each described in its builder below.
 
 Workload (config 2): bf16, 32 query heads, 8 KV heads, head_dim 128, block_size 16, batch 64, context
 lengths U[512, 4096] (seeded), block tables a seeded shuffle of a pool sized 1.25x the blocks needed,
@@ -31,6 +35,8 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
+from dataclasses import dataclass, field
+
 import numpy as np
 import torch
 
@@ -43,16 +49,123 @@ FALLBACK_HBM_GBS = 6650.0
 # ----------------------------------------------------------------------------- workload
 
 
-def config2(batch: int, seed: int = 1234):
-    """Seeded config-2 step: contexts (after the append), block tables, pool size."""
+@dataclass
+class Workload:
+    """One benchmark step: rows whose k/v are appended, rows that attend, and block copies run first."""
+
+    name: str
+    describe: str
+    append_rows: list  # (num_cached, num_new, block_ids)
+    attend_rows: list  # (num_cached, num_new, block_ids); decode rows
+    num_blocks: int
+    copy_src: list = field(default_factory=list)
+    copy_dst: list = field(default_factory=list)
+    kv_scale: float = 1.0
+    layers: int = 32
+    info: dict = field(default_factory=dict)
+
+    @property
+    def attend_ctx(self) -> np.ndarray:
+        return np.array([c + n for c, n, _ in self.attend_rows], dtype=np.int64)
+
+    def unique_pages(self) -> int:
+        """Distinct pool blocks the attention reads (shared prefixes count once)."""
+        return len({b for c, n, blk in self.attend_rows for b in blk[:-(-(c + n) // BS)]})
+
+
+def _take(perm: np.ndarray, counts) -> list[list[int]]:
+    offs = np.concatenate([[0], np.cumsum(counts)])
+    return [perm[offs[i]:offs[i + 1]].tolist() for i in range(len(counts))]
+
+
+def config2(batch: int = 64, seed: int = 1234) -> Workload:
+    """batch 64, context U[512, 4096] after the append, pool 1.25x the blocks needed,
+    tables a seeded shuffle, K/V 0.5 N(0,1); one decode token per sequence, 32 layer pools."""
     r = np.random.default_rng(seed)
     ctx = r.integers(512, 4097, size=batch).astype(np.int64)
     pages = -(-ctx // BS)
     nb = int(math.ceil(1.25 * int(pages.sum())))
+    blocks = _take(r.permutation(nb), pages)
+    rows = [(int(c) - 1, 1, b) for c, b in zip(ctx, blocks)]
+    return Workload("config 2", "Llama-3.1-8B decode attention (H32/Hkv8/Dh128, bs16), batch 64, ctx U[512,4096], "
+                    "32 layer pools, append 1 token/seq + paged attention", rows, rows, nb, kv_scale=0.5)
+
+
+def config3(seed: int = 33) -> Workload:
+    """256 decode rows with context lognormal(median 1024, sigma 1) capped at 32768, and a
+    varlen append of 8 prefill chunks of U[1, 2048] tokens.  Blocks come from a seeded random permutation of a
+    pool 1.25x the need, so every table is scattered (a fragmented pool).  The chunks only append here; their
+    attention is a prefill kernel's job."""
+    r = np.random.default_rng(seed)
+    ctx = np.clip(np.rint(1024.0 * np.exp(r.standard_normal(256))), 1, 32768).astype(np.int64)
+    chunks = r.integers(1, 2049, size=8).astype(np.int64)
+    pages, cpages = -(-ctx // BS), -(-chunks // BS)
+    nb = int(math.ceil(1.25 * int(pages.sum() + cpages.sum())))
     perm = r.permutation(nb)
-    offs = np.concatenate([[0], np.cumsum(pages)])
-    blocks = [perm[offs[i]:offs[i + 1]].tolist() for i in range(batch)]
-    return ctx, blocks, nb
+    blocks = _take(perm, np.concatenate([pages, cpages]))
+    decode = [(int(c) - 1, 1, b) for c, b in zip(ctx, blocks[:256])]
+    prefill = [(0, int(n), b) for n, b in zip(chunks, blocks[256:])]
+    return Workload("config 3", "mixed step: 256 decode rows ctx lognormal(1024, 1.0) <= 32768 + varlen append of "
+                    "8 prefill chunks U[1,2048], fragmented pool, 32 layer pools", decode + prefill, decode, nb,
+                    info={"chunk_tokens": int(chunks.sum()), "decode_ctx_sum": int(ctx.sum())})
+
+
+CONFIG4_PREFIX = 8200  # 512 full blocks + 8 tokens: the shared prefix ends mid-block, so its last block is COW'd
+
+
+def config4(seed: int = 44) -> Workload:
+    """128 sequences share one prefix (identical block ids, refcount 128) and each has a
+    unique suffix of U[64, 512] tokens.  8192 tokens would fill the shared blocks exactly, so the prefix here
+    is 8200 tokens: its last block holds 8 tokens, and every step first copies that shared partial block into
+    each sequence's private block (copy-on-write: 128 copies) before appending one token per sequence and
+    attending over shared + private blocks."""
+    r = np.random.default_rng(seed)
+    b = 128
+    suffix = r.integers(64, 513, size=b).astype(np.int64)
+    ctx = CONFIG4_PREFIX + suffix  # context after the append
+    full = CONFIG4_PREFIX // BS
+    private = -(-ctx // BS) - full  # the first private block is the COW copy of the shared partial block
+    nb = full + 1 + int(private.sum())
+    perm = r.permutation(nb)
+    shared, partial = perm[:full].tolist(), int(perm[full])
+    own = _take(perm[full + 1:], private)
+    rows = [(int(c) - 1, 1, shared + o) for c, o in zip(ctx, own)]
+    return Workload("config 4", "prefix sharing: 128 seqs share an 8200-token prefix (refcount 128; its partial last "
+                    "block is COW-copied to each seq every step) + suffix U[64,512]; append 1 token/seq + attention, "
+                    "32 layer pools", rows, rows, nb, copy_src=[partial] * b, copy_dst=[o[0] for o in own],
+                    info={"prefix_tokens": CONFIG4_PREFIX})
+
+
+def config5(seed: int = 55) -> Workload:
+    """32 sequences of 131072 tokens in a pool with 64 spare blocks.  Each step evicts a
+    seeded 10% (3 sequences), compacts the pool by copying every live block above the live count into the
+    freed blocks below it (BlockManager.compact, one block-copy launch), then runs split-K decode for the 29
+    survivors over their rewritten tables.  One layer (its K+V pool is 17 GB at one GPU)."""
+    r = np.random.default_rng(seed)
+    b, ctx = 32, 131072
+    pages = ctx // BS
+    nb = b * pages + 64
+    tables = _take(r.permutation(nb), [pages] * b)
+    evict = set(r.choice(b, size=3, replace=False).tolist())
+    live = [t for i, t in enumerate(tables) if i not in evict]
+    # compaction plan, as the block manager makes it: live blocks at ids >= n_live move to the free ids below
+    n_live = len(live) * pages
+    used = np.zeros(nb, dtype=bool)
+    for t in live:
+        used[t] = True
+    holes = np.nonzero(~used[:n_live])[0]
+    movers = np.nonzero(used[n_live:])[0] + n_live
+    remap = np.arange(nb)
+    remap[movers] = holes
+    live = [remap[t].tolist() for t in live]
+    rows = [(ctx - 1, 1, t) for t in live]
+    return Workload("config 5", "long context: 32 x 131072 tokens, evict 3 (10%), compact by block copy into the "
+                    "freed blocks, split-K decode of the 29 survivors; 1 layer", rows, rows, nb,
+                    copy_src=movers.tolist(), copy_dst=holes.tolist(), layers=1,
+                    info={"evicted": sorted(evict), "moved_blocks": int(len(movers))})
+
+
+WORKLOADS = {2: config2, 3: config3, 4: config4, 5: config5}
 
 
 def kv_bytes(ctx, hkv: int, elt: int = 2) -> int:
@@ -153,34 +266,37 @@ def max_over_ranks(x: float, world: int, device) -> float:
 # ----------------------------------------------------------------------------- CPU reference leg
 
 
-def cpu_reference_step(ctx, blocks, nb_sample_seqs: int, seed: int = 7):
+def cpu_reference_step(wl: Workload, nb_sample_seqs: int, seed: int = 7):
     """Build the oracle's inputs for a bounded sample of the config-2 step (first `nb_sample_seqs`
     sequences, one layer, pool holding just their blocks) and return a callable that runs one step."""
     sys.path.insert(0, str(REPO))
     import oracle  # the reference's CPU algorithm (paged_torch_ref.py restated): the baseline, not the product
 
     sel = list(range(nb_sample_seqs))
-    sctx = [int(ctx[i]) for i in sel]
+    sctx = [int(wl.attend_ctx[i]) for i in sel]
     sblocks, nxt = [], 0
     for i in sel:  # renumber the sample's blocks densely: a small pool, same access pattern per sequence
-        sblocks.append(list(range(nxt, nxt + len(blocks[i]))))
-        nxt += len(blocks[i])
+        n = len(wl.attend_rows[i][2])
+        sblocks.append(list(range(nxt, nxt + n)))
+        nxt += n
     g = torch.Generator().manual_seed(seed)
-    k_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
-    v_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    sc = wl.kv_scale
+    k_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * sc).to(torch.bfloat16)
+    v_pool = (torch.randn(nxt, BS, HKV, DH, generator=g) * sc).to(torch.bfloat16)
     q = torch.randn(len(sel), H, DH, generator=g).to(torch.bfloat16)
-    k = (torch.randn(len(sel), HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
-    v = (torch.randn(len(sel), HKV, DH, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(len(sel), HKV, DH, generator=g) * sc).to(torch.bfloat16)
+    v = (torch.randn(len(sel), HKV, DH, generator=g) * sc).to(torch.bfloat16)
     meta = oracle.build_metadata([(c - 1, 1, b) for c, b in zip(sctx, sblocks)], BS)
 
     def step():
         oracle.forward(q, k, v, k_pool, v_pool, meta, compute_dtype=None)  # the reference's own dtype: bf16
 
-    return step, kv_bytes(sctx, HKV), f"{len(sel)} of 64 sequences (sum ctx {sum(sctx)}), 1 layer, bf16"
+    return step, kv_bytes(sctx, HKV), (f"{len(sel)} of {len(wl.attend_rows)} sequences (sum ctx {sum(sctx)}), "
+                                       "1 layer, bf16")
 
 
-def run_cpu_baseline(ctx, blocks, seqs: int, reps: int, warmup: int = 1) -> dict:
-    step, nbytes, sample = cpu_reference_step(ctx, blocks, seqs)
+def run_cpu_baseline(wl: Workload, seqs: int, reps: int, warmup: int = 1) -> dict:
+    step, nbytes, sample = cpu_reference_step(wl, seqs)
     for _ in range(warmup):
         step()
     t0 = time.perf_counter()
@@ -196,8 +312,7 @@ def run_reference_arm(args) -> None:
     if rank != 0:
         return  # the CPU arm runs once, on rank 0 only
     torch.set_num_threads(os.cpu_count() or 1)
-    ctx, blocks, _ = config2(args.batch)
-    step, nbytes, sample = cpu_reference_step(ctx, blocks, args.cpu_sample_seqs)
+    step, nbytes, sample = cpu_reference_step(config2(args.batch), args.cpu_sample_seqs)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -238,40 +353,49 @@ def run_ours(args) -> None:
     sharding = importlib.import_module(PACKAGE + ".sharding")
     ops = mlb.ops
 
+    wl = config2(args.batch) if args.config == 2 else WORKLOADS[args.config]()
+    layers = args.layers or wl.layers
     hkv_l, h_l = HKV // world, H // world
-    ctx, blocks, nb = config2(args.batch)
-    seqs = [mlb.SeqStep(int(c) - 1, 1, b) for c, b in zip(ctx, blocks)]
-    layers = args.layers
+    n_app, n_att = sum(n for _, n, _ in wl.append_rows), len(wl.attend_rows)
+    nb = wl.num_blocks
 
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     k_pools, v_pools = [], []
     for _ in range(layers):
         for pools in (k_pools, v_pools):
             p = torch.empty(nb, BS, hkv_l, DH, device=dev, dtype=torch.bfloat16)
-            p.normal_(0.0, 0.5, generator=g)
+            p.normal_(0.0, wl.kv_scale, generator=g)
             pools.append(p)
     gq = torch.Generator(device=dev).manual_seed(7)  # the same full q/k/v on every rank
-    q = torch.randn(args.batch, H, DH, device=dev, generator=gq).to(torch.bfloat16)
-    k = (torch.randn(args.batch, HKV, DH, device=dev, generator=gq) * 0.5).to(torch.bfloat16)
-    v = (torch.randn(args.batch, HKV, DH, device=dev, generator=gq) * 0.5).to(torch.bfloat16)
-    qs = sharding.head_range(rank, world, H)
-    ks = sharding.head_range(rank, world, HKV)
+    q = torch.randn(n_att, H, DH, device=dev, generator=gq).to(torch.bfloat16)
+    k = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
+    v = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
+    qs, ks = sharding.head_range(rank, world, H), sharding.head_range(rank, world, HKV)
     q_l, k_l, v_l = q[:, qs], k[:, ks], v[:, ks]
 
-    meta = mlb.AttentionMetadata.build(seqs, BS, dev)
-    backend = mlb.B200Backend()
-    plan = backend.plan(meta, h_l, hkv_l, dev)
+    def seqsteps(rows):
+        return [mlb.SeqStep(c, n, b) for c, n, b in rows]
+
+    meta_att = mlb.AttentionMetadata.build(seqsteps(wl.attend_rows), BS, dev)
+    meta_app = meta_att if wl.append_rows is wl.attend_rows else mlb.AttentionMetadata.build(
+        seqsteps(wl.append_rows), BS, dev)
+    plan = mlb.B200Backend().plan(meta_att, h_l, hkv_l, dev)
     ws = ops.Workspace()
-    out_l = torch.empty(args.batch, h_l, DH, device=dev, dtype=torch.bfloat16)
-    gathered = torch.empty(world * args.batch, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 else None
+    out_l = torch.empty(n_att, h_l, DH, device=dev, dtype=torch.bfloat16)
+    gathered = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 else None
+    copies = len(wl.copy_src)
+    if copies:
+        ptrs = ops.pool_pointer_table(k_pools + v_pools)
+        src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
+        dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
     launches_per_layer = 2 + (1 if plan.num_partial_rows else 0)
 
     def layer_step(l, ev=None):
-        ops.kv_append(k_pools[l], v_pools[l], meta.slot_mapping, k_l, v_l)
+        ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
         if ev is not None:
             ev[0].record()
-        ops.attention_partials(q_l, k_pools[l], v_pools[l], meta.block_tables_i32, meta.seq_lens_i32,
-                               meta.qo_indptr, plan, ws, out_l)
+        ops.attention_partials(q_l, k_pools[l], v_pools[l], meta_att.block_tables_i32, meta_att.seq_lens_i32,
+                               meta_att.qo_indptr, plan, ws, out_l)
         if ev is not None:
             ev[1].record()
         ops.splitk_reduce(plan, ws, out_l)
@@ -279,6 +403,12 @@ def run_ours(args) -> None:
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(gathered, out_l)
+
+    def full_step():
+        if copies:  # COW / compaction: one launch over every layer's K and V pools
+            ops.block_copy(ptrs, k_pools[0], src, dst)
+        for l in range(layers):
+            layer_step(l)
 
     def barrier():
         torch.cuda.synchronize()
@@ -290,17 +420,15 @@ def run_ours(args) -> None:
 
     # --- warm-up (eager): NCCL communicators, kernel attributes, the workspace
     for _ in range(args.warmup):
-        for l in range(layers):
-            layer_step(l)
+        full_step()
     barrier()
 
-    # --- value: the whole step (every layer's append, attention, reduction [, all-gather]) as one CUDA
-    # graph, replayed; device time between events, max over ranks.  A decode step is what serving engines
-    # capture in a graph, and it keeps the device time from hiding behind Python launch overhead.
+    # --- value: the whole step (block copies, then every layer's append, attention, reduction [, all-gather])
+    # as one CUDA graph, replayed; device time between events, max over ranks.  A decode step is what
+    # serving engines capture in a graph, and it keeps the device time from hiding behind Python launches.
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph):
-        for l in range(layers):
-            layer_step(l)
+        full_step()
     step_graph.replay()
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -310,11 +438,10 @@ def run_ours(args) -> None:
             step_graph.replay()
         end.record()
         barrier()
-    elapsed_ms = max_over_ranks(start.elapsed_time(end), world, dev)
-    ms_per_step = elapsed_ms / args.steps
+    ms_per_step = max_over_ranks(start.elapsed_time(end), world, dev) / args.steps
 
-    # --- roofline of the dominant kernel: every attention launch of eager steps bracketed by events on
-    # the launching stream
+    # --- roofline of the dominant kernel: every attention launch of eager steps bracketed by events on the
+    # launching stream
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
            for _ in range(args.kernel_steps)]
     barrier()
@@ -322,24 +449,26 @@ def run_ours(args) -> None:
         for l in range(layers):
             layer_step(l, evs[s][l])
     barrier()
-    attn_ms = [e0.elapsed_time(e1) for step in evs for (e0, e1) in step]
-    attn_avg_ms = max_over_ranks(statistics.mean(attn_ms), world, dev)
+    attn_avg_ms = max_over_ranks(statistics.mean(e0.elapsed_time(e1) for st in evs for e0, e1 in st), world, dev)
 
-    bytes_rank_layer = kv_bytes(ctx, hkv_l)
-    bytes_step_total = bytes_rank_layer * layers * world
-    value = bytes_step_total / (ms_per_step * 1e-3) / 1e9
+    # --- the block copy alone (COW / compaction bytes moved)
+    copy_ms = None
+    if copies:
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        c0.record()
+        for _ in range(3):
+            ops.block_copy(ptrs, k_pools[0], src, dst)
+        c1.record()
+        barrier()
+        copy_ms = max_over_ranks(c0.elapsed_time(c1) / 3, world, dev)
 
-    # --- append kernel alone (append GB/s): K1 over the 32 pools, captured in a CUDA graph so the
+    # --- append kernel alone (append GB/s): K1 over the layer pools, captured in a CUDA graph so the
     # launch-bound kernel is timed on the device, not behind the Python launch path
     graph = torch.cuda.CUDAGraph()
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        ops.kv_append(k_pools[0], v_pools[0], meta.slot_mapping, k_l, v_l)  # warm the path outside capture
-    torch.cuda.current_stream(dev).wait_stream(side)
     with torch.cuda.graph(graph):
         for l in range(layers):
-            ops.kv_append(k_pools[l], v_pools[l], meta.slot_mapping, k_l, v_l)
+            ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
     graph.replay()
     ap_s, ap_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -351,50 +480,65 @@ def run_ours(args) -> None:
     barrier()
     del graph, step_graph  # graphs holding NCCL work go before the process group
     append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
-    append_bytes = 2 * 2 * args.batch * hkv_l * DH * 2  # K and V rows read + written, bf16
+    append_bytes = 2 * 2 * n_app * hkv_l * DH * 2  # K and V rows read + written, bf16
 
     # --- optional GPU comparison: FlashInfer's paged decode on the same pools, called as the reference's
     # FlashInfer backend calls it (attention/flashinfer_backend.py:48-58: NHD, plan once, run per layer)
     flashinfer = None
     if args.flashinfer and world == 1:
-        flashinfer = run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, args.kernel_steps, dev)
+        flashinfer = run_flashinfer(meta_att, q, k_pools, v_pools, wl.attend_ctx, layers, args.kernel_steps, dev)
 
     # --- end to end through the public API with host buffers (metadata build + H2D in, D2H out)
     e2e = None
-    if not args.no_e2e:
-        e2e = run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx)
+    if not args.no_e2e and args.config == 2:
+        e2e = run_e2e(args, mlb, sharding, seqsteps(wl.attend_rows), q, k, v, k_pools, v_pools, dev, world,
+                      wl.attend_ctx)
 
+    ctx = wl.attend_ctx
+    bytes_rank_layer = kv_bytes(ctx, hkv_l)
+    value = bytes_rank_layer * layers * world / (ms_per_step * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = bytes_rank_layer / (attn_avg_ms * 1e-3) / 1e9
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
         torch.set_num_threads(os.cpu_count() or 1)
-        cpu = run_cpu_baseline(ctx, blocks, args.cpu_sample_seqs, reps=args.cpu_reps)
+        cpu = run_cpu_baseline(wl, args.cpu_sample_seqs, reps=args.cpu_reps)
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC if args.config == 2 else f"{wl.name}: paged decode attn KV-read GB/s (step incl. "
+                                                        f"appends{' and block copies' if copies else ''})",
+            "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "config 2: Llama-3.1-8B decode attention (H32/Hkv8/Dh128, bs16), batch 64, "
-                                   "ctx U[512,4096], 32 layer pools, append 1 token/seq + paged attention",
-                       "layers": layers, "batch": args.batch, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
+            "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "decode_rows": n_att,
+                       "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
                        "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
-                       "l2": "no flush: every layer reads 604 MB of KV, > 126 MB L2",
+                       "l2": "no flush: every layer's pool reads exceed the 126 MB L2",
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
-                       "partial_rows": plan.num_partial_rows},
-            "seqs_per_s": round(args.batch / (ms_per_step * 1e-3 / layers), 1),
+                       "partial_rows": plan.num_partial_rows, **wl.info},
+            "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
             "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 2),
             "append_us": round(append_ms * 1e3, 2),
             "attention_us": round(attn_avg_ms * 1e3, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profiled_traffic(), "algorithmic_bytes": bytes_rank_layer,
+                         "traffic": profiled_traffic() if args.config == 2 and world == 1 else None,
+                         "algorithmic_bytes": bytes_rank_layer,
                          "kernel": "paged_attn_mma_kernel<bf16, Dh 128, 2 slots, 4 warps>"},
-            "gpu_launches": launches_per_layer * layers * args.steps,
-            "timing": "value: CUDA-graph replays of the 32-layer step; roofline: event-timed eager attention launches",
+            "gpu_launches": launches_per_layer * layers * args.steps + (args.steps if copies else 0),
+            "timing": "value: CUDA-graph replays of the step; roofline: event-timed eager attention launches",
             "clocks": clocks.summary(),
         }
+        if args.config == 4:  # shared prefix: HBM sees each shared block once per launch
+            unique = wl.unique_pages() * BS * 2 * hkv_l * DH * 2
+            line["roofline"]["unique_bytes"] = unique
+            line["roofline"]["unique_gbs"] = round(unique / (attn_avg_ms * 1e-3) / 1e9, 1)
+            line["roofline"]["unique_frac"] = round(unique / (attn_avg_ms * 1e-3) / 1e9 / peak, 4)
+        if copies:
+            moved = copies * 2 * layers * BS * hkv_l * DH * 2  # blocks x (K, V) x layers, each read and written
+            line["block_copy"] = {"pairs": copies, "us": round(copy_ms * 1e3, 2),
+                                  "gbs_read_plus_write": round(2 * moved / (copy_ms * 1e-3) / 1e9, 1)}
         if e2e:
             line["e2e"] = e2e
         if flashinfer:
@@ -490,7 +634,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=2)
+    ap.add_argument("--layers", type=int, default=0, help="layer pools (default: the config's, 32 or 1)")
     ap.add_argument("--kernel-steps", type=int, default=10, help="eager steps whose attention launches are timed")
     ap.add_argument("--batch", type=int, default=64)
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
@@ -499,8 +644,6 @@ def main() -> None:
     ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
-    if args.warmup < 3 and args.impl == "ours" and args.layers == 32:
-        print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference_arm(args)
     else:
