@@ -388,7 +388,7 @@ def run_ours(args) -> None:
         ptrs = ops.pool_pointer_table(k_pools + v_pools)
         src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
         dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
-    launches_per_layer = 2 + (1 if plan.num_partial_rows else 0)
+    launches_per_layer = 2 + (1 if plan.num_partial_rows else 0)  # append, attention, split-K reduction
 
     def layer_step(l, ev=None):
         ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)

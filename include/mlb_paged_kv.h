@@ -65,8 +65,9 @@ MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t
                   int64_t num_tokens, int num_kv_heads, int head_dim, int32_t* err_word, void* stream);
 
 /*
- * One unit of paged-attention work: query tile `q_tile` of sequence `seq` over the pages
- * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads).
+ * One unit of paged-attention work: query tile `tile_splits & 0xFFFFF` of sequence `seq` over the pages
+ * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads);
+ * `tile_splits >> 20` is the number of units the tile's pages are split into (at most 4095).
  * part_row < 0: the unit covers the whole context and writes `out` itself; otherwise it writes
  * normalised fp32 partial rows part_row + t (t = token within the tile) for the split-K reduction.
  * q0 / num_new / seq_len repeat the sequence's qo_indptr[seq], new-token count and context length so
@@ -74,7 +75,7 @@ MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t
  */
 typedef struct {
   int32_t seq;
-  int32_t q_tile;
+  int32_t tile_splits;
   int32_t page_begin;
   int32_t page_end;
   int32_t part_row;
@@ -115,6 +116,10 @@ MLB_API int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_l
  * [num_partial_rows, num_heads] (fp32, caller-owned) may be NULL when the plan has no partial rows.
  * out: [N, num_heads, head_dim] of q's dtype.  Supported: head_dim 64/128/256, block_size 16,
  * num_heads / num_kv_heads <= 8; f16/bf16 pools use tensor-core tiles, f32 pools CUDA cores.
+ * split_counters: NULL leaves the split sequences' partial rows for mlb_splitk_reduce.  Otherwise a device
+ * int32 array of ceil(num_partial_rows / tokens_per_tile) * num_kv_heads entries, all zero before the first
+ * call: the last CTA of each split group merges the group itself (no reduction launch) and returns its
+ * counter to zero, so the array can be reused call after call.
  */
 MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                         const void* k_cache, const void* v_cache, int dtype, int64_t num_blocks, int block_size,
@@ -122,7 +127,7 @@ MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_s
                         const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
                         const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
                         float* partial_o, float* partial_lse, int64_t num_partial_rows,
-                        void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        int32_t* split_counters, void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         int32_t* err_word, void* stream);
 
 /*
@@ -150,11 +155,12 @@ MLB_API int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks
  * callers that cannot allocate device memory when they attend, e.g. an engine that gave nearly all free
  * device memory to the KV pool at start-up (as the reference sizes its pool, engine/process.py:91-115), or a
  * non-PyTorch serving loop with no device allocator and no room for cudaMalloc's implicit synchronisation.
- * Same arguments and results as mlb_paged_attention followed by mlb_splitk_reduce (out gets q's dtype),
- * with the split-K partial rows kept in a static device array of MLB_NOALLOC_SCRATCH_BYTES that every GPU
- * loading the library holds until exit.  Plans whose partial rows need more than that (rows x num_heads x
- * (head_dim + 1) x 4 bytes, each part 256-byte aligned) return MLB_ENOSPACE.  All calls share the array and
- * it keeps the last call's contents; calls that overlap on the GPU race.  The first call on a device looks
+ * Same arguments and results as mlb_paged_attention with the split groups merged in-kernel (out gets q's
+ * dtype), with the split-K partial rows and merge counters kept in a static device array of
+ * MLB_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit.  Plans whose partial rows
+ * need more than that (a 64 KiB counter area, then rows x num_heads x (head_dim + 1) x 4 bytes, each part
+ * 256-byte aligned) return MLB_ENOSPACE.  All calls share the array and it keeps the last call's
+ * contents; each call clears the counters it uses; calls that overlap on the GPU race.  The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) with that device current: make it before any stream
  * capture.  reduce_rows / reduce_chunks / num_tokens are the plan's (mlb_plan_attention).
  */

@@ -26,7 +26,7 @@ NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 class WorkUnit(ctypes.Structure):
     """mlb_work_unit: one (sequence, query tile, page range) of paged-attention work."""
 
-    _fields_ = [("seq", c_int32), ("q_tile", c_int32), ("page_begin", c_int32), ("page_end", c_int32),
+    _fields_ = [("seq", c_int32), ("tile_splits", c_int32), ("page_begin", c_int32), ("page_end", c_int32),
                 ("part_row", c_int32), ("q0", c_int32), ("num_new", c_int32), ("seq_len", c_int32)]
 
 
@@ -43,8 +43,8 @@ _SIGNATURES = {
     "mlb_plan_capacity": (c_int64, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]),
     "mlb_paged_attention": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                     c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
-                                    c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
-                                    c_void_p]),
+                                    c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                    c_void_p, c_void_p]),
     "mlb_splitk_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                   c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,

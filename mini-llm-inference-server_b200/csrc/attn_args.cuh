@@ -20,10 +20,10 @@ struct AttnArgs {
   const mlb_work_unit* units;
   float* part_o;
   float* part_lse;
+  int32_t* counters;  // split-group arrival counters (NULL: leave partial rows for the reduction kernel)
   char* out;
   int64_t o_st, o_sh;  // out strides (tokens, heads) in elements
   int32_t* err;
-  uint64_t wait_ns;  // bound on every mbarrier wait
 };
 
 }  // namespace mlb

@@ -48,7 +48,7 @@ bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a)
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
 constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
 constexpr int kWaveTenths = 15;      // the auto split aims for 1.5 waves of resident CTAs (measured best)
-constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits give up after 2 s
+constexpr int kMaxSplits = 4095;     // splits per query tile (12 bits of mlb_work_unit.tile_splits)
 
 int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
 
@@ -74,6 +74,7 @@ int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_bl
     if (L < n) return fail(MLB_EINVAL, "sequence %d: seq_len %d < %d new tokens", s, L, n);
     if (max_blocks >= 0 && static_cast<int64_t>(L) > static_cast<int64_t>(max_blocks) * bs)
       return fail(MLB_EINVAL, "sequence %d: %d blocks can't hold %d tokens", s, max_blocks, L);
+    if ((n + tpt - 1) / tpt > (1 << 20)) return fail(MLB_EINVAL, "sequence %d: %d new tokens is too many query tiles", s, n);
     for (int t = 0; t * tpt < n; ++t) {
       const int last = std::min((t + 1) * tpt, n) - 1;
       const int extent = L - n + last + 1;
@@ -166,14 +167,17 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
     for (int64_t t = 0; t < num_tokens; ++t) reduce_rows[t] = -1, reduce_chunks[t] = 0;
   int64_t rows = 0;
   for (const Group& g : groups) {
-    const int64_t nch = std::max<int64_t>(1, (g.pages + chunk - 1) / chunk);
-    const int64_t per = (g.pages + nch - 1) / nch;
+    // Split into runs of `per` pages; nch runs, none empty, and ceil(pages / nch) == per again (the kernel
+    // recovers a unit's run index from page_begin / per).
+    const int64_t n0 = std::min<int64_t>(kMaxSplits, std::max<int64_t>(1, (g.pages + chunk - 1) / chunk));
+    const int64_t per = std::max<int64_t>(1, (g.pages + n0 - 1) / n0);
+    const int64_t nch = std::max<int64_t>(1, (g.pages + per - 1) / per);
     const int64_t base = nch > 1 ? rows : -1;
     if (nch > 1) rows += nch * tpt;
     for (int64_t c = 0; c < nch; ++c) {
       mlb_work_unit u{};
       u.seq = g.seq;
-      u.q_tile = g.tile;
+      u.tile_splits = g.tile | static_cast<int32_t>(nch << 20);
       u.page_begin = static_cast<int32_t>(c * per);
       u.page_end = static_cast<int32_t>(std::min<int64_t>((c + 1) * per, g.pages));
       u.part_row = nch > 1 ? static_cast<int32_t>(base + c * tpt) : -1;
@@ -209,8 +213,9 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
                         int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
                         const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
-                        int64_t num_units, float* partial_o, float* partial_lse, int64_t num_partial_rows, void* out,
-                        int64_t out_stride_tok, int64_t out_stride_head, int32_t* err_word, void* stream) {
+                        int64_t num_units, float* partial_o, float* partial_lse, int64_t num_partial_rows,
+                        int32_t* split_counters, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        int32_t* err_word, void* stream) {
   if (!elt_bytes(dtype)) return fail(MLB_EINVAL, "paged_attention: unknown dtype %d", dtype);
   if (block_size != mlb::kBlockSize)
     return fail(MLB_EUNSUPPORTED, "paged_attention: block_size %d (kernels are built for 16)", block_size);
@@ -251,11 +256,11 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   a.units = units;
   a.part_o = partial_o;
   a.part_lse = partial_lse;
+  a.counters = split_counters;
   a.out = static_cast<char*>(out);
   a.o_st = out_stride_tok;
   a.o_sh = out_stride_head;
   a.err = err_word;
-  a.wait_ns = kWaitNs;
   return cuda_status(mlb::launch_paged_attention(a, dtype, head_dim, num_units, static_cast<cudaStream_t>(stream)),
                      "paged_attention launch");
 }

@@ -1,5 +1,5 @@
 // Shared device helpers for the sm_100a paged-KV kernels: dtype traits, RNE casts, and thin inline-PTX
-// wrappers for mbarriers, bulk (TMA) copies, ldmatrix / movmatrix and the m16n8k16 tensor-core MMA.
+// wrappers for 16-byte cp.async, ldmatrix / movmatrix and the m16n8k16 tensor-core MMA.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -57,12 +57,6 @@ __device__ __forceinline__ void flag_error(int32_t* err, int bit) {
   if (err) atomicOr(err, bit);
 }
 
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 __device__ __forceinline__ float fast_exp2(float x) {  // ex2.approx: 2^x, -inf -> +0
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -71,57 +65,6 @@ __device__ __forceinline__ float fast_exp2(float x) {  // ex2.approx: 2^x, -inf 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// ---------------------------------------------------------------- mbarrier + bulk copy (TMA engine)
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Wait for phase `parity` of `bar` to complete, for at most `limit_ns`.  Returns false on time-out.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > limit_ns) return false;
-  }
-  return true;
-}
-
-// 1-D bulk copy global -> this CTA's shared memory, completion counted in bytes on `bar`.
-// dst, src and bytes must be multiples of 16.  Never used with .multicast.
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
 }
 
 // ---------------------------------------------------------------- 16-byte asynchronous copies (LDGSTS)

@@ -7,13 +7,16 @@
 // Work decomposition (one CTA = one work unit x one KV head):
 //   unit = (sequence, query tile, page range).  A query tile is up to 8 "columns" = (query token,
 //   query head) pairs that share this KV head; a decode row of GQA group 4 is 4 columns.
-//   The CTA's 4 warps take the unit's pages round robin.  Each warp streams its pages through a private
-//   ring of STAGES shared-memory slots filled by the TMA engine: 32 one-dimensional bulk copies per
-//   page (16 K rows + 16 V rows of this head, one per lane) complete on the slot's mbarrier.  Shared
-//   rows are padded by 16 bytes so ldmatrix reads are free of bank conflicts.
+//   The CTA's warps take the unit's pages round robin.  Each warp streams its pages through a private
+//   ring of shared-memory slots filled with 16-byte cp.async (a page of one head = 16 K rows + 16 V rows);
+//   rows are padded by 16 bytes so ldmatrix reads are free of bank conflicts.  (On B200 this load path
+//   measured 6.75-6.86 TB/s for these 256-byte rows, equal to tensor-map TMA with 2 KB boxes and above
+//   1-D bulk copies of single rows.)
 //   Per page and warp: S^T[16 tok x 8 col] = K[16 x Dh] . Q^T (m16n8k16 MMAs, fp32 accumulate),
 //   online softmax per column (exp2 domain), P^T goes back to a B fragment with movmatrix.trans, and
-//   O^T[Dh x 8] += V^T . P^T.  The 4 warps' (m, l, O) are merged through shared memory at the end.
+//   O^T[Dh x 8] += V^T . P^T.  The warps' (m, l, O) are merged through shared memory at the end.
+//   A sequence split over several units writes normalised fp32 partial rows; the last CTA of the split
+//   group to finish merges them (in-kernel split-K reduction), or K2b does when no counters are given.
 // f32 pools take a CUDA-core path with the same decomposition (fp32 accuracy, 1e-5).
 #include "attn_args.cuh"
 
@@ -35,24 +38,30 @@ constexpr float kNegInf = -__builtin_huge_valf();
 
 struct UnitInfo {
   int seq, q0, n_new, L, t0, ncols, pb, pe, part_row;
+  int nsplit;      // units the query tile's pages are split into
+  int split_base;  // first partial row of the tile's split group (valid when part_row >= 0)
 };
 
 __device__ __forceinline__ UnitInfo unit_info(const AttnArgs& a, int unit_idx) {
   const int4* rec = reinterpret_cast<const int4*>(a.units + unit_idx);  // one 32-byte record, two loads
   const int4 x = __ldg(rec), y = __ldg(rec + 1);
-  mlb_work_unit u;
-  u.seq = x.x, u.q_tile = x.y, u.page_begin = x.z, u.page_end = x.w;
-  u.part_row = y.x, u.q0 = y.y, u.num_new = y.z, u.seq_len = y.w;
   UnitInfo r;
-  r.seq = u.seq;
-  r.q0 = u.q0;
-  r.n_new = u.num_new;
-  r.L = u.seq_len;
-  r.t0 = u.q_tile * a.tile_tokens;
-  r.ncols = min(a.tile_tokens, r.n_new - r.t0) * a.group;
-  r.pb = u.page_begin;
-  r.pe = u.page_end;
-  r.part_row = u.part_row;
+  r.seq = x.x;
+  const int tile = x.y & 0xFFFFF;
+  r.nsplit = static_cast<int>(static_cast<uint32_t>(x.y) >> 20);
+  r.pb = x.z;
+  r.pe = x.w;
+  r.part_row = y.x;
+  r.q0 = y.y;
+  r.n_new = y.z;
+  r.L = y.w;
+  r.t0 = tile * a.tile_tokens;
+  const int ntok = min(a.tile_tokens, r.n_new - r.t0);
+  r.ncols = ntok * a.group;
+  // The planner split the tile's pages into nsplit runs of `per` pages; this unit is run pb / per.
+  const int pages = (r.L - r.n_new + r.t0 + ntok + kBlockSize - 1) / kBlockSize;
+  const int per = (pages + r.nsplit - 1) / max(r.nsplit, 1);
+  r.split_base = r.part_row - (per > 0 ? r.pb / per : 0) * a.tile_tokens;
   return r;
 }
 
@@ -94,6 +103,43 @@ __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInf
       a.part_o[(row * a.h + head) * DH + d] = val;
       if (d == 0) a.part_lse[row * a.h + head] = lsum > 0.f ? M + log2f(lsum) : kNegInf;
     }
+  }
+}
+
+// Split-K merge done by the last CTA of a split group (no reduction launch): every CTA of the group has
+// written its normalised partial row and its log2-sum-exp; the CTA whose arrival completes the group's
+// counter combines them into `out` and returns the counter to zero for the next launch.
+template <int DH, int OUT_DT>
+__device__ __forceinline__ void merge_split_group(const AttnArgs& a, const UnitInfo& ui, int kvh) {
+  __shared__ int s_last;
+  __threadfence();  // this CTA's partial rows are visible device-wide before it is counted
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t* cnt = a.counters + static_cast<int64_t>(ui.split_base / a.tile_tokens) * a.hkv + kvh;
+    const int prev = atomicAdd(cnt, 1);
+    s_last = prev == ui.nsplit - 1;
+    if (s_last) *cnt = 0;  // every other CTA of the group has already arrived
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < ui.ncols * DH; idx += blockDim.x) {
+    const int j = idx / DH, d = idx % DH;
+    const int t = j / a.group, head = kvh * a.group + j % a.group;
+    float M = kNegInf;
+    for (int c = 0; c < ui.nsplit; ++c)
+      M = fmaxf(M, __ldcg(a.part_lse + (static_cast<int64_t>(ui.split_base + c * a.tile_tokens + t)) * a.h + head));
+    float lsum = 0.f, acc = 0.f;
+    for (int c = 0; c < ui.nsplit; ++c) {
+      const int64_t row = ui.split_base + c * a.tile_tokens + t;
+      const float lse = __ldcg(a.part_lse + row * a.h + head);
+      const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
+      lsum += w;
+      acc = fmaf(w, __ldcg(a.part_o + (row * a.h + head) * DH + d), acc);
+    }
+    char* o = a.out + ((static_cast<int64_t>(ui.q0 + ui.t0 + t) * a.o_st + static_cast<int64_t>(head) * a.o_sh + d) *
+                       Elt<OUT_DT>::bytes);
+    store_f32<OUT_DT>(o, lsum > 0.f ? acc / lsum : 0.f);
   }
 }
 
@@ -308,6 +354,7 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
     sl_w[w] = sm_w[w] + 8;
   }
   merge_and_store<DH, DT, NW>(a, ui, kvh, so_w, sm_w, sl_w);
+  if (ui.part_row >= 0 && a.counters) merge_split_group<DH, DT>(a, ui, kvh);
 }
 
 // ------------------------------------------------------------------ f32 pools: CUDA cores
@@ -438,6 +485,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a)
     sl_w[w] = sm_w[w] + 8;
   }
   merge_and_store<DH, MLB_F32, kWarps>(a, ui, kvh, so_w, sm_w, sl_w);
+  if (ui.part_row >= 0 && a.counters) merge_split_group<DH, MLB_F32>(a, ui, kvh);
 }
 
 // ------------------------------------------------------------------ split-K reduction

@@ -156,11 +156,13 @@ def plan_attention(qo_indptr: list[int], seq_lens: list[int], max_blocks: int, n
 
 
 class Workspace:
-    """Split-K scratch (fp32 partial rows + their log-sum-exp), grown on demand and reused across calls."""
+    """Split-K scratch, grown on demand and reused across calls: fp32 partial rows, their log-sum-exp, and the
+    int32 split-group counters of the in-kernel merge (allocated zeroed; the kernel leaves them zero)."""
 
     def __init__(self) -> None:
         self._o: torch.Tensor | None = None
         self._lse: torch.Tensor | None = None
+        self._cnt: torch.Tensor | None = None
 
     def get(self, rows: int, heads: int, dh: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
         need_o, need_l = rows * heads * dh, rows * heads
@@ -170,31 +172,38 @@ class Workspace:
             self._lse = torch.empty(max(need_l, 1), dtype=torch.float32, device=device)
         return self._o, self._lse
 
+    def counters(self, plan: AttentionPlan, device: torch.device) -> torch.Tensor:
+        need = -(-plan.num_partial_rows // plan.tokens_per_tile) * plan.num_kv_heads
+        if self._cnt is None or self._cnt.device != device or self._cnt.numel() < need:
+            self._cnt = torch.zeros(max(need, 1), dtype=torch.int32, device=device)
+        return self._cnt
+
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan,
                     workspace: Workspace | None = None, out: torch.Tensor | None = None, scale: float | None = None,
-                    err: torch.Tensor | None = None) -> torch.Tensor:
+                    err: torch.Tensor | None = None, fused_reduce: bool = False) -> torch.Tensor:
     """paged_attention (paged_torch_ref.py:40-74) on the GPU: q [N, H, Dh] -> [N, H, Dh] in q's dtype.
 
     block_tables int32 [S, W], seq_lens int32 [S], qo_indptr int32 [S + 1] are AttentionMetadata's
     device tensors (block_tables_i32, seq_lens_i32, qo_indptr).  The pools must already hold this
-    step's k/v (kv_append first).  Launches the attention kernel, then the split-K reduction when the
-    plan split any sequence.
+    step's k/v (kv_append first).  Split sequences are merged by the split-K reduction kernel (measured
+    faster on B200), or with fused_reduce=True by the last CTA of each split group (one launch fewer).
     """
     workspace = workspace or Workspace()
     out = attention_partials(q, k_cache, v_cache, block_tables, seq_lens, qo_indptr, plan, workspace, out, scale,
-                             err)
-    splitk_reduce(plan, workspace, out)
+                             err, fused_reduce)
+    if not fused_reduce:
+        splitk_reduce(plan, workspace, out)
     return out
 
 
 def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                        seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan, workspace: Workspace,
                        out: torch.Tensor | None = None, scale: float | None = None,
-                       err: torch.Tensor | None = None) -> torch.Tensor:
-    """The attention kernel alone (K2a): unsplit sequences are final in `out`; split ones leave fp32 partial
-    rows in `workspace` for `splitk_reduce`."""
+                       err: torch.Tensor | None = None, fused_reduce: bool = False) -> torch.Tensor:
+    """The attention kernel (K2a).  Unsplit sequences are final in `out`; split ones are merged in-kernel
+    (fused_reduce) or left as fp32 partial rows in `workspace` for `splitk_reduce`."""
     _check_pool(k_cache, "paged_attention")
     _check_pool(v_cache, "paged_attention")
     nb, bs, hkv, dh = k_cache.shape
@@ -215,15 +224,17 @@ def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     if n == 0 or plan.num_units == 0:
         return out
     scale = 1.0 / math.sqrt(dh) if scale is None else float(scale)
-    po = plse = None
+    po = plse = cnt = None
     if plan.num_partial_rows:
         po, plse = workspace.get(plan.num_partial_rows, h, dh, q.device)
+        if fused_reduce:
+            cnt = workspace.counters(plan, q.device)
     rc = lib().mlb_paged_attention(q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
                                    _code(q, "paged_attention"), nb, bs, h, hkv, dh, scale, block_tables.data_ptr(),
                                    block_tables.stride(0), seq_lens.data_ptr(), qo_indptr.data_ptr(),
                                    seq_lens.shape[0], plan.units.data_ptr(), plan.num_units, _ptr(po), _ptr(plse),
-                                   plan.num_partial_rows, out.data_ptr(), out.stride(0), out.stride(1), _ptr(err),
-                                   _stream(q.device))
+                                   plan.num_partial_rows, _ptr(cnt), out.data_ptr(), out.stride(0), out.stride(1),
+                                   _ptr(err), _stream(q.device))
     check(rc, "paged_attention")
     return out
 

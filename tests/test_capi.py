@@ -52,19 +52,23 @@ def test_invalid_arguments_return_status_without_launching(L):
     rc = lib.mlb_kv_append(None, None, 2, 10, 16, None, None, 0, 0, None, 0, 0, 2, 1, 2, 64, None, None)
     assert rc == L.MLB_EINVAL and "null" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 32, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, 0, 0, None, None)
+                                 None, None, 0, None, None, 0, 0, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "block_size" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 16, 32, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, 0, 0, None, None)
+                                 None, None, 0, None, None, 0, 0, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "query heads per KV head" in L.last_error()
     rc = lib.mlb_block_copy(None, 2, 10, 100, None, None, 3, None, None)
     assert rc == L.MLB_EUNSUPPORTED
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 8, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, 0, 0, None, None)
+                                 None, None, 0, None, None, 0, 0, None, None)
     with pytest.raises(ValueError, match="block_size"):  # status codes become the reference's ValueError
         L.check(rc, "paged_attention")
     # zero work is a successful no-op
     assert lib.mlb_block_copy(None, 0, 10, 64, None, None, 0, None, None) == L.MLB_OK
+
+
+def _first_token(qo, seq, tile, tpt):
+    return qo[seq] + tile * tpt
 
 
 def plan(mlb, steps, h=32, hkv=8, ppu=0, sms=148, width=None):
@@ -91,8 +95,9 @@ def test_planner_covers_every_page_once(mlb, seed, h, hkv, ppu):
     assert (np.diff(sizes) <= 0).all(), "largest units first"
     # per (seq, tile) the units tile the pages the tile's last query can see, exactly once
     cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
-    for seq, tile, pb, pe, prow, *_ in u.tolist():
-        cover.setdefault((seq, tile), []).append((pb, pe, prow))
+    for seq, tile_splits, pb, pe, prow, *_ in u.tolist():
+        cover.setdefault((seq, tile_splits & 0xFFFFF), []).append((pb, pe, prow))
+        assert tile_splits >> 20 == p.reduce_chunks_host[_first_token(qo, seq, tile_splits & 0xFFFFF, tpt)]
     for s, (cached, new) in enumerate(steps):
         for t in range(-(-new // tpt)):
             last = min((t + 1) * tpt, new) - 1

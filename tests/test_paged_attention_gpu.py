@@ -42,11 +42,23 @@ def test_golden_cases(mlb, cuda, case, dtype):
 
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
 @pytest.mark.parametrize("ppu", [1, 2, 5])
-def test_forced_split_k_matches(mlb, cuda, dtype, ppu):
+@pytest.mark.parametrize("fused", [True, False], ids=["merged_in_kernel", "reduction_kernel"])
+def test_forced_split_k_matches(mlb, cuda, dtype, ppu, fused):
+    ws = mlb.Workspace()  # shared across cases and calls: the merge counters must come back to zero
     for case in (cases.llama_decode(21, 4, 512, 4096), cases.mixed_step(), cases.boundaries(6, 32, 8, 128)):
-        out, _, backend = run_backend(mlb, case, dtype, cuda, ppu=ppu)
-        assert backend._plan.num_partial_rows > 0
-        assert_close(out, oracle_forward(case, dtype)[0], dtype)
+        t = device_case(case, dtype, cuda)
+        meta = mlb.AttentionMetadata.build([mlb.SeqStep(c, n, list(b)) for c, n, b in case.seqs], case.bs, cuda)
+        mlb.kv_append(t["k_pool"], t["v_pool"], meta.slot_mapping, t["k"], t["v"])
+        plan = mlb.plan_attention(meta.query_start_loc, meta.seq_lens, meta.block_tables_i32.shape[1], case.h,
+                                  case.hkv, cuda, pages_per_unit=ppu)
+        assert plan.num_partial_rows > 0
+        expected = oracle_forward(case, dtype)[0]
+        for _ in range(2):
+            out = mlb.paged_attention(t["q"], t["k_pool"], t["v_pool"], meta.block_tables_i32, meta.seq_lens_i32,
+                                      meta.qo_indptr, plan, ws, fused_reduce=fused)
+            assert_close(out, expected, dtype)
+    if fused:
+        assert int(torch.count_nonzero(ws._cnt).item()) == 0
 
 
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
