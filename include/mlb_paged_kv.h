@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);
+MLB_API int mlb_abi_version(void);  /* 2 */
 
 /*
  * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three
@@ -65,9 +65,8 @@ MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t
                   int64_t num_tokens, int num_kv_heads, int head_dim, int32_t* err_word, void* stream);
 
 /*
- * One unit of paged-attention work: query tile `tile_splits & 0xFFFFF` of sequence `seq` over the pages
- * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads);
- * `tile_splits >> 20` is the number of units the tile's pages are split into (at most 4095).
+ * One unit of paged-attention work: query tile `q_tile` of sequence `seq` over the pages
+ * [page_begin, page_end) of its block table, for every KV head (the kernel's grid is units x heads).
  * part_row < 0: the unit covers the whole context and writes `out` itself; otherwise it writes
  * normalised fp32 partial rows part_row + t (t = token within the tile) for the split-K reduction.
  * q0 / num_new / seq_len repeat the sequence's qo_indptr[seq], new-token count and context length so
@@ -75,7 +74,7 @@ MLB_API int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t
  */
 typedef struct {
   int32_t seq;
-  int32_t tile_splits;
+  int32_t q_tile;
   int32_t page_begin;
   int32_t page_end;
   int32_t part_row;
@@ -85,25 +84,51 @@ typedef struct {
 } mlb_work_unit;
 
 /*
+ * Shared-prefix work (a prefix-cache hit seen by many decode rows): pages [page_begin, page_end) are the
+ * same blocks in the tables of members [member_begin, member_begin + member_count) of the members array,
+ * and the table row of sequence `table_seq` holds them.  One CTA per (unit, KV head) loads each page once
+ * and applies it to every member's query heads, writing each member's partial row
+ * members[m].part_base + piece * tokens_per_tile.
+ */
+typedef struct {
+  int32_t member_begin;
+  int32_t member_count;
+  int32_t page_begin;
+  int32_t page_end;
+  int32_t piece;
+  int32_t table_seq;
+  int32_t reserved[2];
+} mlb_shared_unit;
+
+typedef struct {
+  int32_t seq;       /* the member sequence (a decode row: one new token)   */
+  int32_t q0;        /* qo_indptr[seq]: its token                          */
+  int32_t part_base; /* its first partial row                              */
+  int32_t reserved;
+} mlb_share_member;
+
+/*
  * Host-side planner (host pointers).  Plays the role of FlashInfer's per-step plan() that the reference
  * runs once per AttentionMetadata and reuses across layers (flashinfer_backend.py:44-45, :48-64).
  * Inputs: qo_indptr [num_seqs + 1] and seq_lens [num_seqs] exactly as AttentionMetadata holds them
  * (metadata.py:39-40, :97-98); max_blocks_per_seq = block_tables width (validates seq_lens).
- * pages_per_unit = 0 picks a split size from the total work and num_sms.
- * Outputs: units[*num_units] (capacity units_capacity; MLB_ENOSPACE with the needed count in
- * *num_units if too small), per token reduce_rows / reduce_chunks [num_tokens] (chunks <= 1: no
- * reduction for that token) and the number of fp32 partial rows the workspace must hold.
- * Query tokens per tile = max(1, 8 / (num_heads / num_kv_heads)).
+ * block_tables_host (optional, may be NULL): a host copy of the int32 block tables with row stride
+ * bt_stride_host; when given, decode rows whose tables start with the same run of block ids (shared
+ * prefix blocks) get shared-prefix units (a cascade split).  pages_per_unit = 0 picks a split size from
+ * the total work and num_sms.
+ * With units == NULL only the counts are returned (*num_units, *num_shared_units, *num_members,
+ * *num_partial_rows); otherwise every output array must hold its count (MLB_ENOSPACE if not).
+ * reduce_rows / reduce_chunks [num_tokens]: first partial row and number of pieces per token (pieces
+ * <= 1: nothing to reduce).  Query tokens per tile = max(1, 8 / (num_heads / num_kv_heads)).
  */
 MLB_API int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int max_blocks_per_seq,
+                       const int32_t* block_tables_host, int64_t bt_stride_host,
                        int num_heads, int num_kv_heads, int block_size, int num_sms, int pages_per_unit,
                        mlb_work_unit* units, int64_t units_capacity, int64_t* num_units,
+                       mlb_shared_unit* shared_units, int64_t shared_capacity, int64_t* num_shared_units,
+                       mlb_share_member* members, int64_t members_capacity, int64_t* num_members,
                        int32_t* reduce_rows, int32_t* reduce_chunks, int64_t num_tokens,
                        int64_t* num_partial_rows);
-
-/* Upper bound on the units mlb_plan_attention can emit for these sequences (host pointers). */
-MLB_API int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int num_heads,
-                          int num_kv_heads, int block_size);
 
 /*
  * Paged attention over block tables (decode rows and multi-token rows with the causal mask aligned to
@@ -111,23 +136,22 @@ MLB_API int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_l
  * and the FlashInfer decode/prefill wrappers' run() (flashinfer_backend.py:46).
  * q: [N, num_heads, head_dim] (strides in elements); pools as above, dtype == q's; block_tables:
  * device int32 [num_seqs, bt_stride] (metadata.py:48); seq_lens: device int32 [num_seqs];
- * qo_indptr: device int32 [num_seqs + 1]; units: device copy of the plan.  Scale is usually
- * 1/sqrt(head_dim).  partial_o [num_partial_rows, num_heads, head_dim] and partial_lse
- * [num_partial_rows, num_heads] (fp32, caller-owned) may be NULL when the plan has no partial rows.
- * out: [N, num_heads, head_dim] of q's dtype.  Supported: head_dim 64/128/256, block_size 16,
- * num_heads / num_kv_heads <= 8; f16/bf16 pools use tensor-core tiles, f32 pools CUDA cores.
- * split_counters: NULL leaves the split sequences' partial rows for mlb_splitk_reduce.  Otherwise a device
- * int32 array of ceil(num_partial_rows / tokens_per_tile) * num_kv_heads entries, all zero before the first
- * call: the last CTA of each split group merges the group itself (no reduction launch) and returns its
- * counter to zero, so the array can be reused call after call.
+ * qo_indptr: device int32 [num_seqs + 1]; units / shared_units / members: device copies of the plan
+ * (shared_units may be NULL when num_shared_units == 0).  Scale is usually 1/sqrt(head_dim).
+ * partial_o [num_partial_rows, num_heads, head_dim] and partial_lse [num_partial_rows, num_heads] (fp32,
+ * caller-owned) may be NULL when the plan has no partial rows; when it has some, mlb_splitk_reduce
+ * completes `out`.  out: [N, num_heads, head_dim] of q's dtype.  Supported: head_dim 64/128/256,
+ * block_size 16, num_heads / num_kv_heads <= 8; f16/bf16 pools use tensor-core tiles, f32 pools CUDA
+ * cores (f32 plans carry no shared-prefix units).
  */
 MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
                         const void* k_cache, const void* v_cache, int dtype, int64_t num_blocks, int block_size,
                         int num_heads, int num_kv_heads, int head_dim, float scale,
                         const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
                         const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
+                        const mlb_shared_unit* shared_units, int64_t num_shared_units, const mlb_share_member* members,
                         float* partial_o, float* partial_lse, int64_t num_partial_rows,
-                        int32_t* split_counters, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         int32_t* err_word, void* stream);
 
 /*
@@ -155,12 +179,11 @@ MLB_API int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks
  * callers that cannot allocate device memory when they attend, e.g. an engine that gave nearly all free
  * device memory to the KV pool at start-up (as the reference sizes its pool, engine/process.py:91-115), or a
  * non-PyTorch serving loop with no device allocator and no room for cudaMalloc's implicit synchronisation.
- * Same arguments and results as mlb_paged_attention with the split groups merged in-kernel (out gets q's
- * dtype), with the split-K partial rows and merge counters kept in a static device array of
- * MLB_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until exit.  Plans whose partial rows
- * need more than that (a 64 KiB counter area, then rows x num_heads x (head_dim + 1) x 4 bytes, each part
- * 256-byte aligned) return MLB_ENOSPACE.  All calls share the array and it keeps the last call's
- * contents; each call clears the counters it uses; calls that overlap on the GPU race.  The first call on a device looks
+ * Same arguments and results as mlb_paged_attention followed by mlb_splitk_reduce (out gets q's dtype),
+ * with the split-K partial rows kept in a static device array of MLB_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading the library holds until exit.  Plans whose partial rows need more than that (rows x num_heads x
+ * (head_dim + 1) x 4 bytes, each part 256-byte aligned) return MLB_ENOSPACE.  All calls share the array and
+ * it keeps the last call's contents; calls that overlap on the GPU race.  The first call on a device looks
  * up the array's device address (cudaGetSymbolAddress) with that device current: make it before any stream
  * capture.  reduce_rows / reduce_chunks / num_tokens are the plan's (mlb_plan_attention).
  */
@@ -170,6 +193,7 @@ MLB_API int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int
                         int num_heads, int num_kv_heads, int head_dim, float scale,
                         const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
                         const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
+                        const mlb_shared_unit* shared_units, int64_t num_shared_units, const mlb_share_member* members,
                         int64_t num_partial_rows, const int32_t* reduce_rows, const int32_t* reduce_chunks,
                         int64_t num_tokens, void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         int32_t* err_word, void* stream);

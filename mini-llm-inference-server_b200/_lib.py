@@ -18,8 +18,9 @@ MLB_OK, MLB_EINVAL, MLB_EUNSUPPORTED, MLB_ECUDA, MLB_ENOSPACE = 0, 1, 2, 3, 4
 # bits kernels OR into the device error word
 DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
 
-EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_plan_capacity",
-           "mlb_paged_attention", "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc")
+EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_paged_attention",
+           "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc")
+ABI_VERSION = 2
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 
 
@@ -30,7 +31,22 @@ class WorkUnit(ctypes.Structure):
                 ("part_row", c_int32), ("q0", c_int32), ("num_new", c_int32), ("seq_len", c_int32)]
 
 
+class SharedUnit(ctypes.Structure):
+    """mlb_shared_unit: a page range of a shared prefix, attended once for a block of member rows."""
+
+    _fields_ = [("member_begin", c_int32), ("member_count", c_int32), ("page_begin", c_int32),
+                ("page_end", c_int32), ("piece", c_int32), ("table_seq", c_int32), ("reserved", c_int32 * 2)]
+
+
+class ShareMember(ctypes.Structure):
+    """mlb_share_member: a decode row that reads a shared prefix."""
+
+    _fields_ = [("seq", c_int32), ("q0", c_int32), ("part_base", c_int32), ("reserved", c_int32)]
+
+
 WORK_UNIT_INT32S = ctypes.sizeof(WorkUnit) // 4
+SHARED_UNIT_INT32S = ctypes.sizeof(SharedUnit) // 4
+MEMBER_INT32S = ctypes.sizeof(ShareMember) // 4
 
 _I32P, _I64P = POINTER(c_int32), POINTER(c_int64)
 _SIGNATURES = {
@@ -38,21 +54,22 @@ _SIGNATURES = {
     "mlb_abi_version": (c_int, []),
     "mlb_kv_append": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64,
                               c_void_p, c_int64, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p]),
-    "mlb_plan_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
-                                   c_int64, _I64P, c_void_p, c_void_p, c_int64, _I64P]),
-    "mlb_plan_capacity": (c_int64, [c_void_p, c_void_p, c_int, c_int, c_int, c_int]),
+    "mlb_plan_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_int, c_int, c_int,
+                                   c_int, c_void_p, c_int64, _I64P, c_void_p, c_int64, _I64P, c_void_p, c_int64,
+                                   _I64P, c_void_p, c_void_p, c_int64, _I64P]),
     "mlb_paged_attention": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                     c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
-                                    c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64,
-                                    c_void_p, c_void_p]),
+                                    c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                                    c_int64, c_int64, c_void_p, c_void_p]),
     "mlb_splitk_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                   c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                                c_void_p]),
     "mlb_paged_attention_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
                                             c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p,
-                                            c_int, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
-                                            c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+                                            c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
+                                            c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
+                                            c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -60,12 +60,17 @@ class B200Backend(AttentionBackend):
         return F.scaled_dot_product_attention(q, k, v, attn_mask=mask, enable_gqa=True)
 
     # ------------------------------------------------------------------ paged path
-    def plan(self, meta, num_heads: int, num_kv_heads: int, device: torch.device) -> AttentionPlan:
-        key = (num_heads, num_kv_heads, device)
+    def plan(self, meta, num_heads: int, num_kv_heads: int, device: torch.device,
+             dtype: torch.dtype = torch.bfloat16) -> AttentionPlan:
+        """The step's plan, built on the first call with a new `meta` and reused after.  Shared-prefix units
+        are planned when the metadata carries host block tables (this package's AttentionMetadata does)
+        and the pools are 16-bit."""
+        key = (num_heads, num_kv_heads, device, dtype)
         if self._planned is not meta or self._plan_key != key:
+            tables = getattr(meta, "block_tables_host", None) if dtype != torch.float32 else None
             self._plan = plan_attention(meta.query_start_loc, meta.seq_lens, meta.block_tables_i32.shape[1],
                                         num_heads, num_kv_heads, device, meta.block_size, self.num_sms,
-                                        self.pages_per_unit)
+                                        self.pages_per_unit, block_tables_host=tables)
             self._planned, self._plan_key = meta, key
         return self._plan
 
@@ -74,7 +79,7 @@ class B200Backend(AttentionBackend):
             raise ValueError(f"pool block size {k_cache.shape[1]} != metadata block size {meta.block_size}")
         err = self._error_word(q.device) if self.check_errors else None
         kv_append(k_cache, v_cache, meta.slot_mapping, k, v, err)
-        plan = self.plan(meta, q.shape[1], k_cache.shape[2], q.device)
+        plan = self.plan(meta, q.shape[1], k_cache.shape[2], q.device, k_cache.dtype)
         out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
                               self._workspace, err=err)
         if self.check_errors:

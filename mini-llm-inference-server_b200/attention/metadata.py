@@ -43,6 +43,9 @@ class AttentionMetadata:
     kv_indptr: torch.Tensor  # [S + 1] int32 offsets into kv_indices
     kv_indices: torch.Tensor  # int32: the pages each sequence uses, concatenated
     kv_last_page_len: torch.Tensor  # [S] int32
+    # Not in the reference's metadata: the int32 block tables on the host, which let the planner find decode
+    # rows that share prefix blocks without a device round trip.
+    block_tables_host: np.ndarray | None = None
 
     @property
     def max_query_len(self) -> int:
@@ -109,6 +112,7 @@ class AttentionMetadata:
             kv_indptr=d32[o32[3]:o32[4]],
             kv_indices=d32[o32[4]:o32[5]],
             kv_last_page_len=d32[o32[5]:o32[6]],
+            block_tables_host=table.astype(np.int32),
         )
 
 

@@ -18,9 +18,10 @@ struct AttnArgs {
   const int32_t* seq_lens;
   const int32_t* qo;
   const mlb_work_unit* units;
+  const mlb_shared_unit* shared_units;
+  const mlb_share_member* members;
   float* part_o;
   float* part_lse;
-  int32_t* counters;  // split-group arrival counters (NULL: leave partial rows for the reduction kernel)
   char* out;
   int64_t o_st, o_sh;  // out strides (tokens, heads) in elements
   int32_t* err;

@@ -15,6 +15,7 @@ cudaError_t launch_kv_append(void* k_cache, void* v_cache, int cache_dtype, int6
                              int in_dtype, int64_t num_tokens, int hkv, int dh, bool vec, int32_t* err,
                              cudaStream_t s);
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
+cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
 cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
                                  int tpt, int64_t ntok, int h, int dh, char* out, int64_t o_st, int64_t o_sh,
                                  int out_dtype, cudaStream_t s);
@@ -48,7 +49,10 @@ bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a)
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
 constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
 constexpr int kWaveTenths = 15;      // the auto split aims for 1.5 waves of resident CTAs (measured best)
-constexpr int kMaxSplits = 4095;     // splits per query tile (12 bits of mlb_work_unit.tile_splits)
+constexpr int kSharedWarps = 8;      // warps per shared-prefix CTA; each takes max(1, 8 / group) members
+constexpr int kSharedCtasPerSm = 2;  // resident shared-prefix CTAs per SM
+constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
+constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages
 
 int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
 
@@ -60,7 +64,63 @@ int sm_count() {
 
 struct Group {
   int seq, tile, pages;
+  int start = 0;  // pages before this are planned as shared-prefix units (0: none)
+  int shared_pieces = 0;
 };
+
+// Sets of decode rows whose block tables begin with the same run of block ids (shared prefix-cache blocks).
+struct ShareSet {
+  std::vector<int> seqs;
+  int pages;  // shared pages: identical ids, full, and wholly before every member's new token
+};
+
+std::vector<ShareSet> find_shared_prefixes(const int32_t* qo, const int32_t* lens, int num_seqs, const int32_t* tables,
+                                           int64_t stride, int bs) {
+  // Candidates: decode rows with enough full pages before their new token.  Sorting their tables
+  // lexicographically puts rows that share a long run of leading block ids next to each other; a set is a
+  // maximal run whose neighbours share at least kMinSharePages pages, and it shares the run's minimum.
+  std::vector<int> cand;
+  std::vector<int> full(num_seqs, 0);
+  for (int s = 0; s < num_seqs; ++s) {
+    const int n = qo[s + 1] - qo[s];
+    full[s] = (lens[s] - n) / bs;  // pages wholly before the row's new token
+    if (n == 1 && full[s] >= kMinSharePages) cand.push_back(s);
+  }
+  auto row = [&](int s) { return tables + static_cast<int64_t>(s) * stride; };
+  auto lcp = [&](int a, int b) {
+    const int lim = std::min(full[a], full[b]);
+    const int32_t *ra = row(a), *rb = row(b);
+    int c = 0;
+    while (c < lim && ra[c] == rb[c]) ++c;
+    return c;
+  };
+  std::sort(cand.begin(), cand.end(), [&](int a, int b) {
+    const int c = lcp(a, b);
+    const int lim = std::min(full[a], full[b]);
+    if (c < lim) return row(a)[c] < row(b)[c];
+    return full[a] != full[b] ? full[a] < full[b] : a < b;
+  });
+  std::vector<ShareSet> sets;
+  for (size_t i = 0; i < cand.size();) {
+    size_t j = i + 1;
+    int shared = full[cand[i]];
+    while (j < cand.size()) {
+      const int c = lcp(cand[j - 1], cand[j]);
+      if (c < kMinSharePages) break;
+      shared = std::min(shared, c);
+      ++j;
+    }
+    if (j - i >= static_cast<size_t>(kMinShareSeqs)) {
+      ShareSet set;
+      set.pages = shared;
+      set.seqs.assign(cand.begin() + i, cand.begin() + j);
+      std::sort(set.seqs.begin(), set.seqs.end());
+      sets.push_back(std::move(set));
+    }
+    i = j;
+  }
+  return sets;
+}
 
 // Enumerate (sequence, query tile) groups and the pages each must read; validates the step.
 int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_blocks, int h, int hkv, int bs,
@@ -96,7 +156,7 @@ extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 1; }
+int mlb_abi_version(void) { return 2; }
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
                   const int64_t* slot_mapping, const void* k, int64_t k_stride_tok, int64_t k_stride_head,
@@ -125,23 +185,15 @@ int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blo
                      "kv_append launch");
 }
 
-int64_t mlb_plan_capacity(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int num_heads,
-                          int num_kv_heads, int block_size) {
-  if (num_kv_heads <= 0 || num_heads % num_kv_heads || block_size <= 0) return -1;
-  std::vector<Group> groups;
-  int64_t total = 0;
-  if (plan_groups(qo_indptr, seq_lens, num_seqs, -1, num_heads, num_kv_heads, block_size, groups, &total) != MLB_OK)
-    return -1;
-  int64_t cap = 0;
-  for (const Group& g : groups) cap += (g.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit;
-  return cap;
-}
-
 int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int num_seqs, int max_blocks_per_seq,
-                       int num_heads, int num_kv_heads, int block_size, int num_sms, int pages_per_unit,
-                       mlb_work_unit* units, int64_t units_capacity, int64_t* num_units, int32_t* reduce_rows,
-                       int32_t* reduce_chunks, int64_t num_tokens, int64_t* num_partial_rows) {
-  if (!qo_indptr || !seq_lens || !num_units || !num_partial_rows || num_seqs < 0)
+                       const int32_t* block_tables_host, int64_t bt_stride_host, int num_heads, int num_kv_heads,
+                       int block_size, int num_sms, int pages_per_unit, mlb_work_unit* units, int64_t units_capacity,
+                       int64_t* num_units, mlb_shared_unit* shared_units, int64_t shared_capacity,
+                       int64_t* num_shared_units, mlb_share_member* members, int64_t members_capacity,
+                       int64_t* num_members, int32_t* reduce_rows, int32_t* reduce_chunks, int64_t num_tokens,
+                       int64_t* num_partial_rows) {
+  if (!qo_indptr || !seq_lens || !num_units || !num_shared_units || !num_members || !num_partial_rows ||
+      num_seqs < 0)
     return fail(MLB_EINVAL, "plan: null pointer or negative sequence count");
   if (num_kv_heads <= 0 || num_heads <= 0 || num_heads % num_kv_heads)
     return fail(MLB_EINVAL, "plan: num_heads (%d) must be a positive multiple of num_kv_heads (%d)", num_heads,
@@ -156,42 +208,74 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
                        &total);
   if (rc != MLB_OK) return rc;
   const int tpt = tokens_per_tile(num_heads, num_kv_heads);
+  const int group_size = num_heads / num_kv_heads;
+
+  // ---- shared prefixes: planned once per block of member rows, cut into `pieces` page runs
+  std::vector<ShareSet> sets;
+  if (block_tables_host && bt_stride_host > 0)
+    sets = find_shared_prefixes(qo_indptr, seq_lens, num_seqs, block_tables_host, bt_stride_host, block_size);
+  std::vector<int> seq_group(num_seqs, -1);  // the (single) group of each decode row
+  for (size_t g = 0; g < groups.size(); ++g)
+    if (groups[g].tile == 0) seq_group[groups[g].seq] = static_cast<int>(g);
+  const int per_cta = kSharedWarps * std::max(1, 8 / group_size);  // member rows per shared CTA
+  struct SetPlan {
+    int pieces, per;
+  };
+  std::vector<SetPlan> set_plans;
+  for (const ShareSet& set : sets) {
+    const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
+    const int64_t target = static_cast<int64_t>(num_sms) * kSharedCtasPerSm;
+    int64_t pieces = std::max<int64_t>(1, (target + blocks * num_kv_heads - 1) / (blocks * num_kv_heads));
+    pieces = std::min<int64_t>(pieces, std::max(1, set.pages / kMinPagesPerUnit));
+    const int per = static_cast<int>((set.pages + pieces - 1) / pieces);
+    pieces = (set.pages + per - 1) / per;
+    set_plans.push_back({static_cast<int>(pieces), per});
+    for (int s : set.seqs) {
+      Group& g = groups[seq_group[s]];
+      g.start = set.pages;
+      g.shared_pieces = static_cast<int>(pieces);
+    }
+  }
+
+  // ---- regular units over each group's pages [start, pages)
+  int64_t rest = 0;
+  for (const Group& g : groups) rest += g.pages - g.start;
   int64_t chunk = pages_per_unit;
   if (chunk <= 0) {
     const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaveTenths / 10;
-    chunk = std::max<int64_t>(kMinPagesPerUnit, (total * num_kv_heads + target_ctas - 1) / target_ctas);
+    chunk = std::max<int64_t>(kMinPagesPerUnit, (rest * num_kv_heads + target_ctas - 1) / target_ctas);
   }
   std::vector<mlb_work_unit> out;
   out.reserve(groups.size());
+  std::vector<int64_t> base(groups.size(), -1);
   if (reduce_rows && reduce_chunks)
     for (int64_t t = 0; t < num_tokens; ++t) reduce_rows[t] = -1, reduce_chunks[t] = 0;
   int64_t rows = 0;
-  for (const Group& g : groups) {
-    // Split into runs of `per` pages; nch runs, none empty, and ceil(pages / nch) == per again (the kernel
-    // recovers a unit's run index from page_begin / per).
-    const int64_t n0 = std::min<int64_t>(kMaxSplits, std::max<int64_t>(1, (g.pages + chunk - 1) / chunk));
-    const int64_t per = std::max<int64_t>(1, (g.pages + n0 - 1) / n0);
-    const int64_t nch = std::max<int64_t>(1, (g.pages + per - 1) / per);
-    const int64_t base = nch > 1 ? rows : -1;
-    if (nch > 1) rows += nch * tpt;
+  for (size_t gi = 0; gi < groups.size(); ++gi) {
+    const Group& g = groups[gi];
+    const int64_t own = g.pages - g.start;
+    const int64_t nch = std::max<int64_t>(1, (own + chunk - 1) / chunk);
+    const int64_t per = std::max<int64_t>(1, (own + nch - 1) / nch);
+    const int64_t pieces = g.shared_pieces + nch;
+    if (pieces > 1) base[gi] = rows, rows += pieces * tpt;
     for (int64_t c = 0; c < nch; ++c) {
       mlb_work_unit u{};
       u.seq = g.seq;
-      u.tile_splits = g.tile | static_cast<int32_t>(nch << 20);
-      u.page_begin = static_cast<int32_t>(c * per);
-      u.page_end = static_cast<int32_t>(std::min<int64_t>((c + 1) * per, g.pages));
-      u.part_row = nch > 1 ? static_cast<int32_t>(base + c * tpt) : -1;
+      u.q_tile = g.tile;
+      u.page_begin = static_cast<int32_t>(g.start + c * per);
+      u.page_end = static_cast<int32_t>(std::min<int64_t>(g.start + (c + 1) * per, g.pages));
+      u.part_row = pieces > 1 ? static_cast<int32_t>(base[gi] + (g.shared_pieces + c) * tpt) : -1;
       u.q0 = qo_indptr[g.seq];
       u.num_new = qo_indptr[g.seq + 1] - qo_indptr[g.seq];
       u.seq_len = seq_lens[g.seq];
-      if (u.page_end > u.page_begin || g.pages == 0) out.push_back(u);
+      if (u.page_end > u.page_begin) out.push_back(u);
     }
     if (reduce_rows && reduce_chunks) {
       const int n = qo_indptr[g.seq + 1] - qo_indptr[g.seq];
       for (int i = 0; i < tpt && g.tile * tpt + i < n; ++i) {
         const int64_t tok = qo_indptr[g.seq] + static_cast<int64_t>(g.tile) * tpt + i;
-        reduce_rows[tok] = nch > 1 ? static_cast<int32_t>(base + i) : -1;
-        reduce_chunks[tok] = static_cast<int32_t>(nch);
+        reduce_rows[tok] = pieces > 1 ? static_cast<int32_t>(base[gi] + i) : -1;
+        reduce_chunks[tok] = static_cast<int32_t>(pieces);
       }
     }
   }
@@ -200,12 +284,41 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   std::stable_sort(out.begin(), out.end(), [](const mlb_work_unit& x, const mlb_work_unit& y) {
     return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);
   });
+
+  std::vector<mlb_shared_unit> sunits;
+  std::vector<mlb_share_member> mems;
+  for (size_t k = 0; k < sets.size(); ++k) {
+    const ShareSet& set = sets[k];
+    const int first = static_cast<int>(mems.size());
+    for (int s : set.seqs)
+      mems.push_back({s, qo_indptr[s], static_cast<int32_t>(base[seq_group[s]]), 0});
+    const int nm = static_cast<int>(set.seqs.size());
+    for (int piece = 0; piece < set_plans[k].pieces; ++piece)
+      for (int m = 0; m < nm; m += per_cta) {
+        mlb_shared_unit u{};
+        u.member_begin = first + m;
+        u.member_count = std::min(per_cta, nm - m);
+        u.page_begin = piece * set_plans[k].per;
+        u.page_end = std::min(set.pages, (piece + 1) * set_plans[k].per);
+        u.piece = piece;
+        u.table_seq = set.seqs[0];
+        sunits.push_back(u);
+      }
+  }
   *num_units = static_cast<int64_t>(out.size());
+  *num_shared_units = static_cast<int64_t>(sunits.size());
+  *num_members = static_cast<int64_t>(mems.size());
   *num_partial_rows = rows;
   if (!units) return MLB_OK;  // count only
-  if (static_cast<int64_t>(out.size()) > units_capacity)
-    return fail(MLB_ENOSPACE, "plan: %zu units > capacity %lld", out.size(), static_cast<long long>(units_capacity));
+  if (static_cast<int64_t>(out.size()) > units_capacity || static_cast<int64_t>(sunits.size()) > shared_capacity ||
+      static_cast<int64_t>(mems.size()) > members_capacity)
+    return fail(MLB_ENOSPACE, "plan: output arrays too small (%zu units, %zu shared units, %zu members)", out.size(),
+                sunits.size(), mems.size());
+  if ((!sunits.empty() && !shared_units) || (!mems.empty() && !members))
+    return fail(MLB_EINVAL, "plan: the plan has shared-prefix units but no arrays for them");
   std::copy(out.begin(), out.end(), units);
+  std::copy(sunits.begin(), sunits.end(), shared_units);
+  std::copy(mems.begin(), mems.end(), members);
   return MLB_OK;
 }
 
@@ -213,8 +326,9 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
                         int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
                         const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
-                        int64_t num_units, float* partial_o, float* partial_lse, int64_t num_partial_rows,
-                        int32_t* split_counters, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        int64_t num_units, const mlb_shared_unit* shared_units, int64_t num_shared_units,
+                        const mlb_share_member* members, float* partial_o, float* partial_lse,
+                        int64_t num_partial_rows, void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         int32_t* err_word, void* stream) {
   if (!elt_bytes(dtype)) return fail(MLB_EINVAL, "paged_attention: unknown dtype %d", dtype);
   if (block_size != mlb::kBlockSize)
@@ -227,16 +341,20 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   if (num_heads / num_kv_heads > 8)
     return fail(MLB_EUNSUPPORTED, "paged_attention: %d query heads per KV head (at most 8)",
                 num_heads / num_kv_heads);
-  if (num_units < 0 || num_seqs < 0 || num_blocks <= 0) return fail(MLB_EINVAL, "paged_attention: bad sizes");
-  if (num_units == 0) return MLB_OK;
-  if (!q || !k_cache || !v_cache || !block_tables || !seq_lens || !qo_indptr || !units || !out)
+  if (num_units < 0 || num_shared_units < 0 || num_seqs < 0 || num_blocks <= 0)
+    return fail(MLB_EINVAL, "paged_attention: bad sizes");
+  if (num_units == 0 && num_shared_units == 0) return MLB_OK;
+  if (!q || !k_cache || !v_cache || !block_tables || !seq_lens || !qo_indptr || (num_units && !units) || !out)
     return fail(MLB_EINVAL, "paged_attention: null pointer");
+  if (num_shared_units > 0 && (!shared_units || !members || dtype == MLB_F32))
+    return fail(MLB_EINVAL, "paged_attention: shared-prefix units need their arrays and a 16-bit pool");
   if (num_partial_rows > 0 && (!partial_o || !partial_lse))
     return fail(MLB_EINVAL, "paged_attention: the plan has %lld partial rows but no workspace",
                 static_cast<long long>(num_partial_rows));
   if (!aligned(k_cache, 16) || !aligned(v_cache, 16))
     return fail(MLB_EINVAL, "paged_attention: pools must be 16-byte aligned");
-  if (num_units * num_kv_heads > INT32_MAX) return fail(MLB_EINVAL, "paged_attention: grid too large");
+  if (num_units * num_kv_heads > INT32_MAX || num_shared_units * num_kv_heads > INT32_MAX)
+    return fail(MLB_EINVAL, "paged_attention: grid too large");
   mlb::AttnArgs a{};
   a.q = static_cast<const char*>(q);
   a.q_st = q_stride_tok;
@@ -254,15 +372,22 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   a.seq_lens = seq_lens;
   a.qo = qo_indptr;
   a.units = units;
+  a.shared_units = shared_units;
+  a.members = members;
   a.part_o = partial_o;
   a.part_lse = partial_lse;
-  a.counters = split_counters;
   a.out = static_cast<char*>(out);
   a.o_st = out_stride_tok;
   a.o_sh = out_stride_head;
   a.err = err_word;
-  return cuda_status(mlb::launch_paged_attention(a, dtype, head_dim, num_units, static_cast<cudaStream_t>(stream)),
-                     "paged_attention launch");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (num_shared_units > 0) {
+    const int rc = cuda_status(mlb::launch_shared_prefix_attention(a, dtype, head_dim, num_shared_units, st),
+                               "shared-prefix attention launch");
+    if (rc != MLB_OK) return rc;
+  }
+  if (num_units == 0) return MLB_OK;
+  return cuda_status(mlb::launch_paged_attention(a, dtype, head_dim, num_units, st), "paged_attention launch");
 }
 
 int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,

@@ -15,9 +15,13 @@
 //   Per page and warp: S^T[16 tok x 8 col] = K[16 x Dh] . Q^T (m16n8k16 MMAs, fp32 accumulate),
 //   online softmax per column (exp2 domain), P^T goes back to a B fragment with movmatrix.trans, and
 //   O^T[Dh x 8] += V^T . P^T.  The warps' (m, l, O) are merged through shared memory at the end.
-//   A sequence split over several units writes normalised fp32 partial rows; the last CTA of the split
-//   group to finish merges them (in-kernel split-K reduction), or K2b does when no counters are given.
+//   A sequence split over several units writes normalised fp32 partial rows that K2b merges.
+// Shared prefixes (K2s): pages that many decode rows' tables share (prefix-cache hits) are attended once per
+//   block of up to 16 rows: one CTA loads each shared page into shared memory once and its 8 warps apply it
+//   to 2 rows x 4 query heads each, writing partial rows that K2b merges with the rows' private pages.
 // f32 pools take a CUDA-core path with the same decomposition (fp32 accuracy, 1e-5).
+#include <climits>
+
 #include "attn_args.cuh"
 
 namespace mlb {
@@ -38,8 +42,6 @@ constexpr float kNegInf = -__builtin_huge_valf();
 
 struct UnitInfo {
   int seq, q0, n_new, L, t0, ncols, pb, pe, part_row;
-  int nsplit;      // units the query tile's pages are split into
-  int split_base;  // first partial row of the tile's split group (valid when part_row >= 0)
 };
 
 __device__ __forceinline__ UnitInfo unit_info(const AttnArgs& a, int unit_idx) {
@@ -47,21 +49,14 @@ __device__ __forceinline__ UnitInfo unit_info(const AttnArgs& a, int unit_idx) {
   const int4 x = __ldg(rec), y = __ldg(rec + 1);
   UnitInfo r;
   r.seq = x.x;
-  const int tile = x.y & 0xFFFFF;
-  r.nsplit = static_cast<int>(static_cast<uint32_t>(x.y) >> 20);
+  r.t0 = x.y * a.tile_tokens;
   r.pb = x.z;
   r.pe = x.w;
   r.part_row = y.x;
   r.q0 = y.y;
   r.n_new = y.z;
   r.L = y.w;
-  r.t0 = tile * a.tile_tokens;
-  const int ntok = min(a.tile_tokens, r.n_new - r.t0);
-  r.ncols = ntok * a.group;
-  // The planner split the tile's pages into nsplit runs of `per` pages; this unit is run pb / per.
-  const int pages = (r.L - r.n_new + r.t0 + ntok + kBlockSize - 1) / kBlockSize;
-  const int per = (pages + r.nsplit - 1) / max(r.nsplit, 1);
-  r.split_base = r.part_row - (per > 0 ? r.pb / per : 0) * a.tile_tokens;
+  r.ncols = min(a.tile_tokens, r.n_new - r.t0) * a.group;
   return r;
 }
 
@@ -106,40 +101,59 @@ __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInf
   }
 }
 
-// Split-K merge done by the last CTA of a split group (no reduction launch): every CTA of the group has
-// written its normalised partial row and its log2-sum-exp; the CTA whose arrival completes the group's
-// counter combines them into `out` and returns the counter to zero for the next launch.
-template <int DH, int OUT_DT>
-__device__ __forceinline__ void merge_split_group(const AttnArgs& a, const UnitInfo& ui, int kvh) {
-  __shared__ int s_last;
-  __threadfence();  // this CTA's partial rows are visible device-wide before it is counted
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t* cnt = a.counters + static_cast<int64_t>(ui.split_base / a.tile_tokens) * a.hkv + kvh;
-    const int prev = atomicAdd(cnt, 1);
-    s_last = prev == ui.nsplit - 1;
-    if (s_last) *cnt = 0;  // every other CTA of the group has already arrived
+// One page of one KV head against up to 8 query columns (one warp): S^T = K . Q^T on m16n8k16 tensor-core
+// tiles, the online-softmax update of the columns' running max m / sum l / output O^T, and O^T += V^T . P^T.
+// kaddr / vaddr: this lane's ldmatrix addresses in the page's K and V tiles; tk0: token index of this lane's
+// first S^T row (the second is tk0 + 8); lim0 / lim1: exclusive key limits of the lane's two columns.
+template <int DT, int DH>
+__device__ __forceinline__ void attend_page(uint32_t kaddr, uint32_t vaddr, const uint32_t (&qb)[DH / 16][2], int tk0,
+                                            int lim0, int lim1, float sl2, float (&o)[DH / 16][4], float& m0,
+                                            float& m1, float& l0, float& l1) {
+  constexpr int KSTEPS = DH / 16;
+  // S^T = K . Q^T, two accumulators to halve the dependent-MMA chain
+  float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int ks = 0; ks < KSTEPS; ++ks) {
+    uint32_t x0, x1, x2, x3;
+    ldsm_x4(kaddr + ks * 32, x0, x1, x2, x3);
+    mma16816<DT>((ks & 1) ? sb : sa, x0, x1, x2, x3, qb[ks][0], qb[ks][1]);
   }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < ui.ncols * DH; idx += blockDim.x) {
-    const int j = idx / DH, d = idx % DH;
-    const int t = j / a.group, head = kvh * a.group + j % a.group;
-    float M = kNegInf;
-    for (int c = 0; c < ui.nsplit; ++c)
-      M = fmaxf(M, __ldcg(a.part_lse + (static_cast<int64_t>(ui.split_base + c * a.tile_tokens + t)) * a.h + head));
-    float lsum = 0.f, acc = 0.f;
-    for (int c = 0; c < ui.nsplit; ++c) {
-      const int64_t row = ui.split_base + c * a.tile_tokens + t;
-      const float lse = __ldcg(a.part_lse + row * a.h + head);
-      const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
-      lsum += w;
-      acc = fmaf(w, __ldcg(a.part_o + (row * a.h + head) * DH + d), acc);
-    }
-    char* o = a.out + ((static_cast<int64_t>(ui.q0 + ui.t0 + t) * a.o_st + static_cast<int64_t>(head) * a.o_sh + d) *
-                       Elt<OUT_DT>::bytes);
-    store_f32<OUT_DT>(o, lsum > 0.f ? acc / lsum : 0.f);
+  const int tk1 = tk0 + 8;
+  const float x0 = tk0 < lim0 ? (sa[0] + sb[0]) * sl2 : kNegInf;
+  const float x1 = tk0 < lim1 ? (sa[1] + sb[1]) * sl2 : kNegInf;
+  const float x2 = tk1 < lim0 ? (sa[2] + sb[2]) * sl2 : kNegInf;
+  const float x3 = tk1 < lim1 ? (sa[3] + sb[3]) * sl2 : kNegInf;
+  // online softmax per column; columns j0, j1 are shared by the 8 lanes with equal lane % 4
+  float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+  }
+  const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+  const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
+  const float al0 = fast_exp2(m0 - b0), al1 = fast_exp2(m1 - b1);
+  const float p0 = fast_exp2(x0 - b0), p2 = fast_exp2(x2 - b0);
+  const float p1 = fast_exp2(x1 - b1), p3 = fast_exp2(x3 - b1);
+  l0 = l0 * al0 + p0 + p2;
+  l1 = l1 * al1 + p1 + p3;
+  m0 = mn0;
+  m1 = mn1;
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) {
+    o[mt][0] *= al0;
+    o[mt][1] *= al1;
+    o[mt][2] *= al0;
+    o[mt][3] *= al1;
+  }
+  // P (C layout: token rows, column pairs) -> P^T as the B operand (token = k, column = n)
+  const uint32_t pb0 = movm_t(pack2<DT>(p0, p1));
+  const uint32_t pb1 = movm_t(pack2<DT>(p2, p3));
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) {
+    uint32_t y0, y1, y2, y3;
+    ldsm_x4_t(vaddr + mt * 32, y0, y1, y2, y3);
+    mma16816<DT>(o[mt], y0, y1, y2, y3, pb0, pb1);
   }
 }
 
@@ -266,54 +280,8 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
         __syncwarp();
       }
 
-      // S^T = K . Q^T, two accumulators to halve the dependent-MMA chain
-      float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t kaddr = ring_u32 + s * STAGE + k_off;
-#pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        uint32_t x0, x1, x2, x3;
-        ldsm_x4(kaddr + ks * 32, x0, x1, x2, x3);
-        mma16816<DT>((ks & 1) ? sb : sa, x0, x1, x2, x3, qb[ks][0], qb[ks][1]);
-      }
-      const int tk0 = tok_base + r0, tk1 = tk0 + 8;
-      const float x0 = tk0 < lim0 ? (sa[0] + sb[0]) * a.sl2 : kNegInf;
-      const float x1 = tk0 < lim1 ? (sa[1] + sb[1]) * a.sl2 : kNegInf;
-      const float x2 = tk1 < lim0 ? (sa[2] + sb[2]) * a.sl2 : kNegInf;
-      const float x3 = tk1 < lim1 ? (sa[3] + sb[3]) * a.sl2 : kNegInf;
-
-      // online softmax per column; columns j0, j1 are shared by the 8 lanes with equal lane % 4
-      float mx0 = fmaxf(x0, x2), mx1 = fmaxf(x1, x3);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-      }
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float b0 = mn0 == kNegInf ? 0.f : mn0, b1 = mn1 == kNegInf ? 0.f : mn1;
-      const float al0 = fast_exp2(m0 - b0), al1 = fast_exp2(m1 - b1);
-      const float p0 = fast_exp2(x0 - b0), p2 = fast_exp2(x2 - b0);
-      const float p1 = fast_exp2(x1 - b1), p3 = fast_exp2(x3 - b1);
-      l0 = l0 * al0 + p0 + p2;
-      l1 = l1 * al1 + p1 + p3;
-      m0 = mn0;
-      m1 = mn1;
-#pragma unroll
-      for (int mt = 0; mt < DH / 16; ++mt) {
-        o[mt][0] *= al0;
-        o[mt][1] *= al1;
-        o[mt][2] *= al0;
-        o[mt][3] *= al1;
-      }
-      // P (C layout: token rows, column pairs) -> P^T as the B operand (token = k, column = n)
-      const uint32_t pb0 = movm_t(pack2<DT>(p0, p1));
-      const uint32_t pb1 = movm_t(pack2<DT>(p2, p3));
-      const uint32_t vaddr = ring_u32 + s * STAGE + TILE + v_off;
-#pragma unroll
-      for (int mt = 0; mt < DH / 16; ++mt) {
-        uint32_t y0, y1, y2, y3;
-        ldsm_x4_t(vaddr + mt * 32, y0, y1, y2, y3);
-        mma16816<DT>(o[mt], y0, y1, y2, y3, pb0, pb1);
-      }
+      attend_page<DT, DH>(ring_u32 + s * STAGE + k_off, ring_u32 + s * STAGE + TILE + v_off, qb, tok_base + r0,
+                          lim0, lim1, a.sl2, o, m0, m1, l0, l1);
     }
     __syncwarp();  // every lane is done with slot s before the next iteration refills it
   }
@@ -354,7 +322,135 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
     sl_w[w] = sm_w[w] + 8;
   }
   merge_and_store<DH, DT, NW>(a, ui, kvh, so_w, sm_w, sl_w);
-  if (ui.part_row >= 0 && a.counters) merge_split_group<DH, DT>(a, ui, kvh);
+}
+
+// ------------------------------------------------------------------ shared prefixes (K2s)
+
+constexpr int kSharedWarps = 8;   // warps per shared-prefix CTA (the planner sizes member blocks with it)
+constexpr int kSharedStages = 4;  // CTA-wide ring slots: 3 pages in flight while one is read
+
+// One CTA = (shared unit, KV head).  Every page of the unit's range is loaded once into a CTA-wide ring and
+// read by all warps; warp w owns member rows [w * mpw, (w + 1) * mpw) of the unit (mpw = 8 / group), i.e.
+// up to 8 (row, query head) columns.  Shared pages hold only tokens every member sees (no mask).  Each warp
+// ends with normalised partial rows of its members for the split-K reduction.
+template <int DT, int DH>
+__global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnArgs a) {
+  constexpr int NW = kSharedWarps, S = kSharedStages;
+  constexpr int ROWB = DH * 2 + 16;
+  constexpr int TILE = 16 * ROWB;
+  constexpr int STAGE = 2 * TILE;
+  constexpr int KSTEPS = DH / 16;
+  constexpr int CH_ROW = DH * 2 / 16;
+  constexpr int CHUNKS = 2 * 16 * CH_ROW;  // 16-byte chunks of one page (K and V rows of one head)
+  extern __shared__ __align__(128) uint8_t smem[];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x % a.hkv;
+  const int4* rec = reinterpret_cast<const int4*>(a.shared_units + blockIdx.x / a.hkv);
+  const int4 x = __ldg(rec), y = __ldg(rec + 1);
+  const int mb = x.x, mc = x.y, pb = x.z, pe = x.w, piece = y.x, tseq = y.y;
+  const int npages = pe - pb;
+  const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
+  const int64_t row_stride = static_cast<int64_t>(a.hkv) * DH * 2;
+  const int mpw = a.group >= 8 ? 1 : 8 / a.group;  // member rows per warp
+  const int wm = warp * mpw;
+  const int ncols = max(0, min(mpw, mc - wm)) * a.group;
+
+  uint32_t bad_mask = 0;
+  auto issue = [&](int j) {
+    if (j < npages) {
+      const int bid = __ldg(table + pb + j);
+      const int s = j % S;
+      const bool ok = bid >= 0 && bid < a.num_blocks;
+      bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
+      if (!ok) {
+        if (threadIdx.x == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+      } else {
+        const int64_t page_off = (static_cast<int64_t>(bid) * kBlockSize * a.hkv + kvh) * (DH * 2);
+        uint8_t* slot = smem + s * STAGE;
+        for (int e = threadIdx.x; e < CHUNKS; e += NW * 32) {
+          const int kv = e / (16 * CH_ROW), row = (e / CH_ROW) % 16, ch = e % CH_ROW;
+          cp_async16(slot + kv * TILE + row * ROWB + ch * 16,
+                     (kv ? a.v_cache : a.k_cache) + page_off + row * row_stride + ch * 16);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int j = 0; j < S - 1; ++j) issue(j);
+
+  // Q^T fragments: column n = lane / 4 is member wm + n / group (its one new token), head kvh * group + n % group
+  uint32_t qb[KSTEPS][2];
+  {
+    const int n = lane >> 2, c2 = (lane & 3) * 2;
+    const bool live = n < ncols;
+    const int tok = live ? __ldg(&a.members[mb + wm + n / a.group].q0) : 0;
+    const int head = kvh * a.group + (live ? n % a.group : 0);
+    const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
+                           static_cast<int64_t>(head) * a.q_sh;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks) {
+      const int d = ks * 16 + c2;
+      qb[ks][0] = live ? static_cast<uint32_t>(__ldg(qrow + d)) | (static_cast<uint32_t>(__ldg(qrow + d + 1)) << 16)
+                       : 0u;
+      qb[ks][1] = live ? static_cast<uint32_t>(__ldg(qrow + d + 8)) | (static_cast<uint32_t>(__ldg(qrow + d + 9)) << 16)
+                       : 0u;
+    }
+  }
+  const int r0 = lane >> 2, j0 = (lane & 3) * 2, j1 = j0 + 1;
+  const bool live0 = j0 < ncols, live1 = j1 < ncols;
+  const int lim0 = live0 ? INT_MAX : 0, lim1 = live1 ? INT_MAX : 0;  // every shared token is visible
+  float o[DH / 16][4];
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+  const uint32_t base_u32 = smem_u32(smem);
+  const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
+  const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
+
+  for (int i = 0; i < npages; ++i) {
+    issue(i + S - 1);            // refill the slot page i - 1 used (every warp left it at the last barrier)
+    cp_async_wait<S - 1>();      // this thread's copies of page i have landed
+    __syncthreads();             // ... and every other thread's
+    const int s = i % S;
+    if (ncols > 0 && !((bad_mask >> s) & 1u))
+      attend_page<DT, DH>(base_u32 + s * STAGE + k_off, base_u32 + s * STAGE + TILE + v_off, qb, 0, lim0, lim1,
+                          a.sl2, o, m0, m1, l0, l1);
+    __syncthreads();  // every warp is done with slot s before it is refilled
+  }
+  cp_async_wait<0>();
+
+#pragma unroll
+  for (int off = 4; off < 32; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  // partial row of member m for head h: members[m].part_base + piece * tokens_per_tile (its one token)
+  int64_t slot0 = 0, slot1 = 0;
+  if (live0)
+    slot0 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j0 / a.group].part_base)) +
+             static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j0 % a.group;
+  if (live1)
+    slot1 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j1 / a.group].part_base)) +
+             static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j1 % a.group;
+#pragma unroll
+  for (int mt = 0; mt < DH / 16; ++mt) {
+    const int d = mt * 16 + r0;
+    if (live0) {
+      a.part_o[slot0 * DH + d] = o[mt][0] * inv0;
+      a.part_o[slot0 * DH + d + 8] = o[mt][2] * inv0;
+    }
+    if (live1) {
+      a.part_o[slot1 * DH + d] = o[mt][1] * inv1;
+      a.part_o[slot1 * DH + d + 8] = o[mt][3] * inv1;
+    }
+  }
+  if (r0 == 0) {
+    if (live0) a.part_lse[slot0] = l0 > 0.f ? m0 + log2f(l0) : kNegInf;
+    if (live1) a.part_lse[slot1] = l1 > 0.f ? m1 + log2f(l1) : kNegInf;
+  }
 }
 
 // ------------------------------------------------------------------ f32 pools: CUDA cores
@@ -485,7 +581,6 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a)
     sl_w[w] = sm_w[w] + 8;
   }
   merge_and_store<DH, MLB_F32, kWarps>(a, ui, kvh, so_w, sm_w, sl_w);
-  if (ui.part_row >= 0 && a.counters) merge_split_group<DH, MLB_F32>(a, ui, kvh);
 }
 
 // ------------------------------------------------------------------ split-K reduction
@@ -562,7 +657,31 @@ cudaError_t launch_f32(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+template <int DT, int DH>
+cudaError_t launch_shared(const AttnArgs& a, int64_t units, cudaStream_t s) {
+  constexpr int bytes = kSharedStages * 2 * 16 * (DH * 2 + 16);
+  static unsigned long long done = 0;
+  auto k = shared_prefix_kernel<DT, DH>;
+  cudaError_t e = set_smem(k, bytes, done);
+  if (e != cudaSuccess) return e;
+  k<<<static_cast<unsigned>(units * a.hkv), kSharedWarps * 32, bytes, s>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace
+
+cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
+  if (dtype == MLB_BF16) {
+    if (dh == 64) return launch_shared<MLB_BF16, 64>(a, num_units, s);
+    if (dh == 128) return launch_shared<MLB_BF16, 128>(a, num_units, s);
+    if (dh == 256) return launch_shared<MLB_BF16, 256>(a, num_units, s);
+  } else if (dtype == MLB_F16) {
+    if (dh == 64) return launch_shared<MLB_F16, 64>(a, num_units, s);
+    if (dh == 128) return launch_shared<MLB_F16, 128>(a, num_units, s);
+    if (dh == 256) return launch_shared<MLB_F16, 256>(a, num_units, s);
+  }
+  return cudaErrorInvalidValue;
+}
 
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
   const int64_t ctas = num_units * a.hkv;

@@ -16,7 +16,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import WORK_UNIT_INT32S, check, lib
+from ._lib import MEMBER_INT32S, SHARED_UNIT_INT32S, WORK_UNIT_INT32S, check, lib
 
 DTYPE_CODE = {torch.float32: _lib.MLB_F32, torch.float16: _lib.MLB_F16, torch.bfloat16: _lib.MLB_BF16}
 BLOCK_SIZE = 16
@@ -92,6 +92,9 @@ class AttentionPlan:
 
     units: torch.Tensor  # device int32 [num_units, 8]: mlb_work_unit records
     num_units: int
+    shared_units: torch.Tensor  # device int32 [num_shared_units, 8]: mlb_shared_unit records (may be empty)
+    num_shared_units: int
+    members: torch.Tensor  # device int32 [num_members, 4]: mlb_share_member records
     reduce_rows: torch.Tensor  # device int32 [N]
     reduce_chunks: torch.Tensor  # device int32 [N]
     num_partial_rows: int
@@ -100,7 +103,10 @@ class AttentionPlan:
     num_kv_heads: int
     num_tokens: int
     units_host: np.ndarray  # the same records on the host (inspection and tests)
-    reduce_chunks_host: np.ndarray  # [N] splits per token on the host
+    shared_host: np.ndarray
+    members_host: np.ndarray
+    reduce_rows_host: np.ndarray
+    reduce_chunks_host: np.ndarray  # [N] pieces per token on the host
 
 
 def _i32(a) -> np.ndarray:
@@ -109,11 +115,13 @@ def _i32(a) -> np.ndarray:
 
 def plan_attention(qo_indptr: list[int], seq_lens: list[int], max_blocks: int, num_heads: int, num_kv_heads: int,
                    device: torch.device | str, block_size: int = BLOCK_SIZE, num_sms: int | None = None,
-                   pages_per_unit: int = 0) -> AttentionPlan:
+                   pages_per_unit: int = 0, block_tables_host: np.ndarray | None = None) -> AttentionPlan:
     """Split the step into units (host work, like FlashInfer's plan(); flashinfer_backend.py:48-64).
 
     qo_indptr / seq_lens are the host lists AttentionMetadata keeps (metadata.py:39-40), so planning
-    needs no device round trip.  The plan is copied to the device in one transfer.
+    needs no device round trip.  With `block_tables_host` (int32 [S, W]) decode rows that share leading
+    blocks (prefix-cache hits) are planned as shared-prefix units (16-bit pools only).  The plan is copied
+    to the device in one transfer.
     """
     device = torch.device(device)
     qo, lens = _i32(qo_indptr), _i32(seq_lens)
@@ -123,46 +131,44 @@ def plan_attention(qo_indptr: list[int], seq_lens: list[int], max_blocks: int, n
     n_tok = int(qo[-1]) if s else 0
     if num_sms is None:
         num_sms = torch.cuda.get_device_properties(device).multi_processor_count if device.type == "cuda" else 148
+    tables = None if block_tables_host is None else _i32(block_tables_host)
+    if tables is not None and (tables.ndim != 2 or tables.shape[0] != s):
+        raise ValueError(f"plan: block_tables_host must be [{s}, W], got {tables.shape}")
     L = lib()
-    cap = L.mlb_plan_capacity(qo.ctypes.data, lens.ctypes.data, s, num_heads, num_kv_heads, block_size)
-    if cap < 0:
-        cap = 0  # invalid input: the planner itself reports why
-    units = np.zeros((max(cap, 1), WORK_UNIT_INT32S), dtype=np.int32)
+    nu, ns, nm, npart = (ctypes.c_int64(0) for _ in range(4))
+    head = (qo.ctypes.data, lens.ctypes.data, s, max_blocks, None if tables is None else tables.ctypes.data,
+            0 if tables is None else tables.shape[1], num_heads, num_kv_heads, block_size, num_sms, pages_per_unit)
+    check(L.mlb_plan_attention(*head, None, 0, ctypes.byref(nu), None, 0, ctypes.byref(ns), None, 0,
+                               ctypes.byref(nm), None, None, n_tok, ctypes.byref(npart)), "plan_attention")
+    units = np.zeros((max(nu.value, 1), WORK_UNIT_INT32S), dtype=np.int32)
+    shared = np.zeros((max(ns.value, 1), SHARED_UNIT_INT32S), dtype=np.int32)
+    members = np.zeros((max(nm.value, 1), MEMBER_INT32S), dtype=np.int32)
     rows = np.empty(max(n_tok, 1), dtype=np.int32)
     chunks = np.empty(max(n_tok, 1), dtype=np.int32)
-    nu, npart = ctypes.c_int64(0), ctypes.c_int64(0)
-
-    def run() -> int:
-        return L.mlb_plan_attention(qo.ctypes.data, lens.ctypes.data, s, max_blocks, num_heads, num_kv_heads,
-                                    block_size, num_sms, pages_per_unit, units.ctypes.data, units.shape[0],
-                                    ctypes.byref(nu), rows.ctypes.data, chunks.ctypes.data, n_tok,
-                                    ctypes.byref(npart))
-
-    rc = run()
-    if rc == _lib.MLB_ENOSPACE:  # an explicit pages_per_unit below the capacity estimate's minimum
-        units = np.zeros((nu.value, WORK_UNIT_INT32S), dtype=np.int32)
-        rc = run()
-    check(rc, "plan_attention")
-    n_units = nu.value
+    check(L.mlb_plan_attention(*head, units.ctypes.data, units.shape[0], ctypes.byref(nu), shared.ctypes.data,
+                               shared.shape[0], ctypes.byref(ns), members.ctypes.data, members.shape[0],
+                               ctypes.byref(nm), rows.ctypes.data, chunks.ctypes.data, n_tok, ctypes.byref(npart)),
+          "plan_attention")
+    u, sh, m = nu.value, ns.value, nm.value
     # one host -> device copy for the whole plan
-    packed = np.concatenate([units[:n_units].reshape(-1), rows[:n_tok], chunks[:n_tok]])
-    host = torch.from_numpy(packed)
+    parts = [units[:u].reshape(-1), shared[:sh].reshape(-1), members[:m].reshape(-1), rows[:n_tok], chunks[:n_tok]]
+    offs = np.cumsum([0] + [p.size for p in parts])
+    host = torch.from_numpy(np.concatenate(parts))
     dev = host.pin_memory().to(device, non_blocking=True) if device.type == "cuda" else host.clone()
-    u = n_units * WORK_UNIT_INT32S
-    plan = AttentionPlan(dev[:u].view(n_units, WORK_UNIT_INT32S), n_units, dev[u:u + n_tok],
-                         dev[u + n_tok:u + 2 * n_tok], npart.value, max(1, 8 // (num_heads // num_kv_heads)),
-                         num_heads, num_kv_heads, n_tok, units[:n_units].copy(), chunks[:n_tok].copy())
-    return plan
+    seg = [dev[offs[i]:offs[i + 1]] for i in range(len(parts))]
+    return AttentionPlan(seg[0].view(u, WORK_UNIT_INT32S), u, seg[1].view(sh, SHARED_UNIT_INT32S), sh,
+                         seg[2].view(m, MEMBER_INT32S), seg[3], seg[4], npart.value,
+                         max(1, 8 // (num_heads // num_kv_heads)), num_heads, num_kv_heads, n_tok,
+                         units[:u].copy(), shared[:sh].copy(), members[:m].copy(), rows[:n_tok].copy(),
+                         chunks[:n_tok].copy())
 
 
 class Workspace:
-    """Split-K scratch, grown on demand and reused across calls: fp32 partial rows, their log-sum-exp, and the
-    int32 split-group counters of the in-kernel merge (allocated zeroed; the kernel leaves them zero)."""
+    """Split-K scratch (fp32 partial rows + their log-sum-exp), grown on demand and reused across calls."""
 
     def __init__(self) -> None:
         self._o: torch.Tensor | None = None
         self._lse: torch.Tensor | None = None
-        self._cnt: torch.Tensor | None = None
 
     def get(self, rows: int, heads: int, dh: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
         need_o, need_l = rows * heads * dh, rows * heads
@@ -172,38 +178,31 @@ class Workspace:
             self._lse = torch.empty(max(need_l, 1), dtype=torch.float32, device=device)
         return self._o, self._lse
 
-    def counters(self, plan: AttentionPlan, device: torch.device) -> torch.Tensor:
-        need = -(-plan.num_partial_rows // plan.tokens_per_tile) * plan.num_kv_heads
-        if self._cnt is None or self._cnt.device != device or self._cnt.numel() < need:
-            self._cnt = torch.zeros(max(need, 1), dtype=torch.int32, device=device)
-        return self._cnt
-
 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan,
                     workspace: Workspace | None = None, out: torch.Tensor | None = None, scale: float | None = None,
-                    err: torch.Tensor | None = None, fused_reduce: bool = False) -> torch.Tensor:
+                    err: torch.Tensor | None = None) -> torch.Tensor:
     """paged_attention (paged_torch_ref.py:40-74) on the GPU: q [N, H, Dh] -> [N, H, Dh] in q's dtype.
 
     block_tables int32 [S, W], seq_lens int32 [S], qo_indptr int32 [S + 1] are AttentionMetadata's
     device tensors (block_tables_i32, seq_lens_i32, qo_indptr).  The pools must already hold this
-    step's k/v (kv_append first).  Split sequences are merged by the split-K reduction kernel (measured
-    faster on B200), or with fused_reduce=True by the last CTA of each split group (one launch fewer).
+    step's k/v (kv_append first).  Launches the shared-prefix and per-sequence attention kernels, then
+    the split-K reduction when the plan split any sequence.
     """
     workspace = workspace or Workspace()
     out = attention_partials(q, k_cache, v_cache, block_tables, seq_lens, qo_indptr, plan, workspace, out, scale,
-                             err, fused_reduce)
-    if not fused_reduce:
-        splitk_reduce(plan, workspace, out)
+                             err)
+    splitk_reduce(plan, workspace, out)
     return out
 
 
 def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                        seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan, workspace: Workspace,
                        out: torch.Tensor | None = None, scale: float | None = None,
-                       err: torch.Tensor | None = None, fused_reduce: bool = False) -> torch.Tensor:
-    """The attention kernel (K2a).  Unsplit sequences are final in `out`; split ones are merged in-kernel
-    (fused_reduce) or left as fp32 partial rows in `workspace` for `splitk_reduce`."""
+                       err: torch.Tensor | None = None) -> torch.Tensor:
+    """The attention kernels (K2s, K2a): unsplit sequences are final in `out`; split ones leave fp32
+    partial rows in `workspace` for `splitk_reduce`."""
     _check_pool(k_cache, "paged_attention")
     _check_pool(v_cache, "paged_attention")
     nb, bs, hkv, dh = k_cache.shape
@@ -221,20 +220,19 @@ def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
         out = torch.empty_like(q)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1:
         raise ValueError("paged_attention: out must match q")
-    if n == 0 or plan.num_units == 0:
+    if n == 0 or plan.num_units + plan.num_shared_units == 0:
         return out
     scale = 1.0 / math.sqrt(dh) if scale is None else float(scale)
-    po = plse = cnt = None
+    po = plse = None
     if plan.num_partial_rows:
         po, plse = workspace.get(plan.num_partial_rows, h, dh, q.device)
-        if fused_reduce:
-            cnt = workspace.counters(plan, q.device)
     rc = lib().mlb_paged_attention(q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
                                    _code(q, "paged_attention"), nb, bs, h, hkv, dh, scale, block_tables.data_ptr(),
                                    block_tables.stride(0), seq_lens.data_ptr(), qo_indptr.data_ptr(),
-                                   seq_lens.shape[0], plan.units.data_ptr(), plan.num_units, _ptr(po), _ptr(plse),
-                                   plan.num_partial_rows, _ptr(cnt), out.data_ptr(), out.stride(0), out.stride(1),
-                                   _ptr(err), _stream(q.device))
+                                   seq_lens.shape[0], plan.units.data_ptr(), plan.num_units,
+                                   plan.shared_units.data_ptr(), plan.num_shared_units, plan.members.data_ptr(),
+                                   _ptr(po), _ptr(plse), plan.num_partial_rows, out.data_ptr(), out.stride(0),
+                                   out.stride(1), _ptr(err), _stream(q.device))
     check(rc, "paged_attention")
     return out
 

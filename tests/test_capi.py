@@ -37,11 +37,11 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == 1
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 2
 
 
-def test_work_unit_layout_matches_header(L):
-    assert ctypes.sizeof(L.WorkUnit) == 32 and L.WORK_UNIT_INT32S == 8
+def test_plan_record_layouts_match_header(L):
+    assert ctypes.sizeof(L.WorkUnit) == 32 and ctypes.sizeof(L.SharedUnit) == 32 and ctypes.sizeof(L.ShareMember) == 16
 
 
 def test_invalid_arguments_return_status_without_launching(L):
@@ -52,23 +52,19 @@ def test_invalid_arguments_return_status_without_launching(L):
     rc = lib.mlb_kv_append(None, None, 2, 10, 16, None, None, 0, 0, None, 0, 0, 2, 1, 2, 64, None, None)
     assert rc == L.MLB_EINVAL and "null" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 32, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "block_size" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 16, 32, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "query heads per KV head" in L.last_error()
     rc = lib.mlb_block_copy(None, 2, 10, 100, None, None, 3, None, None)
     assert rc == L.MLB_EUNSUPPORTED
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 8, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, None, 0, None, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
     with pytest.raises(ValueError, match="block_size"):  # status codes become the reference's ValueError
         L.check(rc, "paged_attention")
     # zero work is a successful no-op
     assert lib.mlb_block_copy(None, 0, 10, 64, None, None, 0, None, None) == L.MLB_OK
-
-
-def _first_token(qo, seq, tile, tpt):
-    return qo[seq] + tile * tpt
 
 
 def plan(mlb, steps, h=32, hkv=8, ppu=0, sms=148, width=None):
@@ -95,9 +91,8 @@ def test_planner_covers_every_page_once(mlb, seed, h, hkv, ppu):
     assert (np.diff(sizes) <= 0).all(), "largest units first"
     # per (seq, tile) the units tile the pages the tile's last query can see, exactly once
     cover: dict[tuple[int, int], list[tuple[int, int, int]]] = {}
-    for seq, tile_splits, pb, pe, prow, *_ in u.tolist():
-        cover.setdefault((seq, tile_splits & 0xFFFFF), []).append((pb, pe, prow))
-        assert tile_splits >> 20 == p.reduce_chunks_host[_first_token(qo, seq, tile_splits & 0xFFFFF, tpt)]
+    for seq, tile, pb, pe, prow, *_ in u.tolist():
+        cover.setdefault((seq, tile), []).append((pb, pe, prow))
     for s, (cached, new) in enumerate(steps):
         for t in range(-(-new // tpt)):
             last = min((t + 1) * tpt, new) - 1
@@ -131,3 +126,56 @@ def test_planner_auto_split_targets_waves_of_ctas(mlb):
     ctas = p.num_units * 8
     assert 148 * 3 <= ctas <= 148 * 3 * 4
     assert p.num_partial_rows > 0
+
+
+def test_planner_finds_shared_prefixes(mlb):
+    """Decode rows whose tables start with the same blocks get shared-prefix units over those pages; their
+    own units start after the prefix, and the pieces line up with the partial rows."""
+    r = random.Random(1)
+    shared = list(range(1000, 1040))  # 40 shared full blocks
+    steps, tables = [], []
+    for i in range(20):  # 20 rows share the prefix; suffixes differ
+        ctx = 40 * 16 + r.randint(1, 300)
+        steps.append((ctx - 1, 1))
+        tables.append(shared + [5000 + 100 * i + j for j in range(-(-ctx // 16) - 40)])
+    for i in range(3):  # 3 rows share only their first block with them: not enough to count
+        steps.append((700, 1))
+        tables.append([1000] + [8000 + 100 * i + j for j in range(-(-701 // 16) - 1)])
+    steps.append((500, 7))  # a multi-token row is never a member
+    tables.append(shared + [9000 + j for j in range(-(-507 // 16) - 40)])
+    width = max(len(t) for t in tables)
+    host = np.zeros((len(tables), width), dtype=np.int32)
+    for i, t in enumerate(tables):
+        host[i, :len(t)] = t
+    qo = [0]
+    for _, n in steps:
+        qo.append(qo[-1] + n)
+    lens = [c + n for c, n in steps]
+    p = mlb.plan_attention(qo, lens, width, 32, 8, "cpu", num_sms=148, block_tables_host=host)
+    assert p.num_shared_units > 0
+    members = p.members_host
+    assert sorted(members[:, 0].tolist()) == list(range(20))
+    su = p.shared_host
+    pieces = sorted({(int(x[2]), int(x[3]), int(x[4])) for x in su})
+    assert pieces[0][0] == 0 and pieces[-1][1] == 40 and all(a[1] == b[0] for a, b in zip(pieces, pieces[1:]))
+    npieces = len(pieces)
+    for mb, mc, pb, pe, piece, tseq, *_ in su.tolist():
+        assert 0 < mc <= 16 and tseq in range(20)
+    per_member = {m: 0 for m in range(len(members))}
+    for mb, mc, *_ in su.tolist():
+        for m in range(mb, mb + mc):
+            per_member[m] += 1
+    assert set(per_member.values()) == {npieces}  # each member: every shared piece exactly once
+    units = p.units_host
+    for s in range(20):
+        own = [u for u in units.tolist() if u[0] == s]
+        assert min(u[2] for u in own) == 40 and max(u[3] for u in own) == -(-lens[s] // 16)
+        tok = qo[s]
+        assert p.reduce_chunks_host[tok] == npieces + len(own)
+        base = int(members[list(members[:, 0]).index(s), 2])
+        assert p.reduce_rows_host[tok] == base
+        assert sorted(u[4] for u in own) == [base + (npieces + c) * 2 for c in range(len(own))]
+    for s in range(20, len(steps)):  # the rest plan as usual, from page 0
+        assert min(u[2] for u in units.tolist() if u[0] == s) == 0
+    plain = mlb.plan_attention(qo, lens, width, 32, 8, "cpu", num_sms=148)
+    assert plain.num_shared_units == 0

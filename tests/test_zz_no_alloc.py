@@ -27,7 +27,8 @@ def _noalloc(L, q, k_pool, v_pool, meta, plan, out, err):
         q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(), v_pool.data_ptr(), L.MLB_BF16, nb, bs, q.shape[1],
         hkv, dh, 1.0 / math.sqrt(dh), meta.block_tables_i32.data_ptr(), meta.block_tables_i32.stride(0),
         meta.seq_lens_i32.data_ptr(), meta.qo_indptr.data_ptr(), len(meta.seq_lens), plan.units.data_ptr(),
-        plan.num_units, plan.num_partial_rows, plan.reduce_rows.data_ptr(), plan.reduce_chunks.data_ptr(),
+        plan.num_units, plan.shared_units.data_ptr(), plan.num_shared_units, plan.members.data_ptr(),
+        plan.num_partial_rows, plan.reduce_rows.data_ptr(), plan.reduce_chunks.data_ptr(),
         q.shape[0], out.data_ptr(), out.stride(0), out.stride(1), err.data_ptr(),
         torch.cuda.current_stream().cuda_stream)
 
