@@ -3,6 +3,10 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config 2|3|4|5]
     torchrun --nproc-per-node N bench.py --gpus N ...      (KV-head sharding, NCCL all-gather)
 
+Several GPUs (config 2): rank r of N owns KV heads [8r/N, 8(r+1)/N) of every sequence.  By default the
+batch is 64 x N sequences (weak scaling: each rank reads one GPU's worth of KV bytes, as serving with N
+GPUs runs N times the batch); --scaling strong keeps batch 64 and splits its heads.
+
 The default (config 2) is the headline line.  --config 3/4/5 print the same kind of line for BASELINE's
 mixed continuous-batching step, prefix-sharing step (copy-on-write) and long-context eviction step
 (compaction), each described in its builder below.
@@ -87,8 +91,9 @@ def config2(batch: int = 64, seed: int = 1234) -> Workload:
     nb = int(math.ceil(1.25 * int(pages.sum())))
     blocks = _take(r.permutation(nb), pages)
     rows = [(int(c) - 1, 1, b) for c, b in zip(ctx, blocks)]
-    return Workload("config 2", "Llama-3.1-8B decode attention (H32/Hkv8/Dh128, bs16), batch 64, ctx U[512,4096], "
-                    "32 layer pools, append 1 token/seq + paged attention", rows, rows, nb, kv_scale=0.5)
+    return Workload("config 2", f"Llama-3.1-8B decode attention (H32/Hkv8/Dh128, bs16), batch {batch}, "
+                    "ctx U[512,4096], 32 layer pools, append 1 token/seq + paged attention", rows, rows, nb,
+                    kv_scale=0.5)
 
 
 def config3(seed: int = 33) -> Workload:
@@ -352,8 +357,10 @@ def run_ours(args) -> None:
     mlb = importlib.import_module(PACKAGE)
     sharding = importlib.import_module(PACKAGE + ".sharding")
     ops = mlb.ops
+    mlb._lib.lib().mlb_set_programmatic_launch(0 if args.no_pdl else 1)
 
-    wl = config2(args.batch) if args.config == 2 else WORKLOADS[args.config]()
+    weak = world > 1 and args.config == 2 and args.scaling == "weak"
+    wl = config2(args.batch * (world if weak else 1)) if args.config == 2 else WORKLOADS[args.config]()
     layers = args.layers or wl.layers
     hkv_l, h_l = HKV // world, H // world
     n_app, n_att = sum(n for _, n, _ in wl.append_rows), len(wl.attend_rows)
@@ -382,24 +389,35 @@ def run_ours(args) -> None:
     plan = mlb.B200Backend().plan(meta_att, h_l, hkv_l, dev)
     ws = ops.Workspace()
     out_l = torch.empty(n_att, h_l, DH, device=dev, dtype=torch.bfloat16)
-    gathered = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 else None
+    p2p = world > 1 and args.transport == "p2p"
+    gathered = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None
+    peers = sharding.PeerOutputs(n_att, H, DH, torch.bfloat16, dev) if p2p else None
     copies = len(wl.copy_src)
     if copies:
         ptrs = ops.pool_pointer_table(k_pools + v_pools)
         src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
         dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
-    launches_per_layer = 2 + (1 if plan.num_partial_rows else 0)  # append, attention, split-K reduction
+    # append, attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
+    # [+ p2p barrier]
+    launches_per_layer = (2 + (1 if plan.num_shared_units else 0) + (1 if plan.num_partial_rows or p2p else 0)
+                          + (1 if p2p else 0))
 
     def layer_step(l, ev=None):
         ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
         if ev is not None:
             ev[0].record()
+        slot = l % peers.slots if p2p else 0
         ops.attention_partials(q_l, k_pools[l], v_pools[l], meta_att.block_tables_i32, meta_att.seq_lens_i32,
-                               meta_att.qo_indptr, plan, ws, out_l)
+                               meta_att.qo_indptr, plan, ws, out_l,
+                               targets=peers.local_targets(slot, qs.start) if p2p else None)
         if ev is not None:
             ev[1].record()
-        ops.splitk_reduce(plan, ws, out_l)
-        if world > 1:
+        if p2p:  # reduction + every row into every rank's buffer (one launch), then the flag barrier
+            ops.splitk_reduce_gather(plan, ws, peers.targets(slot, qs.start), peers.self_dest, torch.bfloat16, DH, dev)
+            peers.barrier()
+        else:
+            ops.splitk_reduce(plan, ws, out_l)
+        if world > 1 and not p2p:
             import torch.distributed as dist
 
             dist.all_gather_into_tensor(gathered, out_l)
@@ -479,6 +497,21 @@ def run_ours(args) -> None:
     ap_e.record()
     barrier()
     del graph, step_graph  # graphs holding NCCL work go before the process group
+    if p2p:  # the kernels' NVLink stores must have assembled exactly what an NCCL all-gather does
+        import torch.distributed as dist
+
+        peers.raise_errors()
+        last = layers - 1
+        got = peers.output(last % peers.slots, n_att).clone()
+        ops.attention_partials(q_l, k_pools[last], v_pools[last], meta_att.block_tables_i32, meta_att.seq_lens_i32,
+                               meta_att.qo_indptr, plan, ws, out_l)
+        ops.splitk_reduce(plan, ws, out_l)
+        flat = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(flat, out_l)
+        want = flat.view(world, n_att, h_l, DH).movedim(0, 1).reshape(n_att, H, DH)
+        if not torch.equal(got, want):
+            raise SystemExit(f"rank {rank}: p2p-gathered output differs from the NCCL all-gather")
+        del got, want, flat
     append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
     append_bytes = 2 * 2 * n_app * hkv_l * DH * 2  # K and V rows read + written, bf16
 
@@ -510,11 +543,14 @@ def run_ours(args) -> None:
                                                         f"appends{' and block copies' if copies else ''})",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "decode_rows": n_att,
                        "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
-                       "parallelism": f"kv-head shard x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"kv-head shard x{world}, output gather: "
+                                       + ("kernel NVLink stores + flag barrier" if p2p else "NCCL all-gather"))
+                                      if world > 1 else "single GPU",
                        "l2": "no flush: every layer's pool reads exceed the 126 MB L2",
+                       "programmatic_launch": not args.no_pdl,
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
@@ -549,6 +585,8 @@ def run_ours(args) -> None:
     if world > 1:
         import torch.distributed as dist
 
+        if peers is not None:
+            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -560,7 +598,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]
     qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    backend = sharding.KVHeadShardedBackend() if world > 1 else mlb.B200Backend()
+    backend = sharding.KVHeadShardedBackend(transport=args.transport) if world > 1 else mlb.B200Backend()
 
     def step():
         meta = mlb.AttentionMetadata.build(seqs, BS, dev)
@@ -585,13 +623,16 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     e.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e), world, dev) / args.steps
+    if world > 1:
+        backend.close()
     total = kv_bytes(ctx, HKV) * layers
     meta_bytes = _meta_bytes(mlb, seqs)
     h2d = layers * (q.numel() + k.numel() + v.numel()) * q.element_size() + meta_bytes
     d2h = layers * q.numel() * q.element_size()
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "path": ("KVHeadShardedBackend" if world > 1 else "B200Backend") + ".forward per layer, pinned host I/O"}
+            "path": (f"KVHeadShardedBackend(transport={args.transport!r})" if world > 1 else "B200Backend")
+                    + ".forward per layer, pinned host I/O"}
 
 
 def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:
@@ -637,12 +678,18 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=2)
     ap.add_argument("--layers", type=int, default=0, help="layer pools (default: the config's, 32 or 1)")
     ap.add_argument("--kernel-steps", type=int, default=10, help="eager steps whose attention launches are timed")
-    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=64, help="config 2 sequences per GPU-set (see --scaling)")
+    ap.add_argument("--transport", choices=["p2p", "nccl"], default="p2p",
+                    help="N>1: output all-gather by the kernels' own NVLink stores + a flag barrier (p2p), or NCCL")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N>1, config 2: weak = batch x N sequences (each rank keeps one GPU's KV bytes); "
+                         "strong = the same batch split by KV heads (configs 3-5 are always strong)")
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--cpu-reps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)

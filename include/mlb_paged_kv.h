@@ -48,7 +48,15 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 2 */
+MLB_API int mlb_abi_version(void);  /* 3 */
+
+/*
+ * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
+ * stream serialisation, so it becomes resident while its predecessor on the stream finishes and waits
+ * on the device (griddepcontrol.wait) before reading anything; launch latency hides behind the previous
+ * kernel's tail.  Results are identical either way.  Returns the previous setting.
+ */
+MLB_API int mlb_set_programmatic_launch(int enable);
 
 /*
  * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three
@@ -131,6 +139,25 @@ MLB_API int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens
                        int64_t* num_partial_rows);
 
 /*
+ * Where the final attention rows go.  NULL in the calls below means the call's own `out` (strides in
+ * elements).  Otherwise every final row is stored into each of num_dests (1..MLB_MAX_OUT_DESTS)
+ * destination buffers: row (token t, head h of this call) lands at element offset
+ * t * stride_tok + (head_offset + h) * stride_head of dests[i].  KV-head sharding uses it to do the
+ * output all-gather with the kernels' own stores: dests are every rank's gathered [N, H_total, head_dim]
+ * output (peers' buffers opened with mlb_ipc_open, reached over NVLink), head_offset the rank's first
+ * query head; mlb_peer_barrier then tells the ranks that the rows have landed.  No reference
+ * counterpart (the reference runs on one GPU); it replaces the NCCL all-gather of the output.
+ */
+#define MLB_MAX_OUT_DESTS 8
+typedef struct {
+  int32_t num_dests;
+  int32_t head_offset;
+  int64_t stride_tok;
+  int64_t stride_head;
+  void* dests[MLB_MAX_OUT_DESTS];
+} mlb_out_targets;
+
+/*
  * Paged attention over block tables (decode rows and multi-token rows with the causal mask aligned to
  * the end of each context).  Replaces paged_attention (src/minillm/attention/paged_torch_ref.py:40-74)
  * and the FlashInfer decode/prefill wrappers' run() (flashinfer_backend.py:46).
@@ -140,7 +167,8 @@ MLB_API int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens
  * (shared_units may be NULL when num_shared_units == 0).  Scale is usually 1/sqrt(head_dim).
  * partial_o [num_partial_rows, num_heads, head_dim] and partial_lse [num_partial_rows, num_heads] (fp32,
  * caller-owned) may be NULL when the plan has no partial rows; when it has some, mlb_splitk_reduce
- * completes `out`.  out: [N, num_heads, head_dim] of q's dtype.  Supported: head_dim 64/128/256,
+ * completes `out`.  out: [N, num_heads, head_dim] of q's dtype, or out_targets (then `out` may be NULL).
+ * Supported: head_dim 64/128/256,
  * block_size 16, num_heads / num_kv_heads <= 8; f16/bf16 pools use tensor-core tiles, f32 pools CUDA
  * cores (f32 plans carry no shared-prefix units).
  */
@@ -152,17 +180,19 @@ MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_s
                         const mlb_shared_unit* shared_units, int64_t num_shared_units, const mlb_share_member* members,
                         float* partial_o, float* partial_lse, int64_t num_partial_rows,
                         void* out, int64_t out_stride_tok, int64_t out_stride_head,
-                        int32_t* err_word, void* stream);
+                        const mlb_out_targets* out_targets, int32_t* err_word, void* stream);
 
 /*
  * Split-K reduction: for every token whose reduce_chunks > 1, combine its rows
  * reduce_rows[t] + c * tokens_per_tile (c < reduce_chunks[t]) by their log-sum-exp weights and write
- * out[t].  Completes mlb_paged_attention; no reference counterpart (the reference never splits).
+ * out[t] (or every out_targets destination).  Completes mlb_paged_attention; no reference counterpart
+ * (the reference never splits).
  */
 MLB_API int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
                       const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,
                       int64_t num_tokens, int num_heads, int head_dim,
-                      void* out, int64_t out_stride_tok, int64_t out_stride_head, int out_dtype, void* stream);
+                      void* out, int64_t out_stride_tok, int64_t out_stride_head, int out_dtype,
+                      const mlb_out_targets* out_targets, void* stream);
 
 /*
  * Block copy for prefix-cache copy-on-write and compaction: pool[dst[i]] = pool[src[i]] for every pool
@@ -197,6 +227,48 @@ MLB_API int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int
                         int64_t num_partial_rows, const int32_t* reduce_rows, const int32_t* reduce_chunks,
                         int64_t num_tokens, void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         int32_t* err_word, void* stream);
+
+/*
+ * Device memory shared between the processes of one node (one process per GPU), for the output
+ * all-gather above.  No reference counterpart.  mlb_ipc_alloc: cudaMalloc `bytes` on the current device,
+ * zero it, and export a handle of MLB_IPC_HANDLE_BYTES bytes that other processes pass to mlb_ipc_open
+ * (which maps it, enabling peer access, and returns this process's address of it).  Close what you
+ * opened before the owner frees it.
+ */
+#define MLB_IPC_HANDLE_BYTES 64
+MLB_API int mlb_ipc_alloc(int64_t bytes, void** dev_ptr, void* handle);
+MLB_API int mlb_ipc_open(const void* handle, void** dev_ptr);
+MLB_API int mlb_ipc_close(void* dev_ptr);
+MLB_API int mlb_ipc_free(void* dev_ptr);
+
+/*
+ * Barrier of `world` ranks, one GPU each, over flag words in shared device memory: flags[r] is rank r's
+ * array of `world` uint32 (flags[rank] local, the others peer addresses from mlb_ipc_open).  One launch
+ * on `stream`: makes every write of the earlier work on the stream (the kernels' stores into peers'
+ * buffers) visible to the node, raises this rank's word in every peer's array to the next epoch, then
+ * waits until every peer has done the same here.  `epoch` is this rank's device counter (one uint32,
+ * zero at the start, advanced by the kernel, so CUDA-graph replays stay in step).  The wait gives up after
+ * timeout_ns (0: 2 s) and ORs MLB_DEV_WAIT_TIMEOUT into *err_word.  Every rank must make the same
+ * sequence of calls.  No reference counterpart.
+ */
+MLB_API int mlb_peer_barrier(uint32_t* const* flags, int rank, int world, uint32_t* epoch, int64_t timeout_ns,
+                     int32_t* err_word, void* stream);
+
+/*
+ * The output all-gather carried by the split-K reduction: one launch that finishes every row of a step
+ * and puts it in every rank's gathered buffer.  Call it after mlb_paged_attention was given
+ * out_targets = { 1 destination: out_targets->dests[self_dest], same head_offset and strides } (the rank's
+ * own buffer).  Split tokens are reduced from their partial rows into every destination; unsplit tokens'
+ * rows are copied from dests[self_dest] to the others (NVLink stores into peers' buffers).  Follow it
+ * with mlb_peer_barrier on the same stream: the kernel boundary and the barrier's system-scope fence make
+ * the rows visible before the flags.  reduce_rows / reduce_chunks / tokens_per_tile / num_partial_rows are
+ * the plan's (num_partial_rows may be 0: nothing was split).  No reference counterpart (it replaces the
+ * NCCL all-gather of KV-head sharding).
+ */
+MLB_API int mlb_splitk_reduce_gather(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                      const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,
+                      int64_t num_tokens, int num_heads, int head_dim, int out_dtype,
+                      const mlb_out_targets* out_targets, int self_dest, void* stream);
 
 #ifdef __cplusplus
 }

@@ -19,9 +19,13 @@ MLB_OK, MLB_EINVAL, MLB_EUNSUPPORTED, MLB_ECUDA, MLB_ENOSPACE = 0, 1, 2, 3, 4
 DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
 
 EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_paged_attention",
-           "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc")
-ABI_VERSION = 2
+           "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc", "mlb_ipc_alloc", "mlb_ipc_open",
+           "mlb_ipc_close", "mlb_ipc_free", "mlb_peer_barrier", "mlb_set_programmatic_launch",
+           "mlb_splitk_reduce_gather")
+ABI_VERSION = 3
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
+MAX_OUT_DESTS = 8  # MLB_MAX_OUT_DESTS
+IPC_HANDLE_BYTES = 64  # MLB_IPC_HANDLE_BYTES
 
 
 class WorkUnit(ctypes.Structure):
@@ -44,6 +48,13 @@ class ShareMember(ctypes.Structure):
     _fields_ = [("seq", c_int32), ("q0", c_int32), ("part_base", c_int32), ("reserved", c_int32)]
 
 
+class OutTargets(ctypes.Structure):
+    """mlb_out_targets: the destinations of the final attention rows (every rank's gathered output)."""
+
+    _fields_ = [("num_dests", c_int32), ("head_offset", c_int32), ("stride_tok", c_int64),
+                ("stride_head", c_int64), ("dests", c_void_p * MAX_OUT_DESTS)]
+
+
 WORK_UNIT_INT32S = ctypes.sizeof(WorkUnit) // 4
 SHARED_UNIT_INT32S = ctypes.sizeof(SharedUnit) // 4
 MEMBER_INT32S = ctypes.sizeof(ShareMember) // 4
@@ -52,6 +63,7 @@ _I32P, _I64P = POINTER(c_int32), POINTER(c_int64)
 _SIGNATURES = {
     "mlb_last_error": (c_char_p, []),
     "mlb_abi_version": (c_int, []),
+    "mlb_set_programmatic_launch": (c_int, [c_int]),
     "mlb_kv_append": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int, c_void_p, c_void_p, c_int64, c_int64,
                               c_void_p, c_int64, c_int64, c_int, c_int64, c_int, c_int, c_void_p, c_void_p]),
     "mlb_plan_attention": (c_int, [c_void_p, c_void_p, c_int, c_int, c_void_p, c_int64, c_int, c_int, c_int, c_int,
@@ -60,9 +72,9 @@ _SIGNATURES = {
     "mlb_paged_attention": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                     c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
                                     c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
-                                    c_int64, c_int64, c_void_p, c_void_p]),
+                                    c_int64, c_int64, POINTER(OutTargets), c_void_p, c_void_p]),
     "mlb_splitk_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
-                                  c_void_p, c_int64, c_int64, c_int, c_void_p]),
+                                  c_void_p, c_int64, c_int64, c_int, POINTER(OutTargets), c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                                c_void_p]),
     "mlb_paged_attention_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
@@ -70,6 +82,13 @@ _SIGNATURES = {
                                             c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,
                                             c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
                                             c_void_p]),
+    "mlb_ipc_alloc": (c_int, [c_int64, POINTER(c_void_p), c_void_p]),
+    "mlb_ipc_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "mlb_ipc_close": (c_int, [c_void_p]),
+    "mlb_ipc_free": (c_int, [c_void_p]),
+    "mlb_peer_barrier": (c_int, [POINTER(c_void_p), c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "mlb_splitk_reduce_gather": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
+                                         c_int, c_int, POINTER(OutTargets), c_int, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

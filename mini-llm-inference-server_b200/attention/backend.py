@@ -19,7 +19,8 @@ import torch
 import torch.nn.functional as F
 
 from .. import _lib
-from ..ops import AttentionPlan, Workspace, kv_append, paged_attention, plan_attention
+from ..ops import (AttentionPlan, Workspace, attention_partials, kv_append, paged_attention, plan_attention,
+                   splitk_reduce_gather)
 from .base import AttentionBackend
 
 
@@ -74,14 +75,27 @@ class B200Backend(AttentionBackend):
             self._planned, self._plan_key = meta, key
         return self._plan
 
-    def forward(self, q, k, v, k_cache, v_cache, meta):
+    def forward(self, q, k, v, k_cache, v_cache, meta, out_targets=None, peer_gather=None):
+        """out_targets (optional, `ops.out_targets`): store the output rows there and return None.
+        peer_gather (optional, `(PeerOutputs, slot, head_offset)`, used by KV-head sharding): put every row
+        in every rank's gathered buffer of that slot (the reduction carries the all-gather), then the
+        peers' barrier."""
         if k_cache.shape[1] != meta.block_size:
             raise ValueError(f"pool block size {k_cache.shape[1]} != metadata block size {meta.block_size}")
         err = self._error_word(q.device) if self.check_errors else None
         kv_append(k_cache, v_cache, meta.slot_mapping, k, v, err)
         plan = self.plan(meta, q.shape[1], k_cache.shape[2], q.device, k_cache.dtype)
-        out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
-                              self._workspace, err=err)
+        if peer_gather is not None:
+            peers, slot, head_offset = peer_gather
+            attention_partials(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
+                               self._workspace, err=err, targets=peers.local_targets(slot, head_offset))
+            splitk_reduce_gather(plan, self._workspace, peers.targets(slot, head_offset), peers.self_dest, q.dtype,
+                                 q.shape[2], q.device)
+            peers.barrier()
+            out = None
+        else:
+            out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr,
+                                  plan, self._workspace, err=err, targets=out_targets)
         if self.check_errors:
             self.raise_device_errors()
         return out

@@ -17,6 +17,7 @@ __global__ void __launch_bounds__(kThreads) block_copy_kernel(void* const* pools
                                                               int64_t num_blocks, int64_t block_bytes,
                                                               const int32_t* src, const int32_t* dst,
                                                               int64_t num_pairs, int32_t* err) {
+  griddep_begin();
   const int64_t items = num_pairs * num_pools;
   const int64_t nvec = block_bytes / 16;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
@@ -54,9 +55,8 @@ cudaError_t launch_block_copy(void* const* pools, int num_pools, int64_t num_blo
   const int64_t items = num_pairs * num_pools;
   int64_t grid = items < static_cast<int64_t>(num_sms) * 8 ? items : static_cast<int64_t>(num_sms) * 8;
   if (grid < 1) return cudaSuccess;
-  block_copy_kernel<<<static_cast<unsigned>(grid), kThreads, 0, s>>>(pools, num_pools, num_blocks, block_bytes,
-                                                                      src, dst, num_pairs, err);
-  return cudaGetLastError();
+  return launch_k(block_copy_kernel, dim3(static_cast<unsigned>(grid)), dim3(kThreads), 0, s, pools, num_pools,
+                  num_blocks, block_bytes, src, dst, num_pairs, err);
 }
 
 }  // namespace mlb

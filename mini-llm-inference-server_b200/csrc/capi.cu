@@ -2,6 +2,7 @@
 // dispatch to the kernels, and error reporting by status code + mlb_last_error().  No exception and no
 // device allocation crosses or happens behind this boundary.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <string>
@@ -17,8 +18,11 @@ cudaError_t launch_kv_append(void* k_cache, void* v_cache, int cache_dtype, int6
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
 cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
 cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
-                                 int tpt, int64_t ntok, int h, int dh, char* out, int64_t o_st, int64_t o_sh,
+                                 int tpt, int64_t ntok, int h, int dh, const mlb_out_targets& out,
                                  int out_dtype, cudaStream_t s);
+cudaError_t launch_splitk_reduce_gather(const float* po, const float* plse, const int32_t* rrows,
+                                        const int32_t* rchunks, int tpt, int64_t ntok, int h, int dh,
+                                        const mlb_out_targets& out, int self, int out_dtype, cudaStream_t s);
 cudaError_t launch_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
                               const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err, int num_sms,
                               cudaStream_t s);
@@ -55,6 +59,27 @@ constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for
 constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages
 
 int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
+
+// The destinations of a call's final rows: its own `out`, or the caller's targets (checked).
+int resolve_targets(const char* what, void* out, int64_t st, int64_t sh, const mlb_out_targets* t,
+                    mlb_out_targets* r) {
+  if (!t) {
+    if (!out) return fail(MLB_EINVAL, "%s: null out", what);
+    *r = mlb_out_targets{};
+    r->num_dests = 1;
+    r->stride_tok = st;
+    r->stride_head = sh;
+    r->dests[0] = out;
+    return MLB_OK;
+  }
+  if (t->num_dests < 1 || t->num_dests > MLB_MAX_OUT_DESTS || t->head_offset < 0)
+    return fail(MLB_EINVAL, "%s: out_targets has %d destinations (1..%d), head_offset %d", what, t->num_dests,
+                MLB_MAX_OUT_DESTS, t->head_offset);
+  for (int i = 0; i < t->num_dests; ++i)
+    if (!t->dests[i]) return fail(MLB_EINVAL, "%s: out_targets destination %d is null", what, i);
+  *r = *t;
+  return MLB_OK;
+}
 
 int sm_count() {
   int dev = 0, n = 148;
@@ -150,13 +175,22 @@ int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_bl
 
 namespace mlb {
 int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+namespace {
+std::atomic<int> g_programmatic_launch{1};
+}  // namespace
+bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
 }  // namespace mlb
 
 extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 2; }
+int mlb_abi_version(void) { return 3; }
+
+int mlb_set_programmatic_launch(int enable) {
+  return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+}
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
                   const int64_t* slot_mapping, const void* k, int64_t k_stride_tok, int64_t k_stride_head,
@@ -329,7 +363,7 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
                         int64_t num_units, const mlb_shared_unit* shared_units, int64_t num_shared_units,
                         const mlb_share_member* members, float* partial_o, float* partial_lse,
                         int64_t num_partial_rows, void* out, int64_t out_stride_tok, int64_t out_stride_head,
-                        int32_t* err_word, void* stream) {
+                        const mlb_out_targets* out_targets, int32_t* err_word, void* stream) {
   if (!elt_bytes(dtype)) return fail(MLB_EINVAL, "paged_attention: unknown dtype %d", dtype);
   if (block_size != mlb::kBlockSize)
     return fail(MLB_EUNSUPPORTED, "paged_attention: block_size %d (kernels are built for 16)", block_size);
@@ -344,8 +378,11 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   if (num_units < 0 || num_shared_units < 0 || num_seqs < 0 || num_blocks <= 0)
     return fail(MLB_EINVAL, "paged_attention: bad sizes");
   if (num_units == 0 && num_shared_units == 0) return MLB_OK;
-  if (!q || !k_cache || !v_cache || !block_tables || !seq_lens || !qo_indptr || (num_units && !units) || !out)
+  if (!q || !k_cache || !v_cache || !block_tables || !seq_lens || !qo_indptr || (num_units && !units))
     return fail(MLB_EINVAL, "paged_attention: null pointer");
+  mlb_out_targets targets;
+  if (int rc = resolve_targets("paged_attention", out, out_stride_tok, out_stride_head, out_targets, &targets))
+    return rc;
   if (num_shared_units > 0 && (!shared_units || !members || dtype == MLB_F32))
     return fail(MLB_EINVAL, "paged_attention: shared-prefix units need their arrays and a 16-bit pool");
   if (num_partial_rows > 0 && (!partial_o || !partial_lse))
@@ -376,9 +413,8 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   a.members = members;
   a.part_o = partial_o;
   a.part_lse = partial_lse;
-  a.out = static_cast<char*>(out);
-  a.o_st = out_stride_tok;
-  a.o_sh = out_stride_head;
+  a.out = targets;
+  a.out_vec = mlb::out_vec_ok(targets, elt_bytes(dtype)) ? 1 : 0;
   a.err = err_word;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (num_shared_units > 0) {
@@ -393,19 +429,46 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
 int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
                       const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile_,
                       int64_t num_tokens, int num_heads, int head_dim, void* out, int64_t out_stride_tok,
-                      int64_t out_stride_head, int out_dtype, void* stream) {
+                      int64_t out_stride_head, int out_dtype, const mlb_out_targets* out_targets, void* stream) {
   if (!elt_bytes(out_dtype)) return fail(MLB_EINVAL, "splitk_reduce: unknown dtype %d", out_dtype);
   if (head_dim != 64 && head_dim != 128 && head_dim != 256)
     return fail(MLB_EUNSUPPORTED, "splitk_reduce: head_dim %d", head_dim);
   if (num_tokens < 0 || num_heads <= 0 || tokens_per_tile_ <= 0) return fail(MLB_EINVAL, "splitk_reduce: bad sizes");
   if (num_tokens == 0 || num_partial_rows == 0) return MLB_OK;
-  if (!partial_o || !partial_lse || !reduce_rows || !reduce_chunks || !out)
+  if (!partial_o || !partial_lse || !reduce_rows || !reduce_chunks)
     return fail(MLB_EINVAL, "splitk_reduce: null pointer");
+  mlb_out_targets targets;
+  if (int rc = resolve_targets("splitk_reduce", out, out_stride_tok, out_stride_head, out_targets, &targets))
+    return rc;
   return cuda_status(mlb::launch_splitk_reduce(partial_o, partial_lse, reduce_rows, reduce_chunks, tokens_per_tile_,
-                                               num_tokens, num_heads, head_dim, static_cast<char*>(out),
-                                               out_stride_tok, out_stride_head, out_dtype,
+                                               num_tokens, num_heads, head_dim, targets, out_dtype,
                                                static_cast<cudaStream_t>(stream)),
                      "splitk_reduce launch");
+}
+
+int mlb_splitk_reduce_gather(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                             const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile_,
+                             int64_t num_tokens, int num_heads, int head_dim, int out_dtype,
+                             const mlb_out_targets* out_targets, int self_dest, void* stream) {
+  if (!elt_bytes(out_dtype)) return fail(MLB_EINVAL, "splitk_reduce_gather: unknown dtype %d", out_dtype);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(MLB_EUNSUPPORTED, "splitk_reduce_gather: head_dim %d", head_dim);
+  if (num_tokens < 0 || num_heads <= 0 || tokens_per_tile_ <= 0 || num_partial_rows < 0)
+    return fail(MLB_EINVAL, "splitk_reduce_gather: bad sizes");
+  if (!out_targets) return fail(MLB_EINVAL, "splitk_reduce_gather: null out_targets");
+  mlb_out_targets targets;
+  if (int rc = resolve_targets("splitk_reduce_gather", nullptr, 0, 0, out_targets, &targets)) return rc;
+  if (self_dest < 0 || self_dest >= targets.num_dests)
+    return fail(MLB_EINVAL, "splitk_reduce_gather: self_dest %d outside the %d destinations", self_dest,
+                targets.num_dests);
+  if (num_tokens == 0) return MLB_OK;
+  if (num_partial_rows > 0 && (!partial_o || !partial_lse || !reduce_rows || !reduce_chunks))
+    return fail(MLB_EINVAL, "splitk_reduce_gather: null pointer");
+  return cuda_status(mlb::launch_splitk_reduce_gather(partial_o, partial_lse, reduce_rows,
+                                                      num_partial_rows > 0 ? reduce_chunks : nullptr,
+                                                      tokens_per_tile_, num_tokens, num_heads, head_dim, targets,
+                                                      self_dest, out_dtype, static_cast<cudaStream_t>(stream)),
+                     "splitk_reduce_gather launch");
 }
 
 int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes, const int32_t* src,

@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "mlb_paged_kv.h"
 
 namespace mlb {
@@ -65,6 +67,36 @@ __device__ __forceinline__ float fast_exp2(float x) {  // ex2.approx: 2^x, -inf 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+
+// Every kernel of this library begins with griddep_begin().  Launched with programmatic stream
+// serialisation (launch_k), a kernel's CTAs may become resident while its predecessor on the stream is
+// still finishing; griddepcontrol.wait holds them until that grid has completed and its memory is
+// visible, so no input is read early.  Then launch_dependents lets the next kernel's CTAs do the same, so
+// each launch's latency hides behind the tail of the one before.  Launched normally, both are no-ops.
+__device__ __forceinline__ void griddep_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool programmatic_launch();  // host: the library-wide setting (mlb_set_programmatic_launch)
+
+// kernel<<<grid, block, smem, s>>>(args...), with programmatic stream serialisation when enabled
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = programmatic_launch() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- 16-byte asynchronous copies (LDGSTS)

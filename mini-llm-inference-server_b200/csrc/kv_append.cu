@@ -50,6 +50,7 @@ template <int IN, int OUT, bool VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   constexpr int in_b = Elt<IN>::bytes, out_b = Elt<OUT>::bytes;
   constexpr int per_vec = 16 / out_b;  // elements per output vector
+  griddep_begin();
   const int64_t rows = a.num_tokens * a.hkv;
   const int64_t total = 2 * rows * a.vecs_per_row;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -103,10 +104,8 @@ cudaError_t launch_typed(const AppendArgs& a, bool vec, cudaStream_t s) {
   if (blocks > 148 * 64) blocks = 148 * 64;  // grid-stride beyond 64 CTAs per SM
   if (blocks < 1) blocks = 1;
   if (vec)
-    kv_append_kernel<IN, OUT, true><<<static_cast<unsigned>(blocks), threads, 0, s>>>(a);
-  else
-    kv_append_kernel<IN, OUT, false><<<static_cast<unsigned>(blocks), threads, 0, s>>>(a);
-  return cudaGetLastError();
+    return launch_k(kv_append_kernel<IN, OUT, true>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, a);
+  return launch_k(kv_append_kernel<IN, OUT, false>, dim3(static_cast<unsigned>(blocks)), dim3(threads), 0, s, a);
 }
 
 }  // namespace

@@ -73,29 +73,34 @@ template <int DH, int OUT_DT, int NW>
 __device__ __forceinline__ void merge_and_store(const AttnArgs& a, const UnitInfo& ui, int kvh,
                                                 const float* const* so, const float* const* sm,
                                                 const float* const* sl) {
-  for (int idx = threadIdx.x; idx < ui.ncols * DH; idx += blockDim.x) {
-    const int j = idx / DH, d = idx % DH;
+  constexpr int V = 4, DV = DH / V;  // each thread takes 4 consecutive dims of one column (16-byte reads)
+  for (int idx = threadIdx.x; idx < ui.ncols * DV; idx += blockDim.x) {
+    const int j = idx / DV, d = (idx % DV) * V;
     float M = kNegInf;
 #pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, sm[w][j]);
-    float lsum = 0.f, acc = 0.f;
+    float lsum = 0.f, acc[V] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
       const float mw = sm[w][j];
       const float e = mw == kNegInf ? 0.f : fast_exp2(mw - M);
       lsum += e * sl[w][j];
-      acc += e * so[w][j * DH + d];
+      const float4 x = *reinterpret_cast<const float4*>(so[w] + j * DH + d);
+      acc[0] += e * x.x;
+      acc[1] += e * x.y;
+      acc[2] += e * x.z;
+      acc[3] += e * x.w;
     }
-    const float val = lsum > 0.f ? acc / lsum : 0.f;
+    float val[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) val[k] = lsum > 0.f ? acc[k] / lsum : 0.f;
     const int qi = ui.t0 + j / a.group;
     const int head = kvh * a.group + j % a.group;
     if (ui.part_row < 0) {
-      char* o = a.out + ((static_cast<int64_t>(ui.q0 + qi) * a.o_st + static_cast<int64_t>(head) * a.o_sh + d) *
-                         Elt<OUT_DT>::bytes);
-      store_f32<OUT_DT>(o, val);
+      store_out_n<OUT_DT, V>(a.out, a.out_vec, ui.q0 + qi, head, d, val);
     } else {
       const int64_t row = ui.part_row + j / a.group;
-      a.part_o[(row * a.h + head) * DH + d] = val;
+      *reinterpret_cast<float4*>(a.part_o + (row * a.h + head) * DH + d) = make_float4(val[0], val[1], val[2], val[3]);
       if (d == 0) a.part_lse[row * a.h + head] = lsum > 0.f ? M + log2f(lsum) : kNegInf;
     }
   }
@@ -172,6 +177,7 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
   static_assert(32 % CH_ROW == 0 || CH_ROW % 32 == 0, "row chunks must tile a warp");
 
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_begin();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x % a.hkv;
@@ -343,6 +349,7 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
   constexpr int CH_ROW = DH * 2 / 16;
   constexpr int CHUNKS = 2 * 16 * CH_ROW;  // 16-byte chunks of one page (K and V rows of one head)
   extern __shared__ __align__(128) uint8_t smem[];
+  griddep_begin();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x % a.hkv;
@@ -463,6 +470,7 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a)
   extern __shared__ __align__(128) uint8_t smem[];
   float* qs = reinterpret_cast<float*>(smem);  // [8][DH]
   float* ms = qs + 8 * DH;                     // [warps][8 * DH + 16]
+  griddep_begin();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x % a.hkv;
@@ -585,25 +593,34 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_f32_kernel(AttnArgs a)
 
 // ------------------------------------------------------------------ split-K reduction
 
-template <int DH, int OUT_DT>
-__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* po, const float* plse,
-                                                            const int32_t* rrows, const int32_t* rchunks, int tpt,
-                                                            int64_t ntok, int h, char* out, int64_t o_st,
-                                                            int64_t o_sh) {
+template <int N>
+__device__ __forceinline__ void load_f32(const float* p, float (&x)[N]) {
+  if constexpr (N == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    x[0] = v.x;
+    x[1] = v.y;
+  } else {
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k) {
+      const float4 v = reinterpret_cast<const float4*>(p)[k];
+      x[4 * k] = v.x;
+      x[4 * k + 1] = v.y;
+      x[4 * k + 2] = v.z;
+      x[4 * k + 3] = v.w;
+    }
+  }
+}
+
+// Combine the `nc` partial rows of one (token, head): lane l ends with dims [l * DPL, (l + 1) * DPL) of the
+// normalised result (8- or 16-byte loads of the rows; weights 2^(lse_c - max)).
+template <int DH>
+__device__ __forceinline__ void reduce_token_head(const float* po, const float* plse, int64_t r0, int nc, int tpt,
+                                                  int h, int head, int lane, float (&acc)[DH / 32]) {
   constexpr int DPL = DH / 32;
-  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (wid >= ntok * h) return;
-  const int64_t tok = wid / h;
-  const int head = static_cast<int>(wid % h);
-  const int nc = rchunks[tok];
-  if (nc <= 1) return;
-  const int64_t r0 = rrows[tok];
   float M = kNegInf;
   for (int c = lane; c < nc; c += 32) M = fmaxf(M, plse[(r0 + static_cast<int64_t>(c) * tpt) * h + head]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-  float acc[DPL];
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
   float lw = 0.f;
@@ -612,14 +629,62 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* po, con
     const float lse = plse[row * h + head];
     const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
     lw += w;
-    const float* src = po + (row * h + head) * DH;
+    float x[DPL];
+    load_f32<DPL>(po + (row * h + head) * DH + lane * DPL, x);
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, src[lane + 32 * i], acc[i]);
+    for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, x[i], acc[i]);
   }
   const float inv = lw > 0.f ? 1.f / lw : 0.f;
-  char* o = out + (tok * o_st + static_cast<int64_t>(head) * o_sh) * Elt<OUT_DT>::bytes;
 #pragma unroll
-  for (int i = 0; i < DPL; ++i) store_f32<OUT_DT>(o + (lane + 32 * i) * Elt<OUT_DT>::bytes, acc[i] * inv);
+  for (int i = 0; i < DPL; ++i) acc[i] *= inv;
+}
+
+// One warp per (token, query head) whose sequence was split.
+template <int DH, int OUT_DT>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* po, const float* plse,
+                                                            const int32_t* rrows, const int32_t* rchunks, int tpt,
+                                                            int64_t ntok, int h, const mlb_out_targets out,
+                                                            int out_vec) {
+  constexpr int DPL = DH / 32;
+  griddep_begin();
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= ntok * h) return;
+  const int64_t tok = wid / h;
+  const int head = static_cast<int>(wid % h);
+  const int nc = rchunks[tok];
+  if (nc <= 1) return;
+  float acc[DPL];
+  reduce_token_head<DH>(po, plse, rrows[tok], nc, tpt, h, head, lane, acc);
+  store_out_n<OUT_DT, DPL>(out, out_vec != 0, tok, head, lane * DPL, acc);
+}
+
+// The split-K reduction carrying the output all-gather: one warp per (token, query head) of this rank.
+// Split tokens are reduced into every destination; unsplit tokens' rows (written by the attention kernel
+// into destination `self` only) are copied from there to the others.  No fence here: the barrier kernel
+// that follows on the stream orders these stores before its flags (a per-CTA system-scope fence measured
+// ~12 us slower per launch than the kernel boundary).
+template <int DH, int OUT_DT>
+__global__ void __launch_bounds__(256) splitk_reduce_gather_kernel(const float* po, const float* plse,
+                                                                   const int32_t* rrows, const int32_t* rchunks,
+                                                                   int tpt, int64_t ntok, int h,
+                                                                   const mlb_out_targets out, int out_vec,
+                                                                   int self) {
+  constexpr int DPL = DH / 32;
+  griddep_begin();
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= ntok * h) return;
+  const int64_t tok = wid / h;
+  const int head = static_cast<int>(wid % h);
+  const int nc = rchunks ? rchunks[tok] : 1;
+  if (nc > 1) {
+    float acc[DPL];
+    reduce_token_head<DH>(po, plse, rrows[tok], nc, tpt, h, head, lane, acc);
+    store_out_n<OUT_DT, DPL>(out, out_vec != 0, tok, head, lane * DPL, acc);
+  } else {
+    copy_out_n<OUT_DT, DPL>(out, out_vec != 0, self, tok, head, lane * DPL);
+  }
 }
 
 // Opt in to > 48 KB of dynamic shared memory once per kernel instance and device (`done` is the
@@ -642,8 +707,7 @@ cudaError_t launch_mma(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
   auto k = paged_attn_mma_kernel<DT, DH, STAGES, NW>;
   cudaError_t e = set_smem(k, bytes, done);
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(ctas), NW * 32, bytes, s>>>(a);
-  return cudaGetLastError();
+  return launch_k(k, dim3(static_cast<unsigned>(ctas)), dim3(NW * 32), bytes, s, a);
 }
 
 template <int DH>
@@ -653,8 +717,7 @@ cudaError_t launch_f32(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
   auto k = paged_attn_f32_kernel<DH>;
   cudaError_t e = set_smem(k, bytes, done);
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(ctas), kWarps * 32, bytes, s>>>(a);
-  return cudaGetLastError();
+  return launch_k(k, dim3(static_cast<unsigned>(ctas)), dim3(kWarps * 32), bytes, s, a);
 }
 
 template <int DT, int DH>
@@ -664,8 +727,7 @@ cudaError_t launch_shared(const AttnArgs& a, int64_t units, cudaStream_t s) {
   auto k = shared_prefix_kernel<DT, DH>;
   cudaError_t e = set_smem(k, bytes, done);
   if (e != cudaSuccess) return e;
-  k<<<static_cast<unsigned>(units * a.hkv), kSharedWarps * 32, bytes, s>>>(a);
-  return cudaGetLastError();
+  return launch_k(k, dim3(static_cast<unsigned>(units * a.hkv)), dim3(kSharedWarps * 32), bytes, s, a);
 }
 
 }  // namespace
@@ -702,20 +764,37 @@ cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t
 }
 
 cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
-                                 int tpt, int64_t ntok, int h, int dh, char* out, int64_t o_st, int64_t o_sh,
+                                 int tpt, int64_t ntok, int h, int dh, const mlb_out_targets& out,
                                  int out_dtype, cudaStream_t s) {
   const int64_t warps = ntok * h;
   const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  const int vec = out_vec_ok(out, out_dtype == MLB_F32 ? 4 : 2) ? 1 : 0;
 #define MLB_RED(D, O)                                                                                    \
   if (dh == D && out_dtype == O) {                                                                       \
-    splitk_reduce_kernel<D, O><<<blocks, 256, 0, s>>>(po, plse, rrows, rchunks, tpt, ntok, h, out, o_st, \
-                                                      o_sh);                                             \
-    return cudaGetLastError();                                                                           \
+    return launch_k(splitk_reduce_kernel<D, O>, dim3(blocks), dim3(256), 0, s, po, plse, rrows, rchunks, tpt, \
+                    ntok, h, out, vec);                                                                  \
   }
   MLB_RED(64, MLB_F32) MLB_RED(64, MLB_F16) MLB_RED(64, MLB_BF16)
   MLB_RED(128, MLB_F32) MLB_RED(128, MLB_F16) MLB_RED(128, MLB_BF16)
   MLB_RED(256, MLB_F32) MLB_RED(256, MLB_F16) MLB_RED(256, MLB_BF16)
 #undef MLB_RED
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_splitk_reduce_gather(const float* po, const float* plse, const int32_t* rrows,
+                                        const int32_t* rchunks, int tpt, int64_t ntok, int h, int dh,
+                                        const mlb_out_targets& out, int self, int out_dtype, cudaStream_t s) {
+  const int64_t warps = ntok * h;
+  const unsigned blocks = static_cast<unsigned>((warps * 32 + 255) / 256);
+  const int vec = out_vec_ok(out, out_dtype == MLB_F32 ? 4 : 2) ? 1 : 0;
+#define MLB_REDG(D, O)                                                                                          \
+  if (dh == D && out_dtype == O)                                                                                \
+    return launch_k(splitk_reduce_gather_kernel<D, O>, dim3(blocks), dim3(256), 0, s, po, plse, rrows, rchunks, \
+                    tpt, ntok, h, out, vec, self);
+  MLB_REDG(64, MLB_F32) MLB_REDG(64, MLB_F16) MLB_REDG(64, MLB_BF16)
+  MLB_REDG(128, MLB_F32) MLB_REDG(128, MLB_F16) MLB_REDG(128, MLB_BF16)
+  MLB_REDG(256, MLB_F32) MLB_REDG(256, MLB_F16) MLB_REDG(256, MLB_BF16)
+#undef MLB_REDG
   return cudaErrorInvalidValue;
 }
 

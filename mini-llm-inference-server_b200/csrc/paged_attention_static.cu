@@ -97,13 +97,13 @@ int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int64_t q_s
   const int rc = mlb_paged_attention(q, q_stride_tok, q_stride_head, k_cache, v_cache, dtype, num_blocks, block_size,
                                      num_heads, num_kv_heads, head_dim, scale, block_tables, bt_stride, seq_lens,
                                      qo_indptr, num_seqs, units, num_units, shared_units, num_shared_units, members,
-                                     po, plse, num_partial_rows, out, out_stride_tok, out_stride_head, err_word,
-                                     stream);
+                                     po, plse, num_partial_rows, out, out_stride_tok, out_stride_head, nullptr,
+                                     err_word, stream);
   if (rc != MLB_OK || num_partial_rows == 0 || num_tokens == 0) return rc;  // mlb_last_error() says why
   const int group = num_heads / num_kv_heads;
   const int tpt = group >= 8 ? 1 : 8 / group;  // query tokens per tile, as the planner sets it
   return mlb_splitk_reduce(po, plse, num_partial_rows, reduce_rows, reduce_chunks, tpt, num_tokens, num_heads,
-                           head_dim, out, out_stride_tok, out_stride_head, dtype, stream);
+                           head_dim, out, out_stride_tok, out_stride_head, dtype, nullptr, stream);
 }
 
 }  // extern "C"

@@ -16,7 +16,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import MEMBER_INT32S, SHARED_UNIT_INT32S, WORK_UNIT_INT32S, check, lib
+from ._lib import MAX_OUT_DESTS, MEMBER_INT32S, SHARED_UNIT_INT32S, WORK_UNIT_INT32S, OutTargets, check, lib
 
 DTYPE_CODE = {torch.float32: _lib.MLB_F32, torch.float16: _lib.MLB_F16, torch.bfloat16: _lib.MLB_BF16}
 BLOCK_SIZE = 16
@@ -182,27 +182,40 @@ class Workspace:
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan,
                     workspace: Workspace | None = None, out: torch.Tensor | None = None, scale: float | None = None,
-                    err: torch.Tensor | None = None) -> torch.Tensor:
+                    err: torch.Tensor | None = None, targets: OutTargets | None = None) -> torch.Tensor | None:
     """paged_attention (paged_torch_ref.py:40-74) on the GPU: q [N, H, Dh] -> [N, H, Dh] in q's dtype.
 
     block_tables int32 [S, W], seq_lens int32 [S], qo_indptr int32 [S + 1] are AttentionMetadata's
     device tensors (block_tables_i32, seq_lens_i32, qo_indptr).  The pools must already hold this
     step's k/v (kv_append first).  Launches the shared-prefix and per-sequence attention kernels, then
-    the split-K reduction when the plan split any sequence.
+    the split-K reduction when the plan split any sequence.  With `targets` (see `out_targets`) the rows
+    go to those destinations instead and nothing is returned.
     """
     workspace = workspace or Workspace()
     out = attention_partials(q, k_cache, v_cache, block_tables, seq_lens, qo_indptr, plan, workspace, out, scale,
-                             err)
-    splitk_reduce(plan, workspace, out)
+                             err, targets)
+    splitk_reduce(plan, workspace, out, targets, q.dtype, q.shape[2], q.device)
     return out
+
+
+def out_targets(dests: list[int], head_offset: int, stride_tok: int, stride_head: int) -> OutTargets:
+    """mlb_out_targets: store every final row (token t, local head h) at element offset
+    t * stride_tok + (head_offset + h) * stride_head of each destination address in `dests`."""
+    if not 1 <= len(dests) <= MAX_OUT_DESTS:
+        raise ValueError(f"out_targets: 1..{MAX_OUT_DESTS} destinations, got {len(dests)}")
+    t = OutTargets()
+    t.num_dests, t.head_offset, t.stride_tok, t.stride_head = len(dests), head_offset, stride_tok, stride_head
+    for i, d in enumerate(dests):
+        t.dests[i] = d
+    return t
 
 
 def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                        seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan, workspace: Workspace,
                        out: torch.Tensor | None = None, scale: float | None = None,
-                       err: torch.Tensor | None = None) -> torch.Tensor:
-    """The attention kernels (K2s, K2a): unsplit sequences are final in `out`; split ones leave fp32
-    partial rows in `workspace` for `splitk_reduce`."""
+                       err: torch.Tensor | None = None, targets: OutTargets | None = None) -> torch.Tensor | None:
+    """The attention kernels (K2s, K2a): unsplit sequences are final in `out` (or `targets`); split ones
+    leave fp32 partial rows in `workspace` for `splitk_reduce`."""
     _check_pool(k_cache, "paged_attention")
     _check_pool(v_cache, "paged_attention")
     nb, bs, hkv, dh = k_cache.shape
@@ -216,7 +229,9 @@ def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     for t, name in ((block_tables, "block_tables"), (seq_lens, "seq_lens"), (qo_indptr, "qo_indptr")):
         if t.dtype != torch.int32 or not t.is_contiguous() or t.device != q.device:
             raise ValueError(f"paged_attention: {name} must be a contiguous int32 tensor on {q.device}")
-    if out is None:
+    if targets is not None:
+        out = None
+    elif out is None:
         out = torch.empty_like(q)
     elif out.shape != q.shape or out.dtype != q.dtype or out.stride(2) != 1:
         raise ValueError("paged_attention: out must match q")
@@ -231,22 +246,52 @@ def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
                                    block_tables.stride(0), seq_lens.data_ptr(), qo_indptr.data_ptr(),
                                    seq_lens.shape[0], plan.units.data_ptr(), plan.num_units,
                                    plan.shared_units.data_ptr(), plan.num_shared_units, plan.members.data_ptr(),
-                                   _ptr(po), _ptr(plse), plan.num_partial_rows, out.data_ptr(), out.stride(0),
-                                   out.stride(1), _ptr(err), _stream(q.device))
+                                   _ptr(po), _ptr(plse), plan.num_partial_rows, _ptr(out), *_strides(out),
+                                   _targets(targets), _ptr(err), _stream(q.device))
     check(rc, "paged_attention")
     return out
 
 
-def splitk_reduce(plan: AttentionPlan, workspace: Workspace, out: torch.Tensor) -> None:
-    """K2b: combine the split sequences' partial rows into `out` (no-op when the plan split nothing)."""
+def splitk_reduce(plan: AttentionPlan, workspace: Workspace, out: torch.Tensor | None,
+                  targets: OutTargets | None = None, dtype: torch.dtype | None = None, head_dim: int | None = None,
+                  device: torch.device | None = None) -> None:
+    """K2b: combine the split sequences' partial rows into `out` (no-op when the plan split nothing).
+    With `targets`, the rows go there instead; dtype / head_dim / device then describe them."""
     if not plan.num_partial_rows or plan.num_tokens == 0:
         return
-    n, h, dh = out.shape
-    po, plse = workspace.get(plan.num_partial_rows, h, dh, out.device)
+    if targets is None:
+        if out is None:
+            raise ValueError("splitk_reduce: no out and no targets")
+        dtype, head_dim, device = out.dtype, out.shape[2], out.device
+    n, h = plan.num_tokens, plan.num_heads
+    po, plse = workspace.get(plan.num_partial_rows, h, head_dim, device)
     rc = lib().mlb_splitk_reduce(po.data_ptr(), plse.data_ptr(), plan.num_partial_rows, plan.reduce_rows.data_ptr(),
-                                 plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, n, h, dh, out.data_ptr(),
-                                 out.stride(0), out.stride(1), _code(out, "splitk_reduce"), _stream(out.device))
+                                 plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, n, h, head_dim, _ptr(out),
+                                 *_strides(out), DTYPE_CODE[dtype], _targets(targets), _stream(device))
     check(rc, "splitk_reduce")
+
+
+def splitk_reduce_gather(plan: AttentionPlan, workspace: Workspace, targets: OutTargets, self_dest: int,
+                         dtype: torch.dtype, head_dim: int, device: torch.device) -> None:
+    """The split-K reduction carrying the output all-gather (mlb_splitk_reduce_gather): after
+    `attention_partials` wrote the unsplit rows into destination `self_dest` only, every row of the step
+    is stored into every destination.  Follow it with the peers' barrier (`PeerOutputs.barrier`)."""
+    po = plse = None
+    if plan.num_partial_rows:
+        po, plse = workspace.get(plan.num_partial_rows, plan.num_heads, head_dim, device)
+    rc = lib().mlb_splitk_reduce_gather(_ptr(po), _ptr(plse), plan.num_partial_rows, plan.reduce_rows.data_ptr(),
+                                        plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, plan.num_tokens,
+                                        plan.num_heads, head_dim, DTYPE_CODE[dtype], ctypes.byref(targets), self_dest,
+                                        _stream(device))
+    check(rc, "splitk_reduce_gather")
+
+
+def _strides(out: torch.Tensor | None) -> tuple[int, int]:
+    return (out.stride(0), out.stride(1)) if out is not None else (0, 0)
+
+
+def _targets(t: OutTargets | None):
+    return ctypes.byref(t) if t is not None else None
 
 
 # ---------------------------------------------------------------- K3: block copy

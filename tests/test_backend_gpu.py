@@ -118,3 +118,24 @@ def test_forward_is_stream_ordered_without_host_syncs(mlb, cuda):
         got = mlb.B200Backend().forward(q, k, v, kp2, vp2, meta)
     torch.cuda.current_stream().wait_stream(side)
     assert torch.equal(got, base)
+
+
+def test_programmatic_launch_changes_no_bit(mlb, cuda):
+    """Every kernel with and without programmatic dependent launch: pools and outputs bit-identical over a
+    4-layer chain (append -> attention -> split-K reduction, layer after layer, no host sync between)."""
+    lib = mlb._lib.lib()
+    results = []
+    for enable in (1, 0):
+        prev = lib.mlb_set_programmatic_launch(enable)
+        try:
+            q, k, v, k_pool, v_pool, meta, _ = mixed_step(mlb, cuda)
+            pools = [(k_pool.clone(), v_pool.clone()) for _ in range(4)]
+            backend = mlb.B200Backend(pages_per_unit=1)
+            outs = [backend.forward(q, k, v, kp, vp, meta) for kp, vp in pools]
+            torch.cuda.synchronize()
+            results.append((outs, pools))
+        finally:
+            lib.mlb_set_programmatic_launch(prev)
+    for (o1, p1), (o2, p2) in zip(zip(*results[0]), zip(*results[1])):
+        assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
+        assert torch.equal(p1[0], p2[0]) and torch.equal(p1[1], p2[1])

@@ -37,11 +37,47 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 2
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 3
 
 
 def test_plan_record_layouts_match_header(L):
     assert ctypes.sizeof(L.WorkUnit) == 32 and ctypes.sizeof(L.SharedUnit) == 32 and ctypes.sizeof(L.ShareMember) == 16
+    assert ctypes.sizeof(L.OutTargets) == 24 + 8 * L.MAX_OUT_DESTS
+
+
+def test_output_targets_and_peer_calls_validate_on_the_host(L, mlb):
+    lib = L.lib()
+    fake = 1 << 20  # never dereferenced: every call below is refused before a launch
+    for n, dests in ((0, []), (9, [fake] * 8), (2, [fake, None])):
+        t = L.OutTargets()
+        t.num_dests = n
+        for i, d in enumerate(dests):
+            t.dests[i] = d
+        rc = lib.mlb_splitk_reduce(fake, fake, 4, fake, fake, 2, 4, 8, 64, None, 0, 0, 2, ctypes.byref(t), None)
+        assert rc == L.MLB_EINVAL and "out_targets" in L.last_error()
+    rc = lib.mlb_splitk_reduce(fake, fake, 4, fake, fake, 2, 4, 8, 64, None, 0, 0, 2, None, None)
+    assert rc == L.MLB_EINVAL and "null out" in L.last_error()
+    with pytest.raises(ValueError, match="destinations"):
+        mlb.ops.out_targets([fake] * 9, 0, 1, 1)
+    flags = (ctypes.c_void_p * 8)(*([fake] * 8))
+    for rank, world in ((0, 0), (0, 9), (2, 2), (-1, 2)):
+        rc = lib.mlb_peer_barrier(flags, rank, world, fake, 0, None, None)
+        assert rc == L.MLB_EINVAL and "rank" in L.last_error()
+    assert lib.mlb_peer_barrier(flags, 0, 2, None, 0, None, None) == L.MLB_EINVAL
+    assert lib.mlb_peer_barrier(flags, 0, 2, fake, -1, None, None) == L.MLB_EINVAL
+    flags[1] = None
+    rc = lib.mlb_peer_barrier(flags, 0, 2, fake, 0, None, None)
+    assert rc == L.MLB_EINVAL and "null" in L.last_error()
+    t = mlb.ops.out_targets([fake, fake], 0, 8, 1)
+    red = lambda tg, self_dest: lib.mlb_splitk_reduce_gather(fake, fake, 4, fake, fake, 2, 4, 8, 64, 2, tg,
+                                                             self_dest, None)
+    assert red(None, 0) == L.MLB_EINVAL and "null out_targets" in L.last_error()
+    assert red(ctypes.byref(t), 2) == L.MLB_EINVAL and "self_dest" in L.last_error()
+    assert red(ctypes.byref(t), -1) == L.MLB_EINVAL
+    p = ctypes.c_void_p()
+    assert lib.mlb_ipc_alloc(0, ctypes.byref(p), ctypes.create_string_buffer(64)) == L.MLB_EINVAL
+    assert lib.mlb_ipc_open(None, ctypes.byref(p)) == L.MLB_EINVAL
+    assert lib.mlb_ipc_close(None) == L.MLB_OK and lib.mlb_ipc_free(None) == L.MLB_OK
 
 
 def test_invalid_arguments_return_status_without_launching(L):
@@ -52,15 +88,15 @@ def test_invalid_arguments_return_status_without_launching(L):
     rc = lib.mlb_kv_append(None, None, 2, 10, 16, None, None, 0, 0, None, 0, 0, 2, 1, 2, 64, None, None)
     assert rc == L.MLB_EINVAL and "null" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 32, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "block_size" in L.last_error()
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 16, 32, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None, None)
     assert rc == L.MLB_EUNSUPPORTED and "query heads per KV head" in L.last_error()
     rc = lib.mlb_block_copy(None, 2, 10, 100, None, None, 3, None, None)
     assert rc == L.MLB_EUNSUPPORTED
     rc = lib.mlb_paged_attention(None, 0, 0, None, None, 2, 10, 8, 8, 2, 64, 0.1, None, 0, None, None, 1, None, 1,
-                                 None, 0, None, None, None, 0, None, 0, 0, None, None)
+                                 None, 0, None, None, None, 0, None, 0, 0, None, None, None)
     with pytest.raises(ValueError, match="block_size"):  # status codes become the reference's ValueError
         L.check(rc, "paged_attention")
     # zero work is a successful no-op
