@@ -358,6 +358,7 @@ def run_ours(args) -> None:
     sharding = importlib.import_module(PACKAGE + ".sharding")
     ops = mlb.ops
     mlb._lib.lib().mlb_set_programmatic_launch(0 if args.no_pdl else 1)
+    mlb._lib.lib().mlb_set_tensor_core_prefix(0 if args.no_tc_prefix else 1)
 
     weak = world > 1 and args.config == 2 and args.scaling == "weak"
     wl = config2(args.batch * (world if weak else 1)) if args.config == 2 else WORKLOADS[args.config]()
@@ -551,6 +552,7 @@ def run_ours(args) -> None:
                                       if world > 1 else "single GPU",
                        "l2": "no flush: every layer's pool reads exceed the 126 MB L2",
                        "programmatic_launch": not args.no_pdl,
+                       "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
@@ -690,6 +692,8 @@ def main() -> None:
     ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--no-tc-prefix", action="store_true",
+                    help="shared-prefix units on the mma.sync kernel instead of tcgen05")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)

@@ -59,6 +59,14 @@ MLB_API int mlb_abi_version(void);  /* 3 */
 MLB_API int mlb_set_programmatic_launch(int enable);
 
 /*
+ * Shared-prefix units on the 5th-generation tensor cores (process-wide, default on): tcgen05.mma tiles of
+ * 128 query columns x 128 keys with TMEM accumulators, for 16-bit pools with head_dim 64 or 128 and q rows
+ * 16-byte aligned; otherwise (or when disabled) the warp-level mma.sync kernel.  Same plan either way.
+ * Returns the previous setting.
+ */
+MLB_API int mlb_set_tensor_core_prefix(int enable);
+
+/*
  * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three
  * reference backends (torch_ref.py:47, flashinfer_backend.py:43, flash_attn_backend.py:44):
  *     k_cache.view(-1, Hkv, Dh)[slot_mapping[i]] = k[i].to(k_cache.dtype)   (and the same for v)
@@ -95,8 +103,8 @@ typedef struct {
  * Shared-prefix work (a prefix-cache hit seen by many decode rows): pages [page_begin, page_end) are the
  * same blocks in the tables of members [member_begin, member_begin + member_count) of the members array,
  * and the table row of sequence `table_seq` holds them.  One CTA per (unit, KV head) loads each page once
- * and applies it to every member's query heads, writing each member's partial row
- * members[m].part_base + piece * tokens_per_tile.
+ * and applies it to every member's query heads (up to 128 query columns: member_count <= 128 / group),
+ * writing each member's partial row members[m].part_base + piece * tokens_per_tile.
  */
 typedef struct {
   int32_t member_begin;

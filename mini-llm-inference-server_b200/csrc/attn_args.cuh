@@ -24,6 +24,7 @@ struct AttnArgs {
   const mlb_share_member* members;
   float* part_o;
   float* part_lse;
+  int64_t part_rows;  // rows of part_o / part_lse (writes beyond are skipped and flagged)
   mlb_out_targets out;  // final rows: one or more destinations (the call's `out`, or every rank's buffer)
   int out_vec;          // out_vec_ok(out): rows may be stored with packed 16-byte-aligned stores
   int32_t* err;

@@ -17,6 +17,9 @@ cudaError_t launch_kv_append(void* k_cache, void* v_cache, int cache_dtype, int6
                              cudaStream_t s);
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
 cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
+bool shared_prefix_tc_supported(const AttnArgs& a, int dtype, int dh);
+cudaError_t launch_shared_prefix_tc(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
+bool tensor_core_prefix();
 cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
                                  int tpt, int64_t ntok, int h, int dh, const mlb_out_targets& out,
                                  int out_dtype, cudaStream_t s);
@@ -53,8 +56,8 @@ bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a)
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
 constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
 constexpr int kWaveTenths = 15;      // the auto split aims for 1.5 waves of resident CTAs (measured best)
-constexpr int kSharedWarps = 8;      // warps per shared-prefix CTA; each takes max(1, 8 / group) members
-constexpr int kSharedCtasPerSm = 2;  // resident shared-prefix CTAs per SM
+constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
+constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
 constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages
 
@@ -178,8 +181,10 @@ int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
 namespace {
 std::atomic<int> g_programmatic_launch{1};
+std::atomic<int> g_tensor_core_prefix{1};
 }  // namespace
 bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
+bool tensor_core_prefix() { return g_tensor_core_prefix.load(std::memory_order_relaxed) != 0; }
 }  // namespace mlb
 
 extern "C" {
@@ -190,6 +195,10 @@ int mlb_abi_version(void) { return 3; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+}
+
+int mlb_set_tensor_core_prefix(int enable) {
+  return mlb::g_tensor_core_prefix.exchange(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
@@ -251,17 +260,19 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   std::vector<int> seq_group(num_seqs, -1);  // the (single) group of each decode row
   for (size_t g = 0; g < groups.size(); ++g)
     if (groups[g].tile == 0) seq_group[groups[g].seq] = static_cast<int>(g);
-  const int per_cta = kSharedWarps * std::max(1, 8 / group_size);  // member rows per shared CTA
+  const int per_cta = std::max(1, kSharedColumns / group_size);  // member rows per shared unit
   struct SetPlan {
     int pieces, per;
   };
   std::vector<SetPlan> set_plans;
   for (const ShareSet& set : sets) {
     const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
+    // as many pieces as keep every CTA in one wave, each a whole number of 8-page (128-key) tiles
     const int64_t target = static_cast<int64_t>(num_sms) * kSharedCtasPerSm;
-    int64_t pieces = std::max<int64_t>(1, (target + blocks * num_kv_heads - 1) / (blocks * num_kv_heads));
+    int64_t pieces = std::max<int64_t>(1, target / (blocks * num_kv_heads));
     pieces = std::min<int64_t>(pieces, std::max(1, set.pages / kMinPagesPerUnit));
-    const int per = static_cast<int>((set.pages + pieces - 1) / pieces);
+    int per = static_cast<int>((set.pages + pieces - 1) / pieces);
+    per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;
     pieces = (set.pages + per - 1) / per;
     set_plans.push_back({static_cast<int>(pieces), per});
     for (int s : set.seqs) {
@@ -413,12 +424,15 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   a.members = members;
   a.part_o = partial_o;
   a.part_lse = partial_lse;
+  a.part_rows = num_partial_rows;
   a.out = targets;
   a.out_vec = mlb::out_vec_ok(targets, elt_bytes(dtype)) ? 1 : 0;
   a.err = err_word;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (num_shared_units > 0) {
-    const int rc = cuda_status(mlb::launch_shared_prefix_attention(a, dtype, head_dim, num_shared_units, st),
+    const bool tc = mlb::tensor_core_prefix() && mlb::shared_prefix_tc_supported(a, dtype, head_dim);
+    const int rc = cuda_status(tc ? mlb::launch_shared_prefix_tc(a, dtype, head_dim, num_shared_units, st)
+                                  : mlb::launch_shared_prefix_attention(a, dtype, head_dim, num_shared_units, st),
                                "shared-prefix attention launch");
     if (rc != MLB_OK) return rc;
   }

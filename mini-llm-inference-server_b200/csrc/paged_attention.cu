@@ -360,103 +360,108 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
   const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
   const int64_t row_stride = static_cast<int64_t>(a.hkv) * DH * 2;
   const int mpw = a.group >= 8 ? 1 : 8 / a.group;  // member rows per warp
-  const int wm = warp * mpw;
-  const int ncols = max(0, min(mpw, mc - wm)) * a.group;
+  // A unit may hold more members than one pass covers (NW * mpw rows): the pages are walked once per
+  // block of NW * mpw member rows.
+  for (int sub = 0; sub * NW * mpw < mc; ++sub) {
+    const int wm = sub * NW * mpw + warp * mpw;
+    const int ncols = max(0, min(mpw, mc - wm)) * a.group;
 
-  uint32_t bad_mask = 0;
-  auto issue = [&](int j) {
-    if (j < npages) {
-      const int bid = __ldg(table + pb + j);
-      const int s = j % S;
-      const bool ok = bid >= 0 && bid < a.num_blocks;
-      bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
-      if (!ok) {
-        if (threadIdx.x == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-      } else {
-        const int64_t page_off = (static_cast<int64_t>(bid) * kBlockSize * a.hkv + kvh) * (DH * 2);
-        uint8_t* slot = smem + s * STAGE;
-        for (int e = threadIdx.x; e < CHUNKS; e += NW * 32) {
-          const int kv = e / (16 * CH_ROW), row = (e / CH_ROW) % 16, ch = e % CH_ROW;
-          cp_async16(slot + kv * TILE + row * ROWB + ch * 16,
-                     (kv ? a.v_cache : a.k_cache) + page_off + row * row_stride + ch * 16);
+    uint32_t bad_mask = 0;
+    auto issue = [&](int j) {
+      if (j < npages) {
+        const int bid = __ldg(table + pb + j);
+        const int s = j % S;
+        const bool ok = bid >= 0 && bid < a.num_blocks;
+        bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
+        if (!ok) {
+          if (threadIdx.x == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+        } else {
+          const int64_t page_off = (static_cast<int64_t>(bid) * kBlockSize * a.hkv + kvh) * (DH * 2);
+          uint8_t* slot = smem + s * STAGE;
+          for (int e = threadIdx.x; e < CHUNKS; e += NW * 32) {
+            const int kv = e / (16 * CH_ROW), row = (e / CH_ROW) % 16, ch = e % CH_ROW;
+            cp_async16(slot + kv * TILE + row * ROWB + ch * 16,
+                       (kv ? a.v_cache : a.k_cache) + page_off + row * row_stride + ch * 16);
+          }
         }
       }
-    }
-    cp_async_commit();
-  };
+      cp_async_commit();
+    };
 #pragma unroll
-  for (int j = 0; j < S - 1; ++j) issue(j);
+    for (int j = 0; j < S - 1; ++j) issue(j);
 
-  // Q^T fragments: column n = lane / 4 is member wm + n / group (its one new token), head kvh * group + n % group
-  uint32_t qb[KSTEPS][2];
-  {
-    const int n = lane >> 2, c2 = (lane & 3) * 2;
-    const bool live = n < ncols;
-    const int tok = live ? __ldg(&a.members[mb + wm + n / a.group].q0) : 0;
-    const int head = kvh * a.group + (live ? n % a.group : 0);
-    const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
-                           static_cast<int64_t>(head) * a.q_sh;
+    // Q^T fragments: column n = lane / 4 is member wm + n / group (its one new token), head kvh * group + n % group
+    uint32_t qb[KSTEPS][2];
+    {
+      const int n = lane >> 2, c2 = (lane & 3) * 2;
+      const bool live = n < ncols;
+      const int tok = live ? __ldg(&a.members[mb + wm + n / a.group].q0) : 0;
+      const int head = kvh * a.group + (live ? n % a.group : 0);
+      const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
+                             static_cast<int64_t>(head) * a.q_sh;
 #pragma unroll
-    for (int ks = 0; ks < KSTEPS; ++ks) {
-      const int d = ks * 16 + c2;
-      qb[ks][0] = live ? static_cast<uint32_t>(__ldg(qrow + d)) | (static_cast<uint32_t>(__ldg(qrow + d + 1)) << 16)
-                       : 0u;
-      qb[ks][1] = live ? static_cast<uint32_t>(__ldg(qrow + d + 8)) | (static_cast<uint32_t>(__ldg(qrow + d + 9)) << 16)
-                       : 0u;
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+        const int d = ks * 16 + c2;
+        qb[ks][0] =
+            live ? static_cast<uint32_t>(__ldg(qrow + d)) | (static_cast<uint32_t>(__ldg(qrow + d + 1)) << 16) : 0u;
+        qb[ks][1] =
+            live ? static_cast<uint32_t>(__ldg(qrow + d + 8)) | (static_cast<uint32_t>(__ldg(qrow + d + 9)) << 16) : 0u;
+      }
     }
-  }
-  const int r0 = lane >> 2, j0 = (lane & 3) * 2, j1 = j0 + 1;
-  const bool live0 = j0 < ncols, live1 = j1 < ncols;
-  const int lim0 = live0 ? INT_MAX : 0, lim1 = live1 ? INT_MAX : 0;  // every shared token is visible
-  float o[DH / 16][4];
+    const int r0 = lane >> 2, j0 = (lane & 3) * 2, j1 = j0 + 1;
+    const bool live0 = j0 < ncols, live1 = j1 < ncols;
+    const int lim0 = live0 ? INT_MAX : 0, lim1 = live1 ? INT_MAX : 0;  // every shared token is visible
+    float o[DH / 16][4];
 #pragma unroll
-  for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-  float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
-  const uint32_t base_u32 = smem_u32(smem);
-  const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
-  const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
+    for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+    const uint32_t base_u32 = smem_u32(smem);
+    const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
+    const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
 
-  for (int i = 0; i < npages; ++i) {
-    issue(i + S - 1);            // refill the slot page i - 1 used (every warp left it at the last barrier)
-    cp_async_wait<S - 1>();      // this thread's copies of page i have landed
-    __syncthreads();             // ... and every other thread's
-    const int s = i % S;
-    if (ncols > 0 && !((bad_mask >> s) & 1u))
-      attend_page<DT, DH>(base_u32 + s * STAGE + k_off, base_u32 + s * STAGE + TILE + v_off, qb, 0, lim0, lim1,
-                          a.sl2, o, m0, m1, l0, l1);
-    __syncthreads();  // every warp is done with slot s before it is refilled
-  }
-  cp_async_wait<0>();
+    for (int i = 0; i < npages; ++i) {
+      issue(i + S - 1);            // refill the slot page i - 1 used (every warp left it at the last barrier)
+      cp_async_wait<S - 1>();      // this thread's copies of page i have landed
+      __syncthreads();             // ... and every other thread's
+      const int s = i % S;
+      if (ncols > 0 && !((bad_mask >> s) & 1u))
+        attend_page<DT, DH>(base_u32 + s * STAGE + k_off, base_u32 + s * STAGE + TILE + v_off, qb, 0, lim0, lim1,
+                            a.sl2, o, m0, m1, l0, l1);
+      __syncthreads();  // every warp is done with slot s before it is refilled
+    }
+    cp_async_wait<0>();
 
 #pragma unroll
-  for (int off = 4; off < 32; off <<= 1) {
-    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-  }
-  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  // partial row of member m for head h: members[m].part_base + piece * tokens_per_tile (its one token)
-  int64_t slot0 = 0, slot1 = 0;
-  if (live0)
-    slot0 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j0 / a.group].part_base)) +
-             static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j0 % a.group;
-  if (live1)
-    slot1 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j1 / a.group].part_base)) +
-             static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j1 % a.group;
+    for (int off = 4; off < 32; off <<= 1) {
+      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+    }
+    const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+    // partial row of member m for head h: members[m].part_base + piece * tokens_per_tile (its one token)
+    int64_t slot0 = 0, slot1 = 0;
+    if (live0)
+      slot0 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j0 / a.group].part_base)) +
+               static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j0 % a.group;
+    if (live1)
+      slot1 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j1 / a.group].part_base)) +
+               static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j1 % a.group;
 #pragma unroll
-  for (int mt = 0; mt < DH / 16; ++mt) {
-    const int d = mt * 16 + r0;
-    if (live0) {
-      a.part_o[slot0 * DH + d] = o[mt][0] * inv0;
-      a.part_o[slot0 * DH + d + 8] = o[mt][2] * inv0;
+    for (int mt = 0; mt < DH / 16; ++mt) {
+      const int d = mt * 16 + r0;
+      if (live0) {
+        a.part_o[slot0 * DH + d] = o[mt][0] * inv0;
+        a.part_o[slot0 * DH + d + 8] = o[mt][2] * inv0;
+      }
+      if (live1) {
+        a.part_o[slot1 * DH + d] = o[mt][1] * inv1;
+        a.part_o[slot1 * DH + d + 8] = o[mt][3] * inv1;
+      }
     }
-    if (live1) {
-      a.part_o[slot1 * DH + d] = o[mt][1] * inv1;
-      a.part_o[slot1 * DH + d + 8] = o[mt][3] * inv1;
+    if (r0 == 0) {
+      if (live0) a.part_lse[slot0] = l0 > 0.f ? m0 + log2f(l0) : kNegInf;
+      if (live1) a.part_lse[slot1] = l1 > 0.f ? m1 + log2f(l1) : kNegInf;
     }
-  }
-  if (r0 == 0) {
-    if (live0) a.part_lse[slot0] = l0 > 0.f ? m0 + log2f(l0) : kNegInf;
-    if (live1) a.part_lse[slot1] = l1 > 0.f ? m1 + log2f(l1) : kNegInf;
+    __syncthreads();  // the ring is reused by the next block of members
   }
 }
 

@@ -1,0 +1,516 @@
+// K2s on the 5th-generation tensor cores: shared-prefix (cascade) attention with tcgen05.mma, TMEM
+// accumulators and an mbarrier pipeline.
+//
+// A shared unit is a run of prefix pages that every member row's block table holds (same block ids), for
+// up to 128 / group member rows, i.e. up to 128 query columns of one KV head.  That is a small
+// FlashAttention forward: S = Q . K^T over the pages, online softmax, O = P . V, with M = 128 query
+// columns (the TMEM lanes) per CTA and 128 keys (8 pages) per tile.
+//
+// Roles in one CTA of 256 threads (1 CTA per SM: ~225 KB of shared memory, all 512 TMEM columns):
+// - warp 0, one thread: the producer.  Each page of a tile is 2 x Dh/64 TMA boxes (tensor maps over the
+//   K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle), landing directly in the K-major
+//   layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts the bytes
+//   (expect_tx).  A block id out of range gets a slot coordinate past the pool's end: TMA fills zeros
+//   there and the softmax masks the page.  3 stages.  (16-byte cp.async from 96 threads measured 3.8 us
+//   per 64 KB tile here: too few loads in flight.)
+// - warp 1, one thread: the MMA issuer.  Per tile j: S_j = Q . K_j^T into TMEM buffer j % 2 (K = Dh in
+//   steps of 16), committed to s_full; then O += P_{j-1} . V_{j-1} with P read from TMEM (A operand) and
+//   V as an MN-major B operand (one k-step of 16 keys per loaded page, so pages past the unit's end are
+//   never read), committed to the stage's "empty" barrier and to o_done.  Issuing S_j
+//   before O_{j-1} lets the tensor core compute the next scores while the softmax warps work.
+// - warps 2-3: idle (they keep the softmax warps on a warpgroup boundary: TMEM lane quarter = warp % 4).
+// - warps 4-7 (a warpgroup; thread = one query column = one TMEM lane): read the S row from TMEM, mask,
+//   running max in the exp2 domain, P = 2^(s - m) packed to 16 bits into TMEM buffer j % 2, row sums in
+//   fp32.  O is rescaled (TMEM load / scale / store) only when a row's max grows by more than 8 (a factor
+//   256 of headroom keeps P and the sums finite), which after the first tiles is rare.  At the end every
+//   column's normalised O row and log2-sum-exp go to its split-K partial row, merged by the reduction.
+// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256 + Dh), P0 [384,448), P1 [448,512).
+//
+// Every wait is bounded (time and polls); on expiry the CTA raises MLB_DEV_WAIT_TIMEOUT, drains its own
+// copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+
+#include <climits>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "attn_args.cuh"
+
+namespace mlb {
+
+namespace {
+
+constexpr int kTcThreads = 256;
+constexpr int kTcStages = 3;
+constexpr int kTcRows = 128;        // query columns per CTA = MMA M = TMEM lanes
+constexpr int kTcTileTokens = 128;  // keys per tile = N of S = Q . K^T
+constexpr int kTcTilePages = kTcTileTokens / kBlockSize;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColO = 256;
+__device__ __forceinline__ uint32_t col_s(int b) { return b ? 128u : 0u; }    // S buffers
+__device__ __forceinline__ uint32_t col_p(int b) { return b ? 448u : 384u; }  // P buffers (16-bit pairs)
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+template <int DH>
+struct TcLayout {
+  static constexpr int kTileBytes = kTcTileTokens * DH * 2;  // one K or V tile, [DH/64][128][64] swizzled
+  static constexpr int kQBytes = kTcRows * DH * 2;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kBarOffset = kQBytes + kTcStages * kStageBytes;
+  // barriers: full[3], empty[3], s_full[2], p_full[2], o_done, final; then the TMEM base and the abort flag
+  static constexpr int kBytes = kBarOffset + 16 * 8 + 16;
+  static constexpr int kLaunchBytes = kBytes + 1024;  // slack to align the base to 1024 (swizzle atoms)
+};
+
+// ---------------------------------------------------------------- tcgen05 / proxy wrappers
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// One tiled TMA box (this GPU's memory, no multicast) into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2), sm100 version 1.  Addresses and
+// offsets in bytes (multiples of 16).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, A and B of one 16-bit type (fmt 0 = f16,
+// 1 = bf16), A K-major, B K-major or MN-major, shape M x N.
+__host__ __device__ constexpr uint32_t f16_idesc(uint32_t fmt, bool b_mn_major, int m, int n) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+         (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns (this warp's lane quarter)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%"
+      "19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%"
+      "18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Bounded wait on an mbarrier phase; gives up (and tells the CTA to stop) when another role aborted or
+// after kWaitLimitNs.
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int32_t* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  *abort_flag = 1;
+  flag_error(err, MLB_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+// Bounded wait that ignores the abort flag (draining this CTA's own MMAs before TMEM is freed).
+__device__ __forceinline__ bool tc_drain(uint64_t* bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 0; i < (1u << 26); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  return false;
+}
+
+// Byte offset of 16-byte chunk c (of a DH x 2-byte row) of row r in a [DH/64][128][64] swizzled tile.
+__device__ __forceinline__ uint32_t sw_chunk(int r, int c) {
+  return static_cast<uint32_t>((c >> 3) * (kTcRows * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+template <int DT, int DH>
+__global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tk,
+                                                                          const __grid_constant__ CUtensorMap tv) {
+  using L = TcLayout<DH>;
+  constexpr int CH = DH * 2 / 16;  // 16-byte chunks per row
+  constexpr uint32_t kFmt = DT == MLB_BF16 ? 1u : 0u;
+  constexpr uint32_t kIdescS = f16_idesc(kFmt, false, kTcRows, kTcTileTokens);
+  constexpr uint32_t kIdescO = f16_idesc(kFmt, true, kTcRows, DH);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + 3;
+  uint64_t* s_full = bars + 6;
+  uint64_t* p_full = bars + 8;
+  uint64_t* o_done = bars + 10;
+  uint64_t* final_bar = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16) + 1;
+  const uint32_t q_smem = smem_u32(smem);
+  const uint32_t stage_smem = q_smem + L::kQBytes;
+
+  griddep_begin();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x % a.hkv;
+  const int4* rec = reinterpret_cast<const int4*>(a.shared_units + blockIdx.x / a.hkv);
+  const int4 x = __ldg(rec), y = __ldg(rec + 1);
+  const int mb = x.x, mc = x.y, pb = x.z, pe = x.w, piece = y.x, tseq = y.y;
+  const int npages = pe - pb;
+  const int ntiles = (npages + kTcTilePages - 1) / kTcTilePages;
+  const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(s_full + b, 1);
+      mbar_init(p_full + b, 128);
+    }
+    mbar_init(o_done, 1);
+    mbar_init(final_bar, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {  // the whole warp allocates TMEM; the address lands in shared memory
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp >= 4) {  // Q rows, straight into the swizzled K-major A tile (zero for absent columns)
+    const int c = threadIdx.x - 128;
+    const int m = c / a.group;
+    const bool live = m < mc;
+    const uint4* src = nullptr;
+    if (live) {
+      const int tok = __ldg(&a.members[mb + m].q0);
+      const int head = kvh * a.group + c % a.group;
+      src = reinterpret_cast<const uint4*>(a.q + (static_cast<int64_t>(tok) * a.q_st + static_cast<int64_t>(head) * a.q_sh) * 2);
+    }
+#pragma unroll
+    for (int ch = 0; ch < CH; ++ch) {
+      const uint4 v = live ? __ldg(src + ch) : make_uint4(0u, 0u, 0u, 0u);
+      *reinterpret_cast<uint4*>(smem + sw_chunk(c, ch)) = v;
+    }
+    fence_proxy_async_smem();  // generic-proxy stores, read by the tensor core (async proxy)
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (warp 0): TMA boxes
+    // lane p < 8 owns page p of each tile: it loads the page's block id one tile ahead (so the table
+    // round trip overlaps the previous tile) and issues the page's 2 x Dh/64 boxes.
+    constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
+    constexpr int kHalves = DH / 64;
+    const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
+    auto load_bid = [&](int j) { return lane < kTcTilePages && j * kTcTilePages + lane < npages
+                                            ? __ldg(table + pb + j * kTcTilePages + lane) : 0; };
+    int bid = load_bid(0);
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j % kTcStages;
+      if (j >= kTcStages) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
+        int ok = 1;
+        if (lane == 0) ok = tc_wait(empty + s, ((j / kTcStages) + 1) & 1, abort_flag, a.err) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+      const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+      const uint32_t kbase = stage_smem + s * L::kStageBytes, vbase = kbase + L::kTileBytes;
+      if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(live_pages) * 2 * kHalves * kBoxBytes);
+      __syncwarp();
+      const int next = load_bid(j + 1);
+      if (lane < live_pages) {
+        int slot = oob_slot;
+        if (bid >= 0 && bid < a.num_blocks)
+          slot = bid * kBlockSize;
+        else
+          flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+#pragma unroll
+        for (int h = 0; h < kHalves; ++h) {
+          const uint32_t off = h * (kTcTileTokens * 128) + lane * (kBlockSize * 128);
+          tma_load_3d(kbase + off, &tk, h * 64, kvh, slot, full + s);
+          tma_load_3d(vbase + off, &tv, h * 64, kvh, slot, full + s);
+        }
+      }
+      bid = next;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      for (int j = 0; j <= ntiles && !*abort_flag; ++j) {
+        if (j < ntiles) {
+          const int s = j % kTcStages, b = j & 1;
+          if (!tc_wait(full + s, (j / kTcStages) & 1, abort_flag, a.err)) break;
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const uint32_t kb = stage_smem + s * L::kStageBytes;
+#pragma unroll
+          for (int ks = 0; ks < DH / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
+            umma_ss(tmem + col_s(b), sw128_desc(q_smem + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
+                    ks > 0 ? 1u : 0u);
+          }
+          umma_commit(s_full + b);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, b = jj & 1, s = jj % kTcStages;
+          if (!tc_wait(p_full + b, (jj >> 1) & 1, abort_flag, a.err)) break;
+          tc_fence_after();
+          const uint32_t vb = stage_smem + s * L::kStageBytes + L::kTileBytes;
+          const int live_pages = min(kTcTilePages, npages - jj * kTcTilePages);  // one k-step per page
+          for (int ks = 0; ks < live_pages; ++ks)
+            umma_ts(tmem + kColO, tmem + col_p(b) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
+                    kIdescO, (jj > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(empty + s);
+          umma_commit(o_done);
+        }
+      }
+      umma_commit(final_bar);  // every MMA issued above has completed when this arrives
+      if (!tc_drain(final_bar, 0)) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax warpgroup: one query column each
+    const int row = threadIdx.x - 128;
+    const uint32_t lanes = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    float m_used = -__builtin_huge_valf(), l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1;
+      // keys of this tile: full pages up to the unit's end, minus pages with an out-of-range block id
+      // (lane p checks page p; loaded before the wait so the round trip overlaps it)
+      const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+      int my_bid = 0;
+      if (lane < live_pages) my_bid = __ldg(table + pb + j * kTcTilePages + lane);
+      if (!tc_wait(s_full + b, (j >> 1) & 1, abort_flag, a.err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[kTcTileTokens];
+#pragma unroll
+      for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_ld32(tmem + lanes + col_s(b) + 32 * i, sr + 32 * i);
+      const uint32_t bad = __ballot_sync(0xffffffffu, lane < live_pages && (my_bid < 0 || my_bid >= a.num_blocks));
+      tmem_wait_ld();
+      float mx = -__builtin_huge_valf();
+#pragma unroll
+      for (int k = 0; k < kTcTileTokens; ++k) {
+        const int p = k / kBlockSize;
+        const bool valid = p < live_pages && !((bad >> p) & 1u);
+        const float v = valid ? __uint_as_float(sr[k]) * a.sl2 : -__builtin_huge_valf();
+        sr[k] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      const bool need = mx > m_used + 8.f;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_new = need ? fmaxf(m_used, mx) : m_used;
+        if (j > 0) {
+          const float alpha = m_new == m_used ? 1.f : fast_exp2(m_used - m_new);
+          if (!tc_wait(o_done, (j - 1) & 1, abort_flag, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int i = 0; i < DH / 32; ++i) {
+            uint32_t orow[32];
+            tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 32; ++k) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
+            tmem_st32(tmem + lanes + kColO + 32 * i, orow);
+          }
+          tmem_wait_st();
+          l *= alpha;
+        }
+        m_used = m_new;
+      }
+      const float base = m_used == -__builtin_huge_valf() ? 0.f : m_used;
+      uint32_t pk[kTcTileTokens / 2];
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < kTcTileTokens; k += 2) {
+        const float p0 = fast_exp2(__uint_as_float(sr[k]) - base);
+        const float p1 = fast_exp2(__uint_as_float(sr[k + 1]) - base);
+        sum += p0 + p1;
+        pk[k / 2] = pack2<DT>(p0, p1);
+      }
+      l += sum;
+      tmem_st32(tmem + lanes + col_p(b), pk);
+      tmem_st32(tmem + lanes + col_p(b) + 32, pk + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(p_full + b);
+    }
+    if (ok && ntiles > 0 && tc_wait(o_done, (ntiles - 1) & 1, abort_flag, a.err)) {
+      tc_fence_after();
+      const int m = row / a.group;
+      bool live = m < mc;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      int64_t slot = 0;
+      if (live)
+        slot = (static_cast<int64_t>(__ldg(&a.members[mb + m].part_base)) + static_cast<int64_t>(piece) * a.tile_tokens) *
+                   a.h + kvh * a.group + row % a.group;
+      if (live && (slot < 0 || slot >= a.part_rows * a.h)) {  // a plan inconsistent with the workspace
+        flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+        live = false;
+      }
+#pragma unroll
+      for (int i = 0; i < DH / 32; ++i) {
+        uint32_t orow[32];
+        tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
+        tmem_wait_ld();
+        if (live) {
+          float4* dst = reinterpret_cast<float4*>(a.part_o + slot * DH + 32 * i);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dst[k] = make_float4(__uint_as_float(orow[4 * k]) * inv, __uint_as_float(orow[4 * k + 1]) * inv,
+                                 __uint_as_float(orow[4 * k + 2]) * inv, __uint_as_float(orow[4 * k + 3]) * inv);
+        }
+      }
+      if (live) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -__builtin_huge_valf();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Tensor map of one pool for the K/V boxes: dims {Dh, Hkv, num_blocks * 16}, box {64, 1, 16}, 128-byte
+// swizzle, zero fill out of bounds.  Encoded maps are cached per (address, shape, dtype): a serving loop
+// reuses the same pools every step.
+cudaError_t pool_tensor_map(CUtensorMap* out, const void* pool, int dtype, int64_t num_blocks, int hkv, int dh) {
+  static std::mutex mu;
+  static EncodeTiledFn encode = nullptr;
+  static std::unordered_map<std::string, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+    encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  char key[96];
+  snprintf(key, sizeof key, "%p/%d/%lld/%d/%d", pool, dtype, static_cast<long long>(num_blocks), hkv, dh);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return cudaSuccess;
+  }
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(dh), static_cast<cuuint64_t>(hkv),
+                              static_cast<cuuint64_t>(num_blocks) * kBlockSize};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(dh) * 2, static_cast<cuuint64_t>(hkv) * dh * 2};
+  const cuuint32_t box[3] = {64, 1, kBlockSize};
+  const cuuint32_t elem[3] = {1, 1, 1};
+  const CUresult r = encode(out, dtype == MLB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                            3, const_cast<void*>(pool), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  if (cache.size() >= 1024) cache.clear();  // bounded: pools are few, a churn of new ones restarts it
+  cache.emplace(key, *out);
+  return cudaSuccess;
+}
+
+template <int DT, int DH>
+cudaError_t launch_tc(const AttnArgs& a, int64_t units, cudaStream_t s) {
+  constexpr int bytes = TcLayout<DH>::kLaunchBytes;
+  static_assert(bytes <= 232448, "shared memory budget of one sm_100 CTA");
+  static unsigned long long done = 0;
+  auto k = shared_prefix_tc_kernel<DT, DH>;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (!(dev < 64 && (done >> dev) & 1ull)) {
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) __atomic_fetch_or(&done, 1ull << dev, __ATOMIC_RELAXED);
+  }
+  CUtensorMap tk, tv;
+  e = pool_tensor_map(&tk, a.k_cache, DT, a.num_blocks, a.hkv, DH);
+  if (e == cudaSuccess) e = pool_tensor_map(&tv, a.v_cache, DT, a.num_blocks, a.hkv, DH);
+  if (e != cudaSuccess) return e;
+  return launch_k(k, dim3(static_cast<unsigned>(units * a.hkv)), dim3(kTcThreads), bytes, s, a, tk, tv);
+}
+
+}  // namespace
+
+// True when the tcgen05 kernel takes this launch: 16-bit pools, head_dim 64 or 128, q rows 16-byte aligned,
+// pool slots addressable by the tensor maps' 32-bit coordinates.
+bool shared_prefix_tc_supported(const AttnArgs& a, int dtype, int dh) {
+  if ((dtype != MLB_BF16 && dtype != MLB_F16) || (dh != 64 && dh != 128)) return false;
+  if (a.num_blocks * kBlockSize >= INT32_MAX) return false;
+  return reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.q_st % 8 == 0 && a.q_sh % 8 == 0;
+}
+
+cudaError_t launch_shared_prefix_tc(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
+  if (dtype == MLB_BF16) {
+    if (dh == 64) return launch_tc<MLB_BF16, 64>(a, num_units, s);
+    if (dh == 128) return launch_tc<MLB_BF16, 128>(a, num_units, s);
+  } else if (dtype == MLB_F16) {
+    if (dh == 64) return launch_tc<MLB_F16, 64>(a, num_units, s);
+    if (dh == 128) return launch_tc<MLB_F16, 128>(a, num_units, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace mlb

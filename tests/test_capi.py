@@ -196,7 +196,8 @@ def test_planner_finds_shared_prefixes(mlb):
     assert pieces[0][0] == 0 and pieces[-1][1] == 40 and all(a[1] == b[0] for a, b in zip(pieces, pieces[1:]))
     npieces = len(pieces)
     for mb, mc, pb, pe, piece, tseq, *_ in su.tolist():
-        assert 0 < mc <= 16 and tseq in range(20)
+        assert 0 < mc <= 128 // 4 and tseq in range(20)  # one unit: at most 128 query columns
+        assert (pe - pb) % 8 == 0 or pe == 40  # pieces are whole 8-page (128-key) tiles but the last
     per_member = {m: 0 for m in range(len(members))}
     for mb, mc, *_ in su.tolist():
         for m in range(mb, mb + mc):

@@ -163,20 +163,33 @@ def test_tolerances_are_the_north_star():
     assert TOL[torch.bfloat16] == 2e-2 and TOL[torch.float32] == 1e-5
 
 
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("rows_a", [18, 45])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
 @pytest.mark.parametrize("h,hkv,dh", [(32, 8, 128), (8, 8, 64), (16, 2, 128), (8, 1, 256), (12, 4, 64)])
-def test_shared_prefix_units_match_oracle(mlb, cuda, dtype, h, hkv, dh):
+def test_shared_prefix_units_match_oracle(mlb, cuda, dtype, h, hkv, dh, rows_a, tc):
     """Rows whose tables share leading blocks (prefix-cache hits) are attended through shared-prefix units
-    (one page load per block of rows) plus their own pages; results must equal the oracle's."""
+    (one page load per block of rows) plus their own pages; results must equal the oracle's.  Both kernels
+    of the shared units: tcgen05 (128-column tiles; head_dim 64 / 128) and mma.sync (every head_dim); 45
+    rows need two units of 128 columns at GQA 4, and the 9-page prefix ends in a partial 128-key tile."""
+    lib = mlb._lib.lib()
+    prev = lib.mlb_set_tensor_core_prefix(tc)
+    try:
+        _shared_prefix_case(mlb, cuda, dtype, h, hkv, dh, rows_a)
+    finally:
+        lib.mlb_set_tensor_core_prefix(prev)
+
+
+def _shared_prefix_case(mlb, cuda, dtype, h, hkv, dh, rows_a):
     r = random.Random(h * 100 + dh)
-    nb = 400
+    nb = 1200
     ids = list(range(nb))
     r.shuffle(ids)
     shared_a, shared_b = ids[:24], ids[24:33]  # two prefixes: 24 and 9 full pages
     nxt = 33
     steps, blocks = [], []
-    for i in range(27):
-        prefix = shared_a if i < 18 else shared_b
+    for i in range(rows_a + 9):
+        prefix = shared_a if i < rows_a else shared_b
         ctx = len(prefix) * 16 + r.randint(1, 70)
         own = -(-ctx // 16) - len(prefix)
         steps.append((ctx - 1, 1))
@@ -192,5 +205,5 @@ def test_shared_prefix_units_match_oracle(mlb, cuda, dtype, h, hkv, dh):
     meta = mlb.AttentionMetadata.build([mlb.SeqStep(c, n, list(b)) for c, n, b in case.seqs], 16, cuda)
     backend = mlb.B200Backend()
     out = backend.forward(t["q"], t["k"], t["v"], t["k_pool"], t["v_pool"], meta)
-    assert backend._plan.num_shared_units > 0 and len(backend._plan.members_host) == 27
+    assert backend._plan.num_shared_units > 0 and len(backend._plan.members_host) == rows_a + 9
     assert_close(out, oracle_forward(case, dtype)[0], dtype)
