@@ -7,8 +7,8 @@
 // columns (the TMEM lanes) per CTA and 128 keys (8 pages) per tile.
 //
 // Roles in one CTA of 256 threads (1 CTA per SM: ~225 KB of shared memory, all 512 TMEM columns):
-// - warp 0, one thread: the producer.  Each page of a tile is 2 x Dh/64 TMA boxes (tensor maps over the
-//   K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle), landing directly in the K-major
+// - warps 0, 2, 3: the producers (one lane per page).  Each page of a tile is 2 x Dh/64 TMA boxes (tensor
+//   maps over the K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle), landing in the K-major
 //   layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts the bytes
 //   (expect_tx).  A block id out of range gets a slot coordinate past the pool's end: TMA fills zeros
 //   there and the softmax masks the page.  3 stages.  (16-byte cp.async from 96 threads measured 3.8 us
@@ -18,7 +18,6 @@
 //   V as an MN-major B operand (one k-step of 16 keys per loaded page, so pages past the unit's end are
 //   never read), committed to the stage's "empty" barrier and to o_done.  Issuing S_j
 //   before O_{j-1} lets the tensor core compute the next scores while the softmax warps work.
-// - warps 2-3: idle (they keep the softmax warps on a warpgroup boundary: TMEM lane quarter = warp % 4).
 // - warps 4-7 (a warpgroup; thread = one query column = one TMEM lane): read the S row from TMEM, mask,
 //   running max in the exp2 domain, P = 2^(s - m) packed to 16 bits into TMEM buffer j % 2, row sums in
 //   fp32.  O is rescaled (TMEM load / scale / store) only when a row's max grows by more than 8 (a factor
@@ -47,6 +46,7 @@ constexpr int kTcStages = 3;
 constexpr int kTcRows = 128;        // query columns per CTA = MMA M = TMEM lanes
 constexpr int kTcTileTokens = 128;  // keys per tile = N of S = Q . K^T
 constexpr int kTcTilePages = kTcTileTokens / kBlockSize;
+constexpr int kTcProducerWarps = 3;  // warps 0, 2, 3
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColO = 256;
 __device__ __forceinline__ uint32_t col_s(int b) { return b ? 128u : 0u; }    // S buffers
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(full + s, 1);
+      mbar_init(full + s, kTcProducerWarps);
       mbar_init(empty + s, 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -247,15 +247,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer (warp 0): TMA boxes
-    // lane p < 8 owns page p of each tile: it loads the page's block id one tile ahead (so the table
-    // round trip overlaps the previous tile) and issues the page's 2 x Dh/64 boxes.
+  if (warp == 0 || warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ producers (warps 0, 2, 3): TMA boxes
+    // Producer warp w (index pw 0..2) owns pages pw, pw + 3, pw + 6 of each tile, one per lane: the lane
+    // loads its page's block id one tile ahead (the table round trip overlaps the previous tile) and
+    // issues the page's 2 x Dh/64 boxes; the warp's lane 0 declares the warp's bytes on the stage barrier
+    // (3 arrivals per phase).  Three warps issue a tile's boxes in parallel.
     constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
     constexpr int kHalves = DH / 64;
+    const int pw = warp == 0 ? 0 : warp - 1;
+    const int page_in_tile = pw + kTcProducerWarps * lane;
+    const bool mine = lane < (kTcTilePages - pw + kTcProducerWarps - 1) / kTcProducerWarps;
     const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
-    auto load_bid = [&](int j) { return lane < kTcTilePages && j * kTcTilePages + lane < npages
-                                            ? __ldg(table + pb + j * kTcTilePages + lane) : 0; };
+    auto load_bid = [&](int j) {
+      const int page = j * kTcTilePages + page_in_tile;
+      return mine && page < npages ? __ldg(table + pb + page) : 0;
+    };
     int bid = load_bid(0);
     for (int j = 0; j < ntiles; ++j) {
       const int s = j % kTcStages;
@@ -265,11 +272,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       }
       const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+      const int my_pages = live_pages > pw ? (live_pages - pw + kTcProducerWarps - 1) / kTcProducerWarps : 0;
       const uint32_t kbase = stage_smem + s * L::kStageBytes, vbase = kbase + L::kTileBytes;
-      if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(live_pages) * 2 * kHalves * kBoxBytes);
+      if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(my_pages) * 2 * kHalves * kBoxBytes);
       __syncwarp();
       const int next = load_bid(j + 1);
-      if (lane < live_pages) {
+      if (lane < my_pages) {
         int slot = oob_slot;
         if (bid >= 0 && bid < a.num_blocks)
           slot = bid * kBlockSize;
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
           flag_error(a.err, MLB_DEV_BLOCK_RANGE);
 #pragma unroll
         for (int h = 0; h < kHalves; ++h) {
-          const uint32_t off = h * (kTcTileTokens * 128) + lane * (kBlockSize * 128);
+          const uint32_t off = h * (kTcTileTokens * 128) + page_in_tile * (kBlockSize * 128);
           tma_load_3d(kbase + off, &tk, h * 64, kvh, slot, full + s);
           tma_load_3d(vbase + off, &tv, h * 64, kvh, slot, full + s);
         }
@@ -341,15 +349,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_ld32(tmem + lanes + col_s(b) + 32 * i, sr + 32 * i);
       const uint32_t bad = __ballot_sync(0xffffffffu, lane < live_pages && (my_bid < 0 || my_bid >= a.num_blocks));
       tmem_wait_ld();
-      float mx = -__builtin_huge_valf();
+      // raw scores stay in sr; masked keys become -inf (only on a partial tile or a bad page)
+      if (live_pages < kTcTilePages || bad) {
 #pragma unroll
-      for (int k = 0; k < kTcTileTokens; ++k) {
-        const int p = k / kBlockSize;
-        const bool valid = p < live_pages && !((bad >> p) & 1u);
-        const float v = valid ? __uint_as_float(sr[k]) * a.sl2 : -__builtin_huge_valf();
-        sr[k] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        for (int k = 0; k < kTcTileTokens; ++k) {
+          const int p = k / kBlockSize;
+          if (p >= live_pages || ((bad >> p) & 1u)) sr[k] = __float_as_uint(-__builtin_huge_valf());
+        }
       }
+      float mraw = -__builtin_huge_valf();
+#pragma unroll
+      for (int k = 0; k < kTcTileTokens; ++k) mraw = fmaxf(mraw, __uint_as_float(sr[k]));
+      const float mx = mraw * a.sl2;  // the scale is positive: max commutes with it
       const bool need = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? fmaxf(m_used, mx) : m_used;
@@ -374,13 +385,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         }
         m_used = m_new;
       }
-      const float base = m_used == -__builtin_huge_valf() ? 0.f : m_used;
+      const float nbase = m_used == -__builtin_huge_valf() ? 0.f : -m_used;
+      const float sl2 = a.sl2;
       uint32_t pk[kTcTileTokens / 2];
       float sum = 0.f;
 #pragma unroll
-      for (int k = 0; k < kTcTileTokens; k += 2) {
-        const float p0 = fast_exp2(__uint_as_float(sr[k]) - base);
-        const float p1 = fast_exp2(__uint_as_float(sr[k + 1]) - base);
+      for (int k = 0; k < kTcTileTokens; k += 2) {  // p = 2^(s * scale * log2 e - m): one FFMA + EX2 per key
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[k]), sl2, nbase));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[k + 1]), sl2, nbase));
         sum += p0 + p1;
         pk[k / 2] = pack2<DT>(p0, p1);
       }
