@@ -594,22 +594,89 @@ def run_ours(args) -> None:
 
 
 def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx) -> dict:
-    """Each step: AttentionMetadata.build (host -> device), then per layer the q/k/v rows copied from pinned
-    host memory, the public backend's forward, and the output copied back to pinned host memory."""
+    """Each step, through the public API with pinned host buffers: AttentionMetadata.build (its own H2D
+    copies); the q/k/v rows of every layer copied host-to-device on a loader stream in 4 growing chunks
+    (layers [0,1), [1,3), [3,8), [8,L): each lands while the layers before it compute); per layer the
+    backend's forward once its chunk is in, and a device-to-host copy of its output on a copier stream
+    (layer l's read-back overlaps layer l + 1's attention); the step ends when the last output is on the
+    host.  One GPU: the outputs go into one step-wide device buffer (forward's out_targets) and come back
+    in 4 chunks."""
     layers = len(k_pools)
-    qh, kh, vh = q.cpu().pin_memory(), k.cpu().pin_memory(), v.cpu().pin_memory()
+    sizes = [t.numel() * t.element_size() for t in (q, k, v)]
+    per_layer = sum(sizes)
+    host_in = torch.empty(layers * per_layer, dtype=torch.uint8).pin_memory()
+    dev_in = torch.empty(layers * per_layer, dtype=torch.uint8, device=dev)
+
+    def views(buf, l):
+        out, off = [], l * per_layer
+        for t, n in zip((q, k, v), sizes):
+            out.append(buf[off:off + n].view(t.dtype).view(t.shape))
+            off += n
+        return out
+
+    for l in range(layers):
+        for dst, src in zip(views(host_in, l), (q, k, v)):
+            dst.copy_(src.cpu())
+    dev_views = [views(dev_in, l) for l in range(layers)]
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]
-    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     backend = sharding.KVHeadShardedBackend(transport=args.transport) if world > 1 else mlb.B200Backend()
+    p2p_ring = world > 1 and args.transport == "p2p"
+    # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer, read back
+    # in 4 shrinking chunks (a side-stream copy per layer costs ~60 us of host time: 32 per step made the
+    # step host-bound)
+    direct = world == 1
+    if direct:
+        dev_out = torch.empty((layers, *q.shape), dtype=q.dtype, device=dev)
+        host_out = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
+        o_edges = sorted({0, layers} | {b for b in (layers // 2, layers - 4, layers - 1) if 0 < b < layers})
+        o_chunks = list(zip(o_edges[:-1], o_edges[1:]))
+        o_last = {hi - 1: (lo, hi) for lo, hi in o_chunks}
+        targets = [mlb.ops.out_targets([dev_out[l].data_ptr()], 0, q.shape[1] * q.shape[2], q.shape[2])
+                   for l in range(layers)]
+    compute = torch.cuda.current_stream(dev)
+    loader, copier = torch.cuda.Stream(dev), torch.cuda.Stream(dev)  # H2D of inputs, D2H of outputs
+    # chunk boundaries: layer 0's inputs alone, then chunks that land while the layers before them compute
+    edges = sorted({0, layers} | {b for b in (1, 3, 8) if b < layers})
+    chunks = list(zip(edges[:-1], edges[1:]))
+    chunk_of = {lo: c for c, (lo, _) in enumerate(chunks)}
+    loaded = [torch.cuda.Event() for _ in chunks]  # inputs of a chunk of layers on the device
+    done = [torch.cuda.Event() for _ in range(layers)]  # output l read back
+    ready = [torch.cuda.Event() for _ in range(layers)]  # output l computed
+    step_done = torch.cuda.Event()
+    step_done.record(compute)
 
     def step():
         meta = mlb.AttentionMetadata.build(seqs, BS, dev)
+        loader.wait_event(step_done)  # the previous step has read every layer's inputs
+        with torch.cuda.stream(loader):  # the step's q/k/v rows in a few growing chunks
+            for c, (lo, hi) in enumerate(chunks):
+                dev_in[lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer], non_blocking=True)
+                loaded[c].record(loader)
         for l in range(layers):
-            qd.copy_(qh, non_blocking=True)
-            kd.copy_(kh, non_blocking=True)
-            vd.copy_(vh, non_blocking=True)
+            if l in chunk_of:
+                compute.wait_event(loaded[chunk_of[l]])
+            if p2p_ring and l >= 2:  # a p2p-gathered output is a 2-slot ring view: read back before reuse
+                compute.wait_event(done[l - 2])
+            qd, kd, vd = dev_views[l]
+            if direct:
+                backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[l])
+                if l in o_last:  # a chunk of layers is complete: read it back on the side stream
+                    lo, hi = o_last[l]
+                    ready[l].record(compute)
+                    copier.wait_event(ready[l])
+                    with torch.cuda.stream(copier):
+                        host_out[lo:hi].copy_(dev_out[lo:hi], non_blocking=True)
+                continue
             out = backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)
-            outs[l].copy_(out, non_blocking=True)
+            ready[l].record(compute)
+            copier.wait_event(ready[l])
+            with torch.cuda.stream(copier):
+                outs[l].copy_(out, non_blocking=True)
+                done[l].record(copier)
+            if not p2p_ring:  # a fresh tensor from torch's allocator: keep it alive until the copy ran
+                out.record_stream(copier)
+        compute.wait_stream(copier)
+        step_done.record(compute)
 
     for _ in range(max(1, args.warmup)):
         step()
@@ -629,12 +696,13 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         backend.close()
     total = kv_bytes(ctx, HKV) * layers
     meta_bytes = _meta_bytes(mlb, seqs)
-    h2d = layers * (q.numel() + k.numel() + v.numel()) * q.element_size() + meta_bytes
+    h2d = layers * per_layer + meta_bytes
     d2h = layers * q.numel() * q.element_size()
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "path": (f"KVHeadShardedBackend(transport={args.transport!r})" if world > 1 else "B200Backend")
-                    + ".forward per layer, pinned host I/O"}
+                    + ".forward per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "
+                      "D2H of the outputs " + ("in 4 chunks" if direct else "per layer")}
 
 
 def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:

@@ -29,7 +29,13 @@ def _code(t: torch.Tensor, what: str) -> int:
         raise ValueError(f"{what}: dtype {t.dtype} not supported (float32, float16, bfloat16)") from None
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    """Handle of torch's current stream on `device` (the raw query: a decode step makes ~100 of these)."""
+    if _raw_stream is not None and device.index is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 

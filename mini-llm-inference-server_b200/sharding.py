@@ -26,7 +26,7 @@ import torch.distributed as dist
 
 from . import _lib
 from .attention.base import AttentionBackend
-from .ops import out_targets
+from .ops import _stream, out_targets
 
 
 def head_range(rank: int, world: int, num_heads: int) -> slice:
@@ -125,7 +125,7 @@ class PeerOutputs:
     def barrier(self) -> None:
         rc = _lib.lib().mlb_peer_barrier(self._flags, self.rank, self.world, self._own + self._epoch_off,
                                          self.timeout_ns, self.err.data_ptr(),
-                                         torch.cuda.current_stream(self.device).cuda_stream)
+                                         _stream(self.device))
         _lib.check(rc, "peer_barrier")
 
     def raise_errors(self) -> None:
