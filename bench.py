@@ -300,6 +300,20 @@ def cpu_reference_step(wl: Workload, nb_sample_seqs: int, seed: int = 7):
                                        "1 layer, bf16")
 
 
+def host_info() -> dict:
+    """The host the CPU legs ran on: logical cores, torch's thread count, CPU model."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"os_cpu_count": os.cpu_count(), "torch_threads": torch.get_num_threads(), "cpu_model": model}
+
+
 def run_cpu_baseline(wl: Workload, seqs: int, reps: int, warmup: int = 1) -> dict:
     step, nbytes, sample = cpu_reference_step(wl, seqs)
     for _ in range(warmup):
@@ -309,7 +323,7 @@ def run_cpu_baseline(wl: Workload, seqs: int, reps: int, warmup: int = 1) -> dic
         step()
     dt = (time.perf_counter() - t0) / reps
     return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-            "sample": sample + f", {reps} reps", "ms_per_step": round(dt * 1e3, 2)}
+            "sample": sample + f", {reps} reps", "ms_per_step": round(dt * 1e3, 2), "host": host_info()}
 
 
 def run_reference_arm(args) -> None:
@@ -317,7 +331,10 @@ def run_reference_arm(args) -> None:
     if rank != 0:
         return  # the CPU arm runs once, on rank 0 only
     torch.set_num_threads(os.cpu_count() or 1)
-    step, nbytes, sample = cpu_reference_step(config2(args.batch), args.cpu_sample_seqs)
+    # the same workload as our arm at this N (weak scaling: batch x N), timed on a bounded sample of it
+    weak = args.gpus > 1 and args.scaling == "weak"
+    wl = config2(args.batch * (args.gpus if weak else 1))
+    step, nbytes, sample = cpu_reference_step(wl, args.cpu_sample_seqs)
     for _ in range(args.warmup):
         step()
     t0 = time.perf_counter()
@@ -328,11 +345,10 @@ def run_reference_arm(args) -> None:
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config 2: Llama-3.1-8B decode attention, B64 ctx U[512,4096], bf16",
-                   "sample": sample},
+        "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{wl.name}: {wl.describe}", "sample": sample},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port",
-                         "sample": sample},
+                         "sample": sample, "host": host_info()},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
