@@ -60,7 +60,7 @@ class Workload:
     name: str
     describe: str
     append_rows: list  # (num_cached, num_new, block_ids)
-    attend_rows: list  # (num_cached, num_new, block_ids); decode rows
+    attend_rows: list  # (num_cached, num_new, block_ids): the rows that attend (decode or multi-token)
     num_blocks: int
     copy_src: list = field(default_factory=list)
     copy_dst: list = field(default_factory=list)
@@ -96,11 +96,12 @@ def config2(batch: int = 64, seed: int = 1234) -> Workload:
                     kv_scale=0.5)
 
 
-def config3(seed: int = 33) -> Workload:
+def config3(seed: int = 33, attend_chunks: bool = False) -> Workload:
     """256 decode rows with context lognormal(median 1024, sigma 1) capped at 32768, and a
     varlen append of 8 prefill chunks of U[1, 2048] tokens.  Blocks come from a seeded random permutation of a
-    pool 1.25x the need, so every table is scattered (a fragmented pool).  The chunks only append here; their
-    attention is a prefill kernel's job."""
+    pool 1.25x the need, so every table is scattered (a fragmented pool).  In BASELINE the chunks only append;
+    with attend_chunks (--attend-chunks) they also attend causally over themselves, as an engine's chunked
+    prefill does (multi-token rows, paged_torch_ref.py:61-73)."""
     r = np.random.default_rng(seed)
     ctx = np.clip(np.rint(1024.0 * np.exp(r.standard_normal(256))), 1, 32768).astype(np.int64)
     chunks = r.integers(1, 2049, size=8).astype(np.int64)
@@ -110,6 +111,12 @@ def config3(seed: int = 33) -> Workload:
     blocks = _take(perm, np.concatenate([pages, cpages]))
     decode = [(int(c) - 1, 1, b) for c, b in zip(ctx, blocks[:256])]
     prefill = [(0, int(n), b) for n, b in zip(chunks, blocks[256:])]
+    if attend_chunks:
+        return Workload("config 3", "mixed step: 256 decode rows ctx lognormal(1024, 1.0) <= 32768 + 8 prefill "
+                        "chunks U[1,2048] appended AND attending causally, fragmented pool, 32 layer pools",
+                        decode + prefill, decode + prefill, nb,
+                        info={"chunk_tokens": int(chunks.sum()), "decode_ctx_sum": int(ctx.sum()),
+                              "chunks_attend": True})
     return Workload("config 3", "mixed step: 256 decode rows ctx lognormal(1024, 1.0) <= 32768 + varlen append of "
                     "8 prefill chunks U[1,2048], fragmented pool, 32 layer pools", decode + prefill, decode, nb,
                     info={"chunk_tokens": int(chunks.sum()), "decode_ctx_sum": int(ctx.sum())})
@@ -377,10 +384,16 @@ def run_ours(args) -> None:
     mlb._lib.lib().mlb_set_tensor_core_prefix(0 if args.no_tc_prefix else 1)
 
     weak = world > 1 and args.config == 2 and args.scaling == "weak"
-    wl = config2(args.batch * (world if weak else 1)) if args.config == 2 else WORKLOADS[args.config]()
+    if args.config == 2:
+        wl = config2(args.batch * (world if weak else 1))
+    elif args.config == 3:
+        wl = config3(attend_chunks=args.attend_chunks)
+    else:
+        wl = WORKLOADS[args.config]()
     layers = args.layers or wl.layers
     hkv_l, h_l = HKV // world, H // world
     n_app, n_att = sum(n for _, n, _ in wl.append_rows), len(wl.attend_rows)
+    n_q = sum(n for _, n, _ in wl.attend_rows)  # query tokens (one per decode row; a prefill row has many)
     nb = wl.num_blocks
 
     g = torch.Generator(device=dev).manual_seed(100 + rank)
@@ -391,7 +404,7 @@ def run_ours(args) -> None:
             p.normal_(0.0, wl.kv_scale, generator=g)
             pools.append(p)
     gq = torch.Generator(device=dev).manual_seed(7)  # the same full q/k/v on every rank
-    q = torch.randn(n_att, H, DH, device=dev, generator=gq).to(torch.bfloat16)
+    q = torch.randn(n_q, H, DH, device=dev, generator=gq).to(torch.bfloat16)
     k = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
     v = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
     qs, ks = sharding.head_range(rank, world, H), sharding.head_range(rank, world, HKV)
@@ -403,12 +416,16 @@ def run_ours(args) -> None:
     meta_att = mlb.AttentionMetadata.build(seqsteps(wl.attend_rows), BS, dev)
     meta_app = meta_att if wl.append_rows is wl.attend_rows else mlb.AttentionMetadata.build(
         seqsteps(wl.append_rows), BS, dev)
-    plan = mlb.B200Backend().plan(meta_att, h_l, hkv_l, dev)
+    if args.no_query_tiles:  # every row on 8-column work units (no host tables: no query tiles, no cascade)
+        plan = ops.plan_attention(meta_att.query_start_loc, meta_att.seq_lens, meta_att.block_tables_i32.shape[1],
+                                  h_l, hkv_l, dev)
+    else:
+        plan = mlb.B200Backend().plan(meta_att, h_l, hkv_l, dev)
     ws = ops.Workspace()
-    out_l = torch.empty(n_att, h_l, DH, device=dev, dtype=torch.bfloat16)
+    out_l = torch.empty(n_q, h_l, DH, device=dev, dtype=torch.bfloat16)
     p2p = world > 1 and args.transport == "p2p"
-    gathered = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None
-    peers = sharding.PeerOutputs(n_att, H, DH, torch.bfloat16, dev) if p2p else None
+    gathered = torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None
+    peers = sharding.PeerOutputs(n_q, H, DH, torch.bfloat16, dev) if p2p else None
     copies = len(wl.copy_src)
     if copies:
         ptrs = ops.pool_pointer_table(k_pools + v_pools)
@@ -519,13 +536,13 @@ def run_ours(args) -> None:
 
         peers.raise_errors()
         last = layers - 1
-        got = peers.output(last % peers.slots, n_att).clone()
+        got = peers.output(last % peers.slots, n_q).clone()
         ops.attention_partials(q_l, k_pools[last], v_pools[last], meta_att.block_tables_i32, meta_att.seq_lens_i32,
                                meta_att.qo_indptr, plan, ws, out_l)
         ops.splitk_reduce(plan, ws, out_l)
-        flat = torch.empty(world * n_att, h_l, DH, device=dev, dtype=torch.bfloat16)
+        flat = torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16)
         dist.all_gather_into_tensor(flat, out_l)
-        want = flat.view(world, n_att, h_l, DH).movedim(0, 1).reshape(n_att, H, DH)
+        want = flat.view(world, n_q, h_l, DH).movedim(0, 1).reshape(n_q, H, DH)
         if not torch.equal(got, want):
             raise SystemExit(f"rank {rank}: p2p-gathered output differs from the NCCL all-gather")
         del got, want, flat
@@ -561,7 +578,8 @@ def run_ours(args) -> None:
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "decode_rows": n_att,
+            "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "attend_rows": n_att,
+                       "query_tokens": n_q,
                        "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
                        "parallelism": (f"kv-head shard x{world}, output gather: "
                                        + ("kernel NVLink stores + flag barrier" if p2p else "NCCL all-gather"))
@@ -776,6 +794,10 @@ def main() -> None:
     ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
+    ap.add_argument("--attend-chunks", action="store_true",
+                    help="config 3: the prefill chunks also attend (multi-token rows on query tiles)")
+    ap.add_argument("--no-query-tiles", action="store_true",
+                    help="plan without host tables: every row on the decode kernel's 8-column units")
     ap.add_argument("--no-tc-prefix", action="store_true",
                     help="shared-prefix units on the mma.sync kernel instead of tcgen05")
     args = ap.parse_args()

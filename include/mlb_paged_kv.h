@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 3 */
+MLB_API int mlb_abi_version(void);  /* 4 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -100,11 +100,19 @@ typedef struct {
 } mlb_work_unit;
 
 /*
- * Shared-prefix work (a prefix-cache hit seen by many decode rows): pages [page_begin, page_end) are the
- * same blocks in the tables of members [member_begin, member_begin + member_count) of the members array,
- * and the table row of sequence `table_seq` holds them.  One CTA per (unit, KV head) loads each page once
- * and applies it to every member's query heads (up to 128 query columns: member_count <= 128 / group),
- * writing each member's partial row members[m].part_base + piece * tokens_per_tile.
+ * Units of query-tile work for the tensor-core kernel (one CTA per (unit, KV head), up to 128 query
+ * columns = tokens x query heads of one KV head), of two kinds (reserved[0] & 0xff):
+ * kind 0, a shared prefix (a prefix-cache hit seen by many decode rows): pages [page_begin, page_end) are
+ *   the same blocks in the tables of members [member_begin, member_begin + member_count) of the members
+ *   array (member_count <= 128 / group), and the table row of sequence `table_seq` holds them.  Each page
+ *   is loaded once and applied to every member's query heads; every key is visible.  Each member writes
+ *   its partial row members[m].part_base + piece * tokens_per_tile.
+ * kind 1, a query tile of a multi-token row (a prefill chunk on cache): tokens member_begin ..
+ *   member_begin + member_count - 1 (global token indices, member_count <= 128 / group) of sequence
+ *   table_seq against its pages [page_begin, page_end), causal (token i of the row sees keys up to its own
+ *   position).  piece < 0: the unit covers every key its tokens see and writes the final rows; otherwise
+ *   it is piece `piece` of (reserved[0] >> 8) and token m's partial row is
+ *   reserved[1] + (m * pieces + piece) * tokens_per_tile.
  */
 typedef struct {
   int32_t member_begin;
@@ -129,9 +137,10 @@ typedef struct {
  * Inputs: qo_indptr [num_seqs + 1] and seq_lens [num_seqs] exactly as AttentionMetadata holds them
  * (metadata.py:39-40, :97-98); max_blocks_per_seq = block_tables width (validates seq_lens).
  * block_tables_host (optional, may be NULL): a host copy of the int32 block tables with row stride
- * bt_stride_host; when given, decode rows whose tables start with the same run of block ids (shared
- * prefix blocks) get shared-prefix units (a cascade split).  pages_per_unit = 0 picks a split size from
- * the total work and num_sms.
+ * bt_stride_host; pass it for 16-bit pools only.  When given, decode rows whose tables start with the same
+ * run of block ids (shared prefix blocks) get shared-prefix units (a cascade split), and rows of >= 16 new
+ * tokens get query-tile units (kind 1 above) instead of 8-column work units.  pages_per_unit = 0 picks a
+ * split size from the total work and num_sms.
  * With units == NULL only the counts are returned (*num_units, *num_shared_units, *num_members,
  * *num_partial_rows); otherwise every output array must hold its count (MLB_ENOSPACE if not).
  * reduce_rows / reduce_chunks [num_tokens]: first partial row and number of pieces per token (pieces

@@ -22,7 +22,7 @@ EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_atten
            "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc", "mlb_ipc_alloc", "mlb_ipc_open",
            "mlb_ipc_close", "mlb_ipc_free", "mlb_peer_barrier", "mlb_set_programmatic_launch",
            "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix")
-ABI_VERSION = 3
+ABI_VERSION = 4
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 MAX_OUT_DESTS = 8  # MLB_MAX_OUT_DESTS
 IPC_HANDLE_BYTES = 64  # MLB_IPC_HANDLE_BYTES
@@ -36,7 +36,8 @@ class WorkUnit(ctypes.Structure):
 
 
 class SharedUnit(ctypes.Structure):
-    """mlb_shared_unit: a page range of a shared prefix, attended once for a block of member rows."""
+    """mlb_shared_unit: query-tile work for the tensor-core kernel: a page range of a shared prefix attended
+    once for a block of member rows (kind 0), or a tile of a multi-token row's tokens (kind 1)."""
 
     _fields_ = [("member_begin", c_int32), ("member_count", c_int32), ("page_begin", c_int32),
                 ("page_end", c_int32), ("piece", c_int32), ("table_seq", c_int32), ("reserved", c_int32 * 2)]

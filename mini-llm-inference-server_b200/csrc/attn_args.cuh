@@ -86,6 +86,16 @@ __device__ __forceinline__ void store_out_n(const mlb_out_targets& t, bool vec, 
 }
 
 
+// Store one output element (token tok, head of this call, dim d) into every destination.
+template <int DT>
+__device__ __forceinline__ void store_out1(const mlb_out_targets& t, int64_t tok, int head, int d, float v) {
+  const int64_t off = (tok * t.stride_tok + static_cast<int64_t>(t.head_offset + head) * t.stride_head + d) *
+                      Elt<DT>::bytes;
+#pragma unroll
+  for (int i = 0; i < MLB_MAX_OUT_DESTS; ++i)
+    if (i < t.num_dests) store_f32<DT>(static_cast<char*>(t.dests[i]) + off, v);
+}
+
 template <int B>
 __device__ __forceinline__ void load_bytes(const char* p, uint32_t* w) {
   if constexpr (B == 4) {

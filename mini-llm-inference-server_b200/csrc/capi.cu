@@ -60,6 +60,8 @@ constexpr int kSharedColumns = 128;  // query columns (member rows x group) per 
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
 constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages
+constexpr int kPrefillMinTokens = 16;   // multi-token rows this long go to tensor-core query tiles ...
+constexpr int kPrefillPiecePages = 128;  // ... split into pieces of at most this many pages (16 MMA tiles)
 
 int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
 
@@ -191,7 +193,7 @@ extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 3; }
+int mlb_abi_version(void) { return 4; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -252,6 +254,18 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   if (rc != MLB_OK) return rc;
   const int tpt = tokens_per_tile(num_heads, num_kv_heads);
   const int group_size = num_heads / num_kv_heads;
+
+  // ---- multi-token rows (prefill chunks on cache) of >= kPrefillMinTokens tokens: with host tables
+  // (16-bit pools) they are planned as query tiles of 128 columns below instead of 8-column groups
+  std::vector<int> prefill_seqs;
+  if (block_tables_host && bt_stride_host > 0) {
+    std::vector<char> is_prefill(num_seqs, 0);
+    for (int s = 0; s < num_seqs; ++s)
+      if (qo_indptr[s + 1] - qo_indptr[s] >= kPrefillMinTokens) is_prefill[s] = 1, prefill_seqs.push_back(s);
+    if (!prefill_seqs.empty())
+      groups.erase(std::remove_if(groups.begin(), groups.end(), [&](const Group& g) { return is_prefill[g.seq]; }),
+                   groups.end());
+  }
 
   // ---- shared prefixes: planned once per block of member rows, cut into `pieces` page runs
   std::vector<ShareSet> sets;
@@ -324,6 +338,43 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
       }
     }
   }
+  // ---- query tiles of the prefill rows (mlb_shared_unit of kind 1): 128 / group consecutive tokens of one
+  // sequence over the keys its last token sees (causal), in pieces of <= kPrefillPiecePages pages whose
+  // partial rows are token-major: row(token i, piece p) = part_base + (i * pieces + p) * tpt
+  std::vector<mlb_shared_unit> punits;
+  const int tile_tokens = std::max(1, kSharedColumns / group_size);
+  for (int s : prefill_seqs) {
+    const int n = qo_indptr[s + 1] - qo_indptr[s], L = seq_lens[s];
+    for (int t0 = 0; t0 < n; t0 += tile_tokens) {
+      const int ntok = std::min(tile_tokens, n - t0);
+      const int key_end = L - n + t0 + ntok;  // keys 0 .. key_end - 1: what the tile's last token sees
+      const int pages = (key_end + block_size - 1) / block_size;
+      int pieces = std::min(255, std::max(1, (pages + kPrefillPiecePages - 1) / kPrefillPiecePages));
+      int per = (pages + pieces - 1) / pieces;
+      per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;  // whole 8-page MMA tiles
+      pieces = (pages + per - 1) / per;
+      const int64_t part_base = pieces > 1 ? rows : -1;
+      if (pieces > 1) rows += static_cast<int64_t>(ntok) * pieces * tpt;
+      for (int p = 0; p < pieces; ++p) {
+        mlb_shared_unit u{};
+        u.member_begin = qo_indptr[s] + t0;  // kind 1: the tile's first token
+        u.member_count = ntok;
+        u.page_begin = p * per;
+        u.page_end = std::min(pages, (p + 1) * per);
+        u.piece = pieces > 1 ? p : -1;
+        u.table_seq = s;
+        u.reserved[0] = 1 | (pieces << 8);
+        u.reserved[1] = static_cast<int32_t>(part_base);
+        punits.push_back(u);
+      }
+      if (reduce_rows && reduce_chunks)
+        for (int i = 0; i < ntok; ++i) {
+          const int64_t tok = qo_indptr[s] + t0 + i;
+          reduce_rows[tok] = pieces > 1 ? static_cast<int32_t>(part_base + static_cast<int64_t>(i) * pieces * tpt) : -1;
+          reduce_chunks[tok] = pieces;
+        }
+    }
+  }
   if (rows > INT32_MAX) return fail(MLB_EINVAL, "plan: too many partial rows");
   // Largest units first, so the short tail units fill in behind them.
   std::stable_sort(out.begin(), out.end(), [](const mlb_work_unit& x, const mlb_work_unit& y) {
@@ -350,6 +401,10 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
         sunits.push_back(u);
       }
   }
+  sunits.insert(sunits.end(), punits.begin(), punits.end());
+  std::stable_sort(sunits.begin(), sunits.end(), [](const mlb_shared_unit& x, const mlb_shared_unit& y) {
+    return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);  // largest first
+  });
   *num_units = static_cast<int64_t>(out.size());
   *num_shared_units = static_cast<int64_t>(sunits.size());
   *num_members = static_cast<int64_t>(mems.size());
@@ -394,8 +449,8 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   mlb_out_targets targets;
   if (int rc = resolve_targets("paged_attention", out, out_stride_tok, out_stride_head, out_targets, &targets))
     return rc;
-  if (num_shared_units > 0 && (!shared_units || !members || dtype == MLB_F32))
-    return fail(MLB_EINVAL, "paged_attention: shared-prefix units need their arrays and a 16-bit pool");
+  if (num_shared_units > 0 && (!shared_units || dtype == MLB_F32))  // members: only kind-0 units read them
+    return fail(MLB_EINVAL, "paged_attention: query-tile units need their array and a 16-bit pool");
   if (num_partial_rows > 0 && (!partial_o || !partial_lse))
     return fail(MLB_EINVAL, "paged_attention: the plan has %lld partial rows but no workspace",
                 static_cast<long long>(num_partial_rows));

@@ -356,6 +356,14 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
   const int4* rec = reinterpret_cast<const int4*>(a.shared_units + blockIdx.x / a.hkv);
   const int4 x = __ldg(rec), y = __ldg(rec + 1);
   const int mb = x.x, mc = x.y, pb = x.z, pe = x.w, piece = y.x, tseq = y.y;
+  // kind 0: shared prefix (members mb.., all keys visible); kind 1: query tile of sequence tseq (tokens
+  // mb .. mb + mc - 1, causal keys)
+  const bool tile_unit = (y.z & 0xff) == 1;
+  const int tile_pieces = y.z >> 8, tile_part_base = y.w;
+  const int seq_len = tile_unit ? __ldg(a.seq_lens + tseq) : INT_MAX;
+  const int first_pos = tile_unit ? seq_len - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) + (mb - __ldg(a.qo + tseq))
+                                  : 0;
+  const bool final_rows = tile_unit && piece < 0;
   const int npages = pe - pb;
   const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
   const int64_t row_stride = static_cast<int64_t>(a.hkv) * DH * 2;
@@ -395,7 +403,7 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
     {
       const int n = lane >> 2, c2 = (lane & 3) * 2;
       const bool live = n < ncols;
-      const int tok = live ? __ldg(&a.members[mb + wm + n / a.group].q0) : 0;
+      const int tok = !live ? 0 : tile_unit ? mb + wm + n / a.group : __ldg(&a.members[mb + wm + n / a.group].q0);
       const int head = kvh * a.group + (live ? n % a.group : 0);
       const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
                              static_cast<int64_t>(head) * a.q_sh;
@@ -410,7 +418,9 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
     }
     const int r0 = lane >> 2, j0 = (lane & 3) * 2, j1 = j0 + 1;
     const bool live0 = j0 < ncols, live1 = j1 < ncols;
-    const int lim0 = live0 ? INT_MAX : 0, lim1 = live1 ? INT_MAX : 0;  // every shared token is visible
+    // exclusive key limits: a shared prefix is visible whole; a query tile's token sees keys up to itself
+    const int lim0 = !live0 ? 0 : tile_unit ? first_pos + wm + j0 / a.group + 1 : INT_MAX;
+    const int lim1 = !live1 ? 0 : tile_unit ? first_pos + wm + j1 / a.group + 1 : INT_MAX;
     float o[DH / 16][4];
 #pragma unroll
     for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
@@ -424,9 +434,18 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
       cp_async_wait<S - 1>();      // this thread's copies of page i have landed
       __syncthreads();             // ... and every other thread's
       const int s = i % S;
+      const int key0 = (pb + i) * kBlockSize;  // key position of the page's first slot
+      if (key0 + kBlockSize > seq_len) {       // the sequence's last page: zero V rows past its end (0 x NaN)
+        uint8_t* vt = smem + s * STAGE + TILE;
+        for (int e = threadIdx.x; e < kBlockSize * CH_ROW; e += NW * 32) {
+          const int row = e / CH_ROW, ch = e % CH_ROW;
+          if (key0 + row >= seq_len) *reinterpret_cast<uint4*>(vt + row * ROWB + ch * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncthreads();
+      }
       if (ncols > 0 && !((bad_mask >> s) & 1u))
-        attend_page<DT, DH>(base_u32 + s * STAGE + k_off, base_u32 + s * STAGE + TILE + v_off, qb, 0, lim0, lim1,
-                            a.sl2, o, m0, m1, l0, l1);
+        attend_page<DT, DH>(base_u32 + s * STAGE + k_off, base_u32 + s * STAGE + TILE + v_off, qb,
+                            tile_unit ? key0 + r0 : 0, lim0, lim1, a.sl2, o, m0, m1, l0, l1);
       __syncthreads();  // every warp is done with slot s before it is refilled
     }
     cp_async_wait<0>();
@@ -437,29 +456,46 @@ __global__ void __launch_bounds__(kSharedWarps * 32) shared_prefix_kernel(AttnAr
       l1 += __shfl_xor_sync(0xffffffffu, l1, off);
     }
     const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
-    // partial row of member m for head h: members[m].part_base + piece * tokens_per_tile (its one token)
-    int64_t slot0 = 0, slot1 = 0;
-    if (live0)
-      slot0 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j0 / a.group].part_base)) +
-               static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j0 % a.group;
-    if (live1)
-      slot1 = (static_cast<int64_t>(__ldg(&a.members[mb + wm + j1 / a.group].part_base)) +
-               static_cast<int64_t>(piece) * a.tile_tokens) * a.h + kvh * a.group + j1 % a.group;
+    // partial row of member m: members[m].part_base + piece * tokens_per_tile (its one token); of token m of
+    // a split query tile: part_base + (m * pieces + piece) * tokens_per_tile
+    auto part_row = [&](int m) -> int64_t {
+      return tile_unit ? tile_part_base + (static_cast<int64_t>(m) * tile_pieces + piece) * a.tile_tokens
+                       : __ldg(&a.members[mb + m].part_base) + static_cast<int64_t>(piece) * a.tile_tokens;
+    };
+    const int h0 = kvh * a.group + j0 % a.group, h1 = kvh * a.group + j1 % a.group;
+    const int m0i = wm + j0 / a.group, m1i = wm + j1 / a.group;
+    if (final_rows) {  // an unsplit query tile: its rows are final
 #pragma unroll
-    for (int mt = 0; mt < DH / 16; ++mt) {
-      const int d = mt * 16 + r0;
-      if (live0) {
-        a.part_o[slot0 * DH + d] = o[mt][0] * inv0;
-        a.part_o[slot0 * DH + d + 8] = o[mt][2] * inv0;
+      for (int mt = 0; mt < DH / 16; ++mt) {
+        const int d = mt * 16 + r0;
+        if (live0) {
+          store_out1<DT>(a.out, mb + m0i, h0, d, o[mt][0] * inv0);
+          store_out1<DT>(a.out, mb + m0i, h0, d + 8, o[mt][2] * inv0);
+        }
+        if (live1) {
+          store_out1<DT>(a.out, mb + m1i, h1, d, o[mt][1] * inv1);
+          store_out1<DT>(a.out, mb + m1i, h1, d + 8, o[mt][3] * inv1);
+        }
       }
-      if (live1) {
-        a.part_o[slot1 * DH + d] = o[mt][1] * inv1;
-        a.part_o[slot1 * DH + d + 8] = o[mt][3] * inv1;
+    } else {
+      const int64_t slot0 = live0 ? part_row(m0i) * a.h + h0 : 0;
+      const int64_t slot1 = live1 ? part_row(m1i) * a.h + h1 : 0;
+#pragma unroll
+      for (int mt = 0; mt < DH / 16; ++mt) {
+        const int d = mt * 16 + r0;
+        if (live0) {
+          a.part_o[slot0 * DH + d] = o[mt][0] * inv0;
+          a.part_o[slot0 * DH + d + 8] = o[mt][2] * inv0;
+        }
+        if (live1) {
+          a.part_o[slot1 * DH + d] = o[mt][1] * inv1;
+          a.part_o[slot1 * DH + d + 8] = o[mt][3] * inv1;
+        }
       }
-    }
-    if (r0 == 0) {
-      if (live0) a.part_lse[slot0] = l0 > 0.f ? m0 + log2f(l0) : kNegInf;
-      if (live1) a.part_lse[slot1] = l1 > 0.f ? m1 + log2f(l1) : kNegInf;
+      if (r0 == 0) {
+        if (live0) a.part_lse[slot0] = l0 > 0.f ? m0 + log2f(l0) : kNegInf;
+        if (live1) a.part_lse[slot1] = l1 > 0.f ? m1 + log2f(l1) : kNegInf;
+      }
     }
     __syncthreads();  // the ring is reused by the next block of members
   }

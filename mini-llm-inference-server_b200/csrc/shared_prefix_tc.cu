@@ -72,6 +72,9 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+__device__ __forceinline__ void st_shared_zero16(uint32_t addr) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(addr), "r"(0u) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
@@ -190,6 +193,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   uint64_t* p_full = bars + 8;
   uint64_t* o_done = bars + 10;
   uint64_t* final_bar = bars + 11;
+  uint64_t* q_ready = bars + 12;  // the Q tile is in shared memory (arrived by the 128 softmax threads)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16) + 1;
   const uint32_t q_smem = smem_u32(smem);
@@ -201,6 +205,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   const int4* rec = reinterpret_cast<const int4*>(a.shared_units + blockIdx.x / a.hkv);
   const int4 x = __ldg(rec), y = __ldg(rec + 1);
   const int mb = x.x, mc = x.y, pb = x.z, pe = x.w, piece = y.x, tseq = y.y;
+  // kind 0: a shared prefix, members mb .. mb + mc - 1 (one decode token each), every key visible.
+  // kind 1: a query tile of sequence tseq: mc consecutive tokens from token mb, causal keys.
+  const bool tile_unit = (y.z & 0xff) == 1;
+  const int tile_pieces = y.z >> 8, tile_part_base = y.w;
+  // key position of the tile's first token (kind 1): context length - new tokens + offset in the row
+  const int first_pos = tile_unit ? __ldg(a.seq_lens + tseq) - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) +
+                                        (mb - __ldg(a.qo + tseq))
+                                  : 0;
   const int npages = pe - pb;
   const int ntiles = (npages + kTcTilePages - 1) / kTcTilePages;
   const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
@@ -216,6 +228,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     }
     mbar_init(o_done, 1);
     mbar_init(final_bar, 1);
+    mbar_init(q_ready, 128);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -224,23 +237,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
                  "r"(kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
-  if (warp >= 4) {  // Q rows, straight into the swizzled K-major A tile (zero for absent columns)
-    const int c = threadIdx.x - 128;
-    const int m = c / a.group;
-    const bool live = m < mc;
-    const uint4* src = nullptr;
-    if (live) {
-      const int tok = __ldg(&a.members[mb + m].q0);
-      const int head = kvh * a.group + c % a.group;
-      src = reinterpret_cast<const uint4*>(a.q + (static_cast<int64_t>(tok) * a.q_st + static_cast<int64_t>(head) * a.q_sh) * 2);
-    }
-#pragma unroll
-    for (int ch = 0; ch < CH; ++ch) {
-      const uint4 v = live ? __ldg(src + ch) : make_uint4(0u, 0u, 0u, 0u);
-      *reinterpret_cast<uint4*>(smem + sw_chunk(c, ch)) = v;
-    }
-    fence_proxy_async_smem();  // generic-proxy stores, read by the tensor core (async proxy)
   }
   tc_fence_before();
   __syncthreads();
@@ -295,7 +291,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      for (int j = 0; j <= ntiles && !*abort_flag; ++j) {
+      const bool have_q = tc_wait(q_ready, 0, abort_flag, a.err);
+      for (int j = 0; have_q && j <= ntiles && !*abort_flag; ++j) {
         if (j < ntiles) {
           const int s = j % kTcStages, b = j & 1;
           if (!tc_wait(full + s, (j / kTcStages) & 1, abort_flag, a.err)) break;
@@ -328,8 +325,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax warpgroup: one query column each
+    // the Q rows first, straight into the swizzled K-major A tile (zero for absent columns); the producers
+    // are already fetching the first K/V tiles, and only the MMA issuer waits for q_ready
+    {
+      const int c = threadIdx.x - 128;
+      const int m = c / a.group;
+      const bool live = m < mc;
+      const uint4* src = nullptr;
+      if (live) {
+        const int tok = tile_unit ? mb + m : __ldg(&a.members[mb + m].q0);
+        const int head = kvh * a.group + c % a.group;
+        src = reinterpret_cast<const uint4*>(
+            a.q + (static_cast<int64_t>(tok) * a.q_st + static_cast<int64_t>(head) * a.q_sh) * 2);
+      }
+#pragma unroll
+      for (int ch = 0; ch < CH; ++ch) {
+        const uint4 v = live ? __ldg(src + ch) : make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(smem + sw_chunk(c, ch)) = v;
+      }
+      fence_proxy_async_smem();  // generic-proxy stores, read by the tensor core (async proxy)
+    }
+    mbar_arrive(q_ready);
     const int row = threadIdx.x - 128;
     const uint32_t lanes = static_cast<uint32_t>((warp - 4) * 32) << 16;
+    const int key_lim = first_pos + row / a.group + 1;  // kind 1: exclusive causal key limit of this column
+    const int seq_len = tile_unit ? __ldg(a.seq_lens + tseq) : INT_MAX;
     float m_used = -__builtin_huge_valf(), l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
@@ -355,6 +375,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         for (int k = 0; k < kTcTileTokens; ++k) {
           const int p = k / kBlockSize;
           if (p >= live_pages || ((bad >> p) & 1u)) sr[k] = __float_as_uint(-__builtin_huge_valf());
+        }
+      }
+      const int tile_key0 = (pb + j * kTcTilePages) * kBlockSize;  // key position of element 0
+      if (tile_unit) {
+        // causal: this column sees keys < key_lim (elements from key_lim - tile_key0 on are masked)
+        const int rel = key_lim - tile_key0;
+        if (rel < kTcTileTokens) {
+#pragma unroll
+          for (int k = 0; k < kTcTileTokens; ++k)
+            if (k >= rel) sr[k] = __float_as_uint(-__builtin_huge_valf());
+        }
+        // V rows of slots past the sequence's end (its last page) are junk: 0 x NaN would poison P . V,
+        // so they are zeroed in shared memory before the tile goes to the tensor core
+        const int r0 = max(0, seq_len - tile_key0), r1 = live_pages * kBlockSize;
+        if (r0 < r1) {
+          const uint32_t vb = stage_smem + (j % kTcStages) * L::kStageBytes + L::kTileBytes;
+          constexpr int kRowItems = (DH / 64) * 8;  // 16-byte chunks of one row, both halves
+          for (int e = row; e < (r1 - r0) * kRowItems; e += 128) {
+            const int r = r0 + e / kRowItems, h = (e % kRowItems) / 8, c = e % 8;
+            st_shared_zero16(vb + h * (kTcRows * 128) + r * 128 + c * 16);
+          }
+          fence_proxy_async_smem();
         }
       }
       float mraw = -__builtin_huge_valf();
@@ -406,22 +448,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     if (ok && ntiles > 0 && tc_wait(o_done, (ntiles - 1) & 1, abort_flag, a.err)) {
       tc_fence_after();
       const int m = row / a.group;
+      const int head = kvh * a.group + row % a.group;
       bool live = m < mc;
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      // an unsplit query tile writes its final rows; everything else writes a split-K partial row
+      const bool final_rows = tile_unit && piece < 0;
       int64_t slot = 0;
-      if (live)
-        slot = (static_cast<int64_t>(__ldg(&a.members[mb + m].part_base)) + static_cast<int64_t>(piece) * a.tile_tokens) *
-                   a.h + kvh * a.group + row % a.group;
-      if (live && (slot < 0 || slot >= a.part_rows * a.h)) {  // a plan inconsistent with the workspace
-        flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-        live = false;
+      if (live && !final_rows) {
+        const int64_t prow = tile_unit ? tile_part_base + (static_cast<int64_t>(m) * tile_pieces + piece) * a.tile_tokens
+                                       : __ldg(&a.members[mb + m].part_base) + static_cast<int64_t>(piece) * a.tile_tokens;
+        slot = prow * a.h + head;
+        if (slot < 0 || slot >= a.part_rows * a.h) {  // a plan inconsistent with the workspace
+          flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+          live = false;
+        }
       }
 #pragma unroll
       for (int i = 0; i < DH / 32; ++i) {
         uint32_t orow[32];
         tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
         tmem_wait_ld();
-        if (live) {
+        if (live && final_rows) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float v8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v8[e] = __uint_as_float(orow[8 * k + e]) * inv;
+            store_out_n<DT, 8>(a.out, a.out_vec != 0, mb + m, head, 32 * i + 8 * k, v8);
+          }
+        } else if (live) {
           float4* dst = reinterpret_cast<float4*>(a.part_o + slot * DH + 32 * i);
 #pragma unroll
           for (int k = 0; k < 8; ++k)
@@ -429,7 +484,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
                                  __uint_as_float(orow[4 * k + 2]) * inv, __uint_as_float(orow[4 * k + 3]) * inv);
         }
       }
-      if (live) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -__builtin_huge_valf();
+      if (live && !final_rows) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -__builtin_huge_valf();
     }
   }
 

@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 3
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 4
 
 
 def test_plan_record_layouts_match_header(L):
@@ -216,3 +216,56 @@ def test_planner_finds_shared_prefixes(mlb):
         assert min(u[2] for u in units.tolist() if u[0] == s) == 0
     plain = mlb.plan_attention(qo, lens, width, 32, 8, "cpu", num_sms=148)
     assert plain.num_shared_units == 0
+
+
+@pytest.mark.parametrize("h,hkv", [(32, 8), (8, 8), (16, 2), (12, 4)])
+def test_planner_makes_query_tiles_for_prefill_rows(mlb, h, hkv):
+    """With host tables, rows of >= 16 new tokens become kind-1 query tiles of 128 / group tokens over the
+    keys their last token sees, split in pieces of <= 128 pages with token-major partial rows; shorter rows
+    keep 8-column work units."""
+    g = h // hkv
+    tpt = max(1, 8 // g)
+    tile = 128 // g
+    steps = [(0, 40), (300, 70), (3000, 33), (500, 1), (100, 15), (2400, 16)]
+    qo, lens = [0], []
+    for c, n in steps:
+        qo.append(qo[-1] + n)
+        lens.append(c + n)
+    width = max(-(-n // 16) for n in lens)
+    host = np.arange(len(steps) * width, dtype=np.int32).reshape(len(steps), width)
+    p = mlb.plan_attention(qo, lens, width, h, hkv, "cpu", block_tables_host=host)
+    su = p.shared_host
+    kind1 = [u for u in su.tolist() if (u[6] & 0xFF) == 1]
+    prefill = {s for s, (c, n) in enumerate(steps) if n >= 16}
+    assert {u[5] for u in kind1} == prefill
+    assert not any(u[0] in prefill for u in p.units_host.tolist()), "prefill rows get no 8-column units"
+    covered = {}
+    for first, ntok, pb, pe, piece, seq, kp, base in kind1:
+        c, n = steps[seq]
+        assert 1 <= ntok <= tile and qo[seq] <= first and first + ntok <= qo[seq + 1]
+        t0 = first - qo[seq]
+        pages = -(-(c + t0 + ntok) // 16)  # keys the tile's last token sees
+        pieces = kp >> 8
+        covered.setdefault((seq, t0), []).append((pb, pe, piece, pieces, base, ntok))
+        assert 0 <= pb < pe <= pages
+        if pieces == 1:
+            assert piece == -1 and (pb, pe) == (0, pages)
+        else:
+            assert 0 <= piece < pieces and pe - pb <= 128
+            for i in range(ntok):
+                tok = first + i
+                assert p.reduce_chunks_host[tok] == pieces
+                assert p.reduce_rows_host[tok] == base + i * pieces * tpt
+                assert base + ((i * pieces) + pieces - 1) * tpt < p.num_partial_rows
+    for (seq, t0), parts in covered.items():
+        parts.sort()
+        c, n = steps[seq]
+        ntok = parts[0][5]
+        assert parts[0][0] == 0 and parts[-1][1] == -(-(c + t0 + ntok) // 16)
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+    for s in prefill:  # every token of a prefill row is in exactly one tile
+        n = steps[s][1]
+        starts = sorted(t0 for (seq, t0) in covered if seq == s)
+        assert starts == list(range(0, n, tile))
+    plain = mlb.plan_attention(qo, lens, width, h, hkv, "cpu")
+    assert plain.num_shared_units == 0  # without host tables: 8-column units for every row

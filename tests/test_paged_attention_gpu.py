@@ -207,3 +207,47 @@ def _shared_prefix_case(mlb, cuda, dtype, h, hkv, dh, rows_a):
     out = backend.forward(t["q"], t["k"], t["v"], t["k_pool"], t["v_pool"], meta)
     assert backend._plan.num_shared_units > 0 and len(backend._plan.members_host) == rows_a + 9
     assert_close(out, oracle_forward(case, dtype)[0], dtype)
+
+
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+@pytest.mark.parametrize("h,hkv,dh", [(32, 8, 128), (8, 8, 64), (16, 2, 128), (8, 1, 256), (12, 4, 64)])
+def test_prefill_query_tiles_match_oracle(mlb, cuda, dtype, h, hkv, dh, tc):
+    """Multi-token rows of >= 16 tokens (prefill chunks on cache) run as 128-column query tiles with a causal
+    mask per column (paged_torch_ref.py:61-73), on fresh and cached contexts, split in pieces on a long
+    context, next to short rows and decode rows.  The slots past every sequence's end in its last page hold
+    NaN on the device: they must not reach the output (the oracle sees finite values there)."""
+    lib = mlb._lib.lib()
+    prev = lib.mlb_set_tensor_core_prefix(tc)
+    try:
+        steps = [(0, 40), (300, 70), (3000, 33), (500, 1), (100, 15), (2400, 16), (37, 129)]
+        r = random.Random(h * 7 + dh)
+        nb = 700
+        ids = list(range(nb))
+        r.shuffle(ids)
+        blocks, nxt = [], 0
+        for c, n in steps:
+            need = -(-(c + n) // 16)
+            blocks.append(ids[nxt:nxt + need])
+            nxt += need
+        ntok = sum(n for _, n in steps)
+        gen = np.random.default_rng(11)
+        case = cases.PagedCase("prefill", h, hkv, dh, 16, steps, blocks, *(
+            torch.from_numpy(gen.standard_normal(shape, dtype=np.float32))
+            for shape in ((ntok, h, dh), (ntok, hkv, dh), (ntok, hkv, dh), (nb, 16, hkv, dh), (nb, 16, hkv, dh))))
+        t = device_case(case, dtype, cuda)
+        for (c, n), b in zip(steps, blocks):  # junk past the end of each context
+            rest = (c + n) % 16
+            if rest:
+                t["k_pool"][b[-1], rest:] = float("nan")
+                t["v_pool"][b[-1], rest:] = float("nan")
+        meta = mlb.AttentionMetadata.build([mlb.SeqStep(c, n, list(b)) for c, n, b in case.seqs], 16, cuda)
+        backend = mlb.B200Backend(check_errors=True)
+        out = backend.forward(t["q"], t["k"], t["v"], t["k_pool"], t["v_pool"], meta)
+        kinds = backend._plan.shared_host[:, 6] & 0xFF
+        assert (kinds == 1).sum() > 0, "prefill rows must run as query tiles"
+        assert ((backend._plan.shared_host[:, 6] >> 8) > 1).any(), "the long context must split in pieces"
+        assert torch.isfinite(out).all()
+        assert_close(out, oracle_forward(case, dtype)[0], dtype)
+    finally:
+        lib.mlb_set_tensor_core_prefix(prev)
