@@ -21,8 +21,9 @@
 // - warps 4-7 (a warpgroup; thread = one query column = one TMEM lane): read the S row from TMEM, mask,
 //   running max in the exp2 domain, P = 2^(s - m) packed to 16 bits into TMEM buffer j % 2, row sums in
 //   fp32.  O is rescaled (TMEM load / scale / store) only when a row's max grows by more than 8 (a factor
-//   256 of headroom keeps P and the sums finite), which after the first tiles is rare.  At the end every
-//   column's normalised O row and log2-sum-exp go to its split-K partial row, merged by the reduction.
+//   256 of headroom keeps P and the sums finite), which after the first tiles is rare.  At the end (the
+//   "final" barrier, committed behind the last MMA) every column's normalised O row and log2-sum-exp go
+//   to its split-K partial row, merged by the reduction.
 // TMEM columns: S0 [0,128), S1 [128,256), O [256, 256 + Dh), P0 [384,448), P1 [448,512).
 //
 // Every wait is bounded (time and polls); on expiry the CTA raises MLB_DEV_WAIT_TIMEOUT, drains its own
@@ -144,6 +145,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// The compiler takes a tcgen05.ld's destination registers as written by the ld itself, so arithmetic on them
+// may be scheduled above tcgen05.wait::ld (the wait's memory clobber orders memory, not registers).  This
+// empty asm "rewrites" the 32 registers after the wait (volatile asms keep their order), which pins every use.
+__device__ __forceinline__ void tmem_pin32(uint32_t* r) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
+                 "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                 "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                 "+r"(r[30]), "+r"(r[31]));
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Bounded wait on an mbarrier phase; gives up (and tells the CTA to stop) when another role aborted or
@@ -369,6 +381,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_ld32(tmem + lanes + col_s(b) + 32 * i, sr + 32 * i);
       const uint32_t bad = __ballot_sync(0xffffffffu, lane < live_pages && (my_bid < 0 || my_bid >= a.num_blocks));
       tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_pin32(sr + 32 * i);
       // raw scores stay in sr; masked keys become -inf (only on a partial tile or a bad page)
       if (live_pages < kTcTilePages || bad) {
 #pragma unroll
@@ -399,9 +413,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
           fence_proxy_async_smem();
         }
       }
-      float mraw = -__builtin_huge_valf();
+      // 8 independent max chains (one serial chain of 128 dependent FMNMX was the softmax's critical path)
+      float mx8[8];
 #pragma unroll
-      for (int k = 0; k < kTcTileTokens; ++k) mraw = fmaxf(mraw, __uint_as_float(sr[k]));
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
+#pragma unroll
+      for (int k = 8; k < kTcTileTokens; ++k) mx8[k % 8] = fmaxf(mx8[k % 8], __uint_as_float(sr[k]));
+      const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx = mraw * a.sl2;  // the scale is positive: max commutes with it
       const bool need = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, need)) {
@@ -418,6 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
             uint32_t orow[32];
             tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
             tmem_wait_ld();
+            tmem_pin32(orow);
 #pragma unroll
             for (int k = 0; k < 32; ++k) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
             tmem_st32(tmem + lanes + kColO + 32 * i, orow);
@@ -430,22 +450,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const float nbase = m_used == -__builtin_huge_valf() ? 0.f : -m_used;
       const float sl2 = a.sl2;
       uint32_t pk[kTcTileTokens / 2];
-      float sum = 0.f;
+      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent sum chains
 #pragma unroll
       for (int k = 0; k < kTcTileTokens; k += 2) {  // p = 2^(s * scale * log2 e - m): one FFMA + EX2 per key
         const float p0 = fast_exp2(fmaf(__uint_as_float(sr[k]), sl2, nbase));
         const float p1 = fast_exp2(fmaf(__uint_as_float(sr[k + 1]), sl2, nbase));
-        sum += p0 + p1;
+        s8[(k / 2) % 8] += p0 + p1;
         pk[k / 2] = pack2<DT>(p0, p1);
       }
-      l += sum;
+      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
       tmem_st32(tmem + lanes + col_p(b), pk);
       tmem_st32(tmem + lanes + col_p(b) + 32, pk + 32);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(p_full + b);
     }
-    if (ok && ntiles > 0 && tc_wait(o_done, (ntiles - 1) & 1, abort_flag, a.err)) {
+    // O is complete when final_bar (committed once, after every MMA) arrives.  Not o_done's parity
+    // (ntiles - 1) & 1: here only P . V of tile ntiles - 3 is known complete (it precedes the last S commit),
+    // and while P . V of tile ntiles - 2 is still running that parity names the phase before the current
+    // one, which a parity wait takes as complete.
+    if (ok && ntiles > 0 && tc_wait(final_bar, 0, abort_flag, a.err) && !*abort_flag) {
       tc_fence_after();
       const int m = row / a.group;
       const int head = kvh * a.group + row % a.group;
@@ -468,6 +492,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         uint32_t orow[32];
         tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
         tmem_wait_ld();
+        tmem_pin32(orow);
         if (live && final_rows) {
 #pragma unroll
           for (int k = 0; k < 4; ++k) {

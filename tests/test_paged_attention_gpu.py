@@ -209,6 +209,50 @@ def _shared_prefix_case(mlb, cuda, dtype, h, hkv, dh, rows_a):
     assert_close(out, oracle_forward(case, dtype)[0], dtype)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
+def test_shared_prefix_multi_tile_units_repeatable(mlb, cuda, dtype):
+    """tcgen05 shared units of 2 and 3 key tiles (prefixes of 9, 10, 17 and 24 pages): five runs give
+    bit-identical outputs, equal to the oracle's.  The output rows may only be read once the last tile's
+    P . V is done; a wait that an earlier tile's MMA could satisfy shows here as run-to-run differences."""
+    lib = mlb._lib.lib()
+    prev = lib.mlb_set_tensor_core_prefix(1)
+    try:
+        h, hkv, dh = 32, 8, 128
+        r = random.Random(5)
+        nb = 900
+        ids = list(range(nb))
+        r.shuffle(ids)
+        steps, blocks, nxt = [], [], 0
+        for plen in (9, 10, 17, 24):
+            prefix = ids[nxt:nxt + plen]
+            nxt += plen
+            for _ in range(6):
+                ctx = plen * 16 + r.randint(1, 40)
+                own = -(-ctx // 16) - plen
+                steps.append((ctx - 1, 1))
+                blocks.append(prefix + ids[nxt:nxt + own])
+                nxt += own
+        ntok = len(steps)
+        gen = np.random.default_rng(21)
+        case = cases.PagedCase("multi_tile", h, hkv, dh, 16, steps, blocks, *(
+            torch.from_numpy(gen.standard_normal(shape, dtype=np.float32))
+            for shape in ((ntok, h, dh), (ntok, hkv, dh), (ntok, hkv, dh), (nb, 16, hkv, dh), (nb, 16, hkv, dh))))
+        t = device_case(case, dtype, cuda)
+        meta = mlb.AttentionMetadata.build([mlb.SeqStep(c, n, list(b)) for c, n, b in case.seqs], 16, cuda)
+        backend = mlb.B200Backend()
+        outs = []
+        for _ in range(5):
+            k_pool, v_pool = t["k_pool"].clone(), t["v_pool"].clone()  # each run appends its own k / v
+            outs.append(backend.forward(t["q"], t["k"], t["v"], k_pool, v_pool, meta).clone())
+        assert backend._plan.num_shared_units >= 4
+        assert max(int(u[3]) - int(u[2]) for u in backend._plan.shared_host) > 8  # a unit of several tiles
+        for o in outs[1:]:
+            assert torch.equal(o, outs[0])
+        assert_close(outs[0], oracle_forward(case, dtype)[0], dtype)
+    finally:
+        lib.mlb_set_tensor_core_prefix(prev)
+
+
 @pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16], ids=str)
 @pytest.mark.parametrize("h,hkv,dh", [(32, 8, 128), (8, 8, 64), (16, 2, 128), (8, 1, 256), (12, 4, 64)])
