@@ -431,19 +431,25 @@ def run_ours(args) -> None:
         ptrs = ops.pool_pointer_table(k_pools + v_pools)
         src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
         dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
-    # append, attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
+    # the append rides in the attention launch when every written block is private to its row (the backend's
+    # rule: B200Backend.forward); otherwise K1 runs first
+    fused = (not args.no_fused_append and meta_app is meta_att and meta_att.append_private
+             and ops.can_fuse_append(plan, k_pools[0], k_l, v_l))
+    append = (k_l, v_l, meta_app.slot_mapping) if fused else None
+    # [append,] attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
     # [+ p2p barrier]
-    launches_per_layer = (2 + (1 if plan.num_shared_units else 0) + (1 if plan.num_partial_rows or p2p else 0)
-                          + (1 if p2p else 0))
+    launches_per_layer = ((1 if fused else 2) + (1 if plan.num_shared_units else 0)
+                          + (1 if plan.num_partial_rows or p2p else 0) + (1 if p2p else 0))
 
     def layer_step(l, ev=None):
-        ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
+        if not fused:
+            ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
         if ev is not None:
             ev[0].record()
         slot = l % peers.slots if p2p else 0
         ops.attention_partials(q_l, k_pools[l], v_pools[l], meta_att.block_tables_i32, meta_att.seq_lens_i32,
                                meta_att.qo_indptr, plan, ws, out_l,
-                               targets=peers.local_targets(slot, qs.start) if p2p else None)
+                               targets=peers.local_targets(slot, qs.start) if p2p else None, append=append)
         if ev is not None:
             ev[1].record()
         if p2p:  # reduction + every row into every rank's buffer (one launch), then the flag barrier
@@ -586,11 +592,12 @@ def run_ours(args) -> None:
                                       if world > 1 else "single GPU",
                        "l2": "no flush: every layer's pool reads exceed the 126 MB L2",
                        "programmatic_launch": not args.no_pdl,
+                       "append": "fused into the attention launch" if fused else "separate K1 launch",
                        "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
-            "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 2),
+            "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 2),  # K1 alone (graph of its launches)
             "append_us": round(append_ms * 1e3, 2),
             "attention_us": round(attn_avg_ms * 1e3, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -798,6 +805,8 @@ def main() -> None:
                     help="config 3: the prefill chunks also attend (multi-token rows on query tiles)")
     ap.add_argument("--no-query-tiles", action="store_true",
                     help="plan without host tables: every row on the decode kernel's 8-column units")
+    ap.add_argument("--no-fused-append", action="store_true",
+                    help="launch the append (K1) before attention even when it could ride in the attention launch")
     ap.add_argument("--no-tc-prefix", action="store_true",
                     help="shared-prefix units on the mma.sync kernel instead of tcgen05")
     args = ap.parse_args()

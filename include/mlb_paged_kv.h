@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 4 */
+MLB_API int mlb_abi_version(void);  /* 5 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -198,6 +198,45 @@ MLB_API int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_s
                         float* partial_o, float* partial_lse, int64_t num_partial_rows,
                         void* out, int64_t out_stride_tok, int64_t out_stride_head,
                         const mlb_out_targets* out_targets, int32_t* err_word, void* stream);
+
+/*
+ * The step's new K/V rows for mlb_paged_attention_append: k / v [num_tokens, num_kv_heads, head_dim] in
+ * the pools' dtype (strides in elements; bases and both strides x element bytes 16-byte aligned), and
+ * slot_mapping [num_tokens] (device int64), as mlb_kv_append takes them.
+ */
+typedef struct {
+  const void* k;
+  const void* v;
+  int64_t k_stride_tok, k_stride_head;
+  int64_t v_stride_tok, v_stride_head;
+  const int64_t* slot_mapping;
+  int64_t num_tokens;
+} mlb_append_rows;
+
+/*
+ * mlb_kv_append followed by mlb_paged_attention, as ONE attention launch (the order of the reference's
+ * forward: write, then attend, src/minillm/attention/torch_ref.py:46-48).  Every attention CTA that loads
+ * a page holding new rows takes those rows from k / v (never from the pool, which may not have them yet),
+ * and the units of each row's last query tile store them into the pools at slot_mapping (out-of-range
+ * slots are skipped and flagged MLB_DEV_SLOT_RANGE, as in mlb_kv_append).  16-bit pools only.
+ * The caller guarantees, for the launch to equal the two calls:
+ *   - slot_mapping[t] is the slot the block tables give token t (block_tables[s][pos / 16] * 16 + pos % 16,
+ *     as AttentionMetadata.build makes it, metadata.py:81);
+ *   - every block that receives a row appears once in all sequences' context pages (no other sequence,
+ *     and no other position of the same sequence, reads it), so no other CTA needs the written values;
+ *   - the plan has no query-tile units (kind 1 shared units, rows of >= 16 new tokens).
+ * Otherwise call mlb_kv_append and mlb_paged_attention.  Other arguments as mlb_paged_attention.
+ */
+MLB_API int mlb_paged_attention_append(const void* q, int64_t q_stride_tok, int64_t q_stride_head,
+                        void* k_cache, void* v_cache, int dtype, int64_t num_blocks, int block_size,
+                        int num_heads, int num_kv_heads, int head_dim, float scale,
+                        const int32_t* block_tables, int64_t bt_stride, const int32_t* seq_lens,
+                        const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units, int64_t num_units,
+                        const mlb_shared_unit* shared_units, int64_t num_shared_units, const mlb_share_member* members,
+                        float* partial_o, float* partial_lse, int64_t num_partial_rows,
+                        void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        const mlb_out_targets* out_targets, const mlb_append_rows* append, int32_t* err_word,
+                        void* stream);
 
 /*
  * Split-K reduction: for every token whose reduce_chunks > 1, combine its rows

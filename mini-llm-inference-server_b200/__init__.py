@@ -11,10 +11,11 @@ The directory name is not a Python identifier; import it with
 """
 
 from . import ops
-from .attention import AttentionBackend, AttentionMetadata, B200Backend, SeqStep, get_backend
+from .attention import AttentionBackend, AttentionMetadata, B200Backend, DeviceFault, SeqStep, get_backend
 from .cache import BLOCK_SIZE, BlockManager, KVShape, PagedKVCache, PagedStep, PrefixCache
 from .ops import AttentionPlan, Workspace, block_copy, kv_append, paged_attention, plan_attention
 
 __all__ = ["AttentionBackend", "AttentionMetadata", "AttentionPlan", "B200Backend", "BLOCK_SIZE", "BlockManager",
+           "DeviceFault",
            "KVShape", "PagedKVCache", "PagedStep", "PrefixCache", "SeqStep", "Workspace", "block_copy",
            "get_backend", "kv_append", "ops", "paged_attention", "plan_attention"]

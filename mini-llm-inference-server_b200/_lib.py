@@ -21,8 +21,8 @@ DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
 EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_paged_attention",
            "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc", "mlb_ipc_alloc", "mlb_ipc_open",
            "mlb_ipc_close", "mlb_ipc_free", "mlb_peer_barrier", "mlb_set_programmatic_launch",
-           "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix")
-ABI_VERSION = 4
+           "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix", "mlb_paged_attention_append")
+ABI_VERSION = 5
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 MAX_OUT_DESTS = 8  # MLB_MAX_OUT_DESTS
 IPC_HANDLE_BYTES = 64  # MLB_IPC_HANDLE_BYTES
@@ -56,6 +56,14 @@ class OutTargets(ctypes.Structure):
                 ("stride_head", c_int64), ("dests", c_void_p * MAX_OUT_DESTS)]
 
 
+class AppendRows(ctypes.Structure):
+    """mlb_append_rows: the step's new k / v rows and their slots, for the fused append + attention."""
+
+    _fields_ = [("k", c_void_p), ("v", c_void_p), ("k_stride_tok", c_int64), ("k_stride_head", c_int64),
+                ("v_stride_tok", c_int64), ("v_stride_head", c_int64), ("slot_mapping", c_void_p),
+                ("num_tokens", c_int64)]
+
+
 WORK_UNIT_INT32S = ctypes.sizeof(WorkUnit) // 4
 SHARED_UNIT_INT32S = ctypes.sizeof(SharedUnit) // 4
 MEMBER_INT32S = ctypes.sizeof(ShareMember) // 4
@@ -75,6 +83,11 @@ _SIGNATURES = {
                                     c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_void_p,
                                     c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                                     c_int64, c_int64, POINTER(OutTargets), c_void_p, c_void_p]),
+    "mlb_paged_attention_append": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
+                                           c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p,
+                                           c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
+                                           c_void_p, c_int64, c_void_p, c_int64, c_int64, POINTER(OutTargets),
+                                           POINTER(AppendRows), c_void_p, c_void_p]),
     "mlb_splitk_reduce": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int, c_int,
                                   c_void_p, c_int64, c_int64, c_int, POINTER(OutTargets), c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,

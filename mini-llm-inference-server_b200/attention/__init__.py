@@ -10,7 +10,7 @@
 
 from __future__ import annotations
 
-from .backend import B200Backend
+from .backend import B200Backend, DeviceFault
 from .base import AttentionBackend
 from .metadata import AttentionMetadata, SeqStep
 
@@ -26,4 +26,4 @@ def get_backend(name: str, **kwargs) -> AttentionBackend:
     return reference_get_backend(name)
 
 
-__all__ = ["AttentionBackend", "AttentionMetadata", "B200Backend", "SeqStep", "get_backend"]
+__all__ = ["AttentionBackend", "AttentionMetadata", "B200Backend", "DeviceFault", "SeqStep", "get_backend"]

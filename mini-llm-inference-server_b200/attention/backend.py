@@ -1,10 +1,12 @@
 """`B200Backend`: the reference's `AttentionBackend` (attention/base.py:16-45) on sm_100a kernels.
 
 `forward` per layer (the engine calls it 32 times per step for Llama-3.1-8B):
-1. K1 `kv_append`: this step's k/v rows into the pools through `meta.slot_mapping` (replaces write_kv,
-   paged_torch_ref.py:23-28, which all three reference backends share);
-2. the step's split plan, built on the first layer that sees a new `meta` and reused by the rest, as the
+1. the step's split plan, built on the first layer that sees a new `meta` and reused by the rest, as the
    FlashInfer backend caches its plan() (flashinfer_backend.py:44-45);
+2. K1 `kv_append`: this step's k/v rows into the pools through `meta.slot_mapping` (replaces write_kv,
+   paged_torch_ref.py:23-28, which all three reference backends share) -- or, when every written block is
+   private to its sequence (`meta.append_private`) and the plan allows it, no separate launch: the
+   attention launch stores the rows and uses them for the pages that hold them;
 3. K2a paged attention over `meta.block_tables_i32` + K2b split-K reduction (replaces paged_attention,
    paged_torch_ref.py:40-74, and FlashInfer's run(), flashinfer_backend.py:46).
 No host synchronisation happens inside `forward`; every launch goes on torch's current stream.
@@ -19,8 +21,8 @@ import torch
 import torch.nn.functional as F
 
 from .. import _lib
-from ..ops import (AttentionPlan, Workspace, attention_partials, kv_append, paged_attention, plan_attention,
-                   splitk_reduce_gather)
+from ..ops import (AttentionPlan, Workspace, attention_partials, can_fuse_append, kv_append, paged_attention,
+                   plan_attention, splitk_reduce_gather)
 from .base import AttentionBackend
 
 
@@ -31,14 +33,18 @@ class DeviceFault(RuntimeError):
 class B200Backend(AttentionBackend):
     name = "b200"
 
-    def __init__(self, pages_per_unit: int = 0, num_sms: int | None = None, check_errors: bool = False) -> None:
+    def __init__(self, pages_per_unit: int = 0, num_sms: int | None = None, check_errors: bool = False,
+                 fuse_append: bool = True) -> None:
         """pages_per_unit: split-K size in pages (0 = chosen per step from the work and the SM count).
         check_errors: after every forward, synchronise and raise `DeviceFault` if a kernel flagged a range
-        fault (debugging aid; it costs a host sync per layer)."""
+        fault (debugging aid; it costs a host sync per layer).
+        fuse_append: let the attention launch do the append when that is exact (one launch fewer per layer);
+        False always launches kv_append first.  Same results either way."""
         _lib.lib()  # the CUDA library is required: fail here, not on the first step
         self.pages_per_unit = pages_per_unit
         self.num_sms = num_sms
         self.check_errors = check_errors
+        self.fuse_append = fuse_append
         self._planned = None  # the AttentionMetadata the plan was built for
         self._plan_key: tuple | None = None
         self._plan: AttentionPlan | None = None
@@ -83,19 +89,24 @@ class B200Backend(AttentionBackend):
         if k_cache.shape[1] != meta.block_size:
             raise ValueError(f"pool block size {k_cache.shape[1]} != metadata block size {meta.block_size}")
         err = self._error_word(q.device) if self.check_errors else None
-        kv_append(k_cache, v_cache, meta.slot_mapping, k, v, err)
         plan = self.plan(meta, q.shape[1], k_cache.shape[2], q.device, k_cache.dtype)
+        append = None
+        if self.fuse_append and getattr(meta, "append_private", False) and can_fuse_append(plan, k_cache, k, v):
+            append = (k, v, meta.slot_mapping)
+        else:
+            kv_append(k_cache, v_cache, meta.slot_mapping, k, v, err)
         if peer_gather is not None:
             peers, slot, head_offset = peer_gather
             attention_partials(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
-                               self._workspace, err=err, targets=peers.local_targets(slot, head_offset))
+                               self._workspace, err=err, targets=peers.local_targets(slot, head_offset),
+                               append=append)
             splitk_reduce_gather(plan, self._workspace, peers.targets(slot, head_offset), peers.self_dest, q.dtype,
                                  q.shape[2], q.device)
             peers.barrier()
             out = None
         else:
             out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr,
-                                  plan, self._workspace, err=err, targets=out_targets)
+                                  plan, self._workspace, err=err, targets=out_targets, append=append)
         if self.check_errors:
             self.raise_device_errors()
         return out

@@ -46,6 +46,10 @@ class AttentionMetadata:
     # Not in the reference's metadata: the int32 block tables on the host, which let the planner find decode
     # rows that share prefix blocks without a device round trip.
     block_tables_host: np.ndarray | None = None
+    # Not in the reference's metadata either: True when every block that receives one of this step's rows is
+    # among the context pages of one sequence, once.  No other sequence (or position) then reads a written
+    # block, and the append may ride in the attention launch (ops.attention_partials(append=...)).
+    append_private: bool = False
 
     @property
     def max_query_len(self) -> int:
@@ -91,6 +95,11 @@ class AttentionMetadata:
         np.cumsum(used, out=kv_indptr[1:])
         kv_indices = table[np.arange(width)[None, :] < used[:, None]]  # row-major: sequence by sequence
         last_len = ends - (used - 1) * block_size
+        # the block of every new row must occur once among all sequences' context pages
+        private = n == 0
+        if n and kv_indices.size and int(kv_indices.min()) >= 0:
+            counts = np.bincount(kv_indices)
+            private = bool((counts[table[owner, positions // block_size]] == 1).all())
 
         # two transfers: every int64 tensor in one buffer, every int32 tensor in another
         i64 = np.concatenate([positions, slots, table.reshape(-1), starts[1:] - 1])
@@ -113,6 +122,7 @@ class AttentionMetadata:
             kv_indices=d32[o32[4]:o32[5]],
             kv_last_page_len=d32[o32[5]:o32[6]],
             block_tables_host=table.astype(np.int32),
+            append_private=private,
         )
 
 

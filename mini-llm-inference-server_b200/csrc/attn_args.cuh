@@ -28,6 +28,12 @@ struct AttnArgs {
   mlb_out_targets out;  // final rows: one or more destinations (the call's `out`, or every rank's buffer)
   int out_vec;          // out_vec_ok(out): rows may be stored with packed 16-byte-aligned stores
   int32_t* err;
+  // fused append (mlb_paged_attention_append), app_k == nullptr otherwise: the step's new rows, taken from
+  // here for every page that holds them and stored into the pools at app_slots by the row's last query tile
+  const char* app_k;
+  const char* app_v;
+  int64_t app_k_st, app_k_sh, app_v_st, app_v_sh;  // strides in elements
+  const int64_t* app_slots;
 };
 
 // True when every destination row start is 16-byte aligned (bases and both strides), so a run of

@@ -193,7 +193,7 @@ extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 4; }
+int mlb_abi_version(void) { return 5; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -422,14 +422,19 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   return MLB_OK;
 }
 
-int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k_cache,
-                        const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
-                        int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
-                        const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
-                        int64_t num_units, const mlb_shared_unit* shared_units, int64_t num_shared_units,
-                        const mlb_share_member* members, float* partial_o, float* partial_lse,
-                        int64_t num_partial_rows, void* out, int64_t out_stride_tok, int64_t out_stride_head,
-                        const mlb_out_targets* out_targets, int32_t* err_word, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// mlb_paged_attention and mlb_paged_attention_append: `app` (validated by the caller) or nullptr.
+int attention_call(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k_cache,
+                   const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
+                   int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
+                   const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
+                   int64_t num_units, const mlb_shared_unit* shared_units, int64_t num_shared_units,
+                   const mlb_share_member* members, float* partial_o, float* partial_lse, int64_t num_partial_rows,
+                   void* out, int64_t out_stride_tok, int64_t out_stride_head, const mlb_out_targets* out_targets,
+                   const mlb_append_rows* app, int32_t* err_word, void* stream) {
   if (!elt_bytes(dtype)) return fail(MLB_EINVAL, "paged_attention: unknown dtype %d", dtype);
   if (block_size != mlb::kBlockSize)
     return fail(MLB_EUNSUPPORTED, "paged_attention: block_size %d (kernels are built for 16)", block_size);
@@ -483,6 +488,15 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   a.out = targets;
   a.out_vec = mlb::out_vec_ok(targets, elt_bytes(dtype)) ? 1 : 0;
   a.err = err_word;
+  if (app) {
+    a.app_k = static_cast<const char*>(app->k);
+    a.app_v = static_cast<const char*>(app->v);
+    a.app_k_st = app->k_stride_tok;
+    a.app_k_sh = app->k_stride_head;
+    a.app_v_st = app->v_stride_tok;
+    a.app_v_sh = app->v_stride_head;
+    a.app_slots = app->slot_mapping;
+  }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (num_shared_units > 0) {
     const bool tc = mlb::tensor_core_prefix() && mlb::shared_prefix_tc_supported(a, dtype, head_dim);
@@ -493,6 +507,50 @@ int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_he
   }
   if (num_units == 0) return MLB_OK;
   return cuda_status(mlb::launch_paged_attention(a, dtype, head_dim, num_units, st), "paged_attention launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int mlb_paged_attention(const void* q, int64_t q_stride_tok, int64_t q_stride_head, const void* k_cache,
+                        const void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
+                        int num_kv_heads, int head_dim, float scale, const int32_t* block_tables, int64_t bt_stride,
+                        const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs, const mlb_work_unit* units,
+                        int64_t num_units, const mlb_shared_unit* shared_units, int64_t num_shared_units,
+                        const mlb_share_member* members, float* partial_o, float* partial_lse,
+                        int64_t num_partial_rows, void* out, int64_t out_stride_tok, int64_t out_stride_head,
+                        const mlb_out_targets* out_targets, int32_t* err_word, void* stream) {
+  return attention_call(q, q_stride_tok, q_stride_head, k_cache, v_cache, dtype, num_blocks, block_size, num_heads,
+                        num_kv_heads, head_dim, scale, block_tables, bt_stride, seq_lens, qo_indptr, num_seqs, units,
+                        num_units, shared_units, num_shared_units, members, partial_o, partial_lse, num_partial_rows,
+                        out, out_stride_tok, out_stride_head, out_targets, nullptr, err_word, stream);
+}
+
+int mlb_paged_attention_append(const void* q, int64_t q_stride_tok, int64_t q_stride_head, void* k_cache,
+                               void* v_cache, int dtype, int64_t num_blocks, int block_size, int num_heads,
+                               int num_kv_heads, int head_dim, float scale, const int32_t* block_tables,
+                               int64_t bt_stride, const int32_t* seq_lens, const int32_t* qo_indptr, int num_seqs,
+                               const mlb_work_unit* units, int64_t num_units, const mlb_shared_unit* shared_units,
+                               int64_t num_shared_units, const mlb_share_member* members, float* partial_o,
+                               float* partial_lse, int64_t num_partial_rows, void* out, int64_t out_stride_tok,
+                               int64_t out_stride_head, const mlb_out_targets* out_targets,
+                               const mlb_append_rows* append, int32_t* err_word, void* stream) {
+  if (!append || !append->k || !append->v || !append->slot_mapping)
+    return fail(MLB_EINVAL, "paged_attention_append: null append rows");
+  if (append->num_tokens < 0) return fail(MLB_EINVAL, "paged_attention_append: bad num_tokens");
+  if (dtype != MLB_F16 && dtype != MLB_BF16)
+    return fail(MLB_EUNSUPPORTED, "paged_attention_append: 16-bit pools only (dtype %d)", dtype);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(MLB_EUNSUPPORTED, "paged_attention_append: head_dim %d (supported: 64, 128)", head_dim);
+  if (!aligned(append->k, 16) || !aligned(append->v, 16) || (append->k_stride_tok * 2) % 16 ||
+      (append->k_stride_head * 2) % 16 || (append->v_stride_tok * 2) % 16 || (append->v_stride_head * 2) % 16)
+    return fail(MLB_EINVAL, "paged_attention_append: k / v rows must be 16-byte aligned");
+  if (append->num_tokens == 0) append = nullptr;  // nothing new: plain attention
+  return attention_call(q, q_stride_tok, q_stride_head, k_cache, v_cache, dtype, num_blocks, block_size, num_heads,
+                        num_kv_heads, head_dim, scale, block_tables, bt_stride, seq_lens, qo_indptr, num_seqs, units,
+                        num_units, shared_units, num_shared_units, members, partial_o, partial_lse, num_partial_rows,
+                        out, out_stride_tok, out_stride_head, out_targets, append, err_word, stream);
 }
 
 int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,

@@ -162,6 +162,41 @@ __device__ __forceinline__ void attend_page(uint32_t kaddr, uint32_t vaddr, cons
   }
 }
 
+// Fused append (mlb_paged_attention_append): rows of this page that are new this step (positions
+// [L - n_new, L)) are taken from the call's k / v rows, not from the pool, which need not hold them yet (the
+// page's copy may have read the old slot contents).  The units of the row's last query tile also store them
+// into the pools at slot_mapping; that tile's units split its pages between them, so each new (token, KV
+// head) row is stored once.  Lanes take 16-byte chunks of the rows, K then V.  tok_base: key position of
+// the page's first slot; slot: the page's K tile in the warp's ring (the V tile follows at TILE).
+template <int DH, int ROWB, int TILE>
+__device__ __forceinline__ void take_new_rows(const AttnArgs& a, const UnitInfo& ui, int kvh, uint8_t* slot,
+                                              int tok_base, int lane) {
+  constexpr int CH_ROW = DH * 2 / 16;
+  const int new0 = ui.L - ui.n_new;
+  const int r_lo = max(new0 - tok_base, 0), r_hi = min(ui.L - tok_base, kBlockSize);
+  if (r_lo >= r_hi) return;  // warp-uniform
+  const bool writer = ui.t0 + a.tile_tokens >= ui.n_new;
+  const int64_t slot_end = a.num_blocks * kBlockSize;
+  for (int e = lane; e < (r_hi - r_lo) * 2 * CH_ROW; e += 32) {
+    const int r = r_lo + e / (2 * CH_ROW), kv = (e / CH_ROW) & 1, c = e % CH_ROW;
+    const int64_t t = ui.q0 + (tok_base + r - new0);
+    const char* src = kv ? a.app_v + (t * a.app_v_st + kvh * a.app_v_sh) * 2
+                         : a.app_k + (t * a.app_k_st + kvh * a.app_k_sh) * 2;
+    const uint4 x = __ldg(reinterpret_cast<const uint4*>(src) + c);
+    *reinterpret_cast<uint4*>(slot + kv * TILE + r * ROWB + c * 16) = x;
+    if (writer) {
+      const int64_t sl = __ldg(a.app_slots + t);
+      if (sl >= 0 && sl < slot_end) {
+        char* dst = const_cast<char*>(kv ? a.v_cache : a.k_cache) + (sl * a.hkv + kvh) * (DH * 2);
+        reinterpret_cast<uint4*>(dst)[c] = x;
+      } else if (kv == 0 && c == 0) {
+        flag_error(a.err, MLB_DEV_SLOT_RANGE);
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // ------------------------------------------------------------------ 16-bit pools: tensor-core tiles
 
 // NW warps per CTA, each streaming its pages through a private ring of STAGES shared-memory slots.
@@ -271,6 +306,7 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
     cp_async_wait<STAGES - 1>();     // this lane's copies of page i have landed
     __syncwarp();                    // ... and every other lane's
     const int s = i % STAGES;
+    if (a.app_k) take_new_rows<DH, ROWB, TILE>(a, ui, kvh, ring + s * STAGE, (pb + i * NW) * kBlockSize, lane);
     if (!((bad_mask >> s) & 1u)) {
       const int tok_base = (pb + i * NW) * kBlockSize;
       uint8_t* vt = ring + s * STAGE + TILE;

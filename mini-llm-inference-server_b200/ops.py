@@ -16,7 +16,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import MAX_OUT_DESTS, MEMBER_INT32S, SHARED_UNIT_INT32S, WORK_UNIT_INT32S, OutTargets, check, lib
+from ._lib import (MAX_OUT_DESTS, MEMBER_INT32S, SHARED_UNIT_INT32S, WORK_UNIT_INT32S, AppendRows, OutTargets, check,
+                   lib)
 
 DTYPE_CODE = {torch.float32: _lib.MLB_F32, torch.float16: _lib.MLB_F16, torch.bfloat16: _lib.MLB_BF16}
 BLOCK_SIZE = 16
@@ -188,18 +189,20 @@ class Workspace:
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                     seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan,
                     workspace: Workspace | None = None, out: torch.Tensor | None = None, scale: float | None = None,
-                    err: torch.Tensor | None = None, targets: OutTargets | None = None) -> torch.Tensor | None:
+                    err: torch.Tensor | None = None, targets: OutTargets | None = None,
+                    append: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor | None:
     """paged_attention (paged_torch_ref.py:40-74) on the GPU: q [N, H, Dh] -> [N, H, Dh] in q's dtype.
 
     block_tables int32 [S, W], seq_lens int32 [S], qo_indptr int32 [S + 1] are AttentionMetadata's
     device tensors (block_tables_i32, seq_lens_i32, qo_indptr).  The pools must already hold this
-    step's k/v (kv_append first).  Launches the shared-prefix and per-sequence attention kernels, then
-    the split-K reduction when the plan split any sequence.  With `targets` (see `out_targets`) the rows
-    go to those destinations instead and nothing is returned.
+    step's k/v (kv_append first), unless `append` = (k, v, slot_mapping) asks the attention launch to do
+    the append itself (see `attention_partials`).  Launches the shared-prefix and per-sequence attention
+    kernels, then the split-K reduction when the plan split any sequence.  With `targets` (see
+    `out_targets`) the rows go to those destinations instead and nothing is returned.
     """
     workspace = workspace or Workspace()
     out = attention_partials(q, k_cache, v_cache, block_tables, seq_lens, qo_indptr, plan, workspace, out, scale,
-                             err, targets)
+                             err, targets, append)
     splitk_reduce(plan, workspace, out, targets, q.dtype, q.shape[2], q.device)
     return out
 
@@ -219,9 +222,15 @@ def out_targets(dests: list[int], head_offset: int, stride_tok: int, stride_head
 def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
                        seq_lens: torch.Tensor, qo_indptr: torch.Tensor, plan: AttentionPlan, workspace: Workspace,
                        out: torch.Tensor | None = None, scale: float | None = None,
-                       err: torch.Tensor | None = None, targets: OutTargets | None = None) -> torch.Tensor | None:
+                       err: torch.Tensor | None = None, targets: OutTargets | None = None,
+                       append: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor | None:
     """The attention kernels (K2s, K2a): unsplit sequences are final in `out` (or `targets`); split ones
-    leave fp32 partial rows in `workspace` for `splitk_reduce`."""
+    leave fp32 partial rows in `workspace` for `splitk_reduce`.
+
+    append = (k, v, slot_mapping): kv_append fused into the attention launch (mlb_paged_attention_append;
+    torch_ref.py:46-48 writes, then attends).  The caller guarantees what that entry point needs:
+    slot_mapping is the one the block tables give, and every written block is in one sequence's context
+    pages only (AttentionMetadata.append_private); `can_fuse_append` checks the rest."""
     _check_pool(k_cache, "paged_attention")
     _check_pool(v_cache, "paged_attention")
     nb, bs, hkv, dh = k_cache.shape
@@ -247,15 +256,45 @@ def attention_partials(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     po = plse = None
     if plan.num_partial_rows:
         po, plse = workspace.get(plan.num_partial_rows, h, dh, q.device)
-    rc = lib().mlb_paged_attention(q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
-                                   _code(q, "paged_attention"), nb, bs, h, hkv, dh, scale, block_tables.data_ptr(),
-                                   block_tables.stride(0), seq_lens.data_ptr(), qo_indptr.data_ptr(),
-                                   seq_lens.shape[0], plan.units.data_ptr(), plan.num_units,
-                                   plan.shared_units.data_ptr(), plan.num_shared_units, plan.members.data_ptr(),
-                                   _ptr(po), _ptr(plse), plan.num_partial_rows, _ptr(out), *_strides(out),
-                                   _targets(targets), _ptr(err), _stream(q.device))
-    check(rc, "paged_attention")
+    args = (q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(),
+            _code(q, "paged_attention"), nb, bs, h, hkv, dh, scale, block_tables.data_ptr(), block_tables.stride(0),
+            seq_lens.data_ptr(), qo_indptr.data_ptr(), seq_lens.shape[0], plan.units.data_ptr(), plan.num_units,
+            plan.shared_units.data_ptr(), plan.num_shared_units, plan.members.data_ptr(), _ptr(po), _ptr(plse),
+            plan.num_partial_rows, _ptr(out), *_strides(out), _targets(targets))
+    if append is None:
+        rc = lib().mlb_paged_attention(*args, _ptr(err), _stream(q.device))
+        check(rc, "paged_attention")
+        return out
+    k, v, slots = append
+    if not can_fuse_append(plan, k_cache, k, v):
+        raise ValueError("paged_attention: this append cannot ride in the attention launch (see can_fuse_append)")
+    if slots.dtype != torch.long or not slots.is_contiguous() or slots.shape != (n,) or slots.device != q.device:
+        raise ValueError(f"paged_attention: slot_mapping must be a contiguous int64 [{n}] tensor on {q.device}")
+    rows = AppendRows()
+    rows.k, rows.v, rows.slot_mapping, rows.num_tokens = k.data_ptr(), v.data_ptr(), slots.data_ptr(), n
+    rows.k_stride_tok, rows.k_stride_head, rows.v_stride_tok, rows.v_stride_head = (k.stride(0), k.stride(1),
+                                                                                    v.stride(0), v.stride(1))
+    rc = lib().mlb_paged_attention_append(*args, ctypes.byref(rows), _ptr(err), _stream(q.device))
+    check(rc, "paged_attention_append")
     return out
+
+
+def can_fuse_append(plan: AttentionPlan, k_cache: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> bool:
+    """Whether kv_append can ride in the attention launch, as far as the plan and tensors go: 16-bit pools
+    with head_dim 64 / 128, k / v [N, Hkv, Dh] in the pools' dtype on their device with 16-byte aligned
+    rows, N the plan's token count, and no query-tile units (rows of >= 16 new tokens).  The metadata's
+    half of the condition is AttentionMetadata.append_private."""
+    if k_cache.dtype not in (torch.float16, torch.bfloat16) or k_cache.shape[3] not in (64, 128):
+        return False
+    shape = (plan.num_tokens, k_cache.shape[2], k_cache.shape[3])
+    for t in (k, v):
+        if t.dtype != k_cache.dtype or t.device != k_cache.device or tuple(t.shape) != shape:
+            return False
+        if t.shape[0] and (t.stride(2) != 1 or t.data_ptr() % 16 or (t.stride(0) * 2) % 16 or (t.stride(1) * 2) % 16):
+            return False
+    if plan.num_shared_units and bool(((plan.shared_host[:, 6] & 0xFF) == 1).any()):
+        return False
+    return True
 
 
 def splitk_reduce(plan: AttentionPlan, workspace: Workspace, out: torch.Tensor | None,

@@ -9,6 +9,7 @@ import re
 
 import numpy as np
 import pytest
+import torch
 
 from conftest import REPO
 
@@ -37,7 +38,7 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 4
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 5
 
 
 def test_plan_record_layouts_match_header(L):
@@ -101,6 +102,54 @@ def test_invalid_arguments_return_status_without_launching(L):
         L.check(rc, "paged_attention")
     # zero work is a successful no-op
     assert lib.mlb_block_copy(None, 0, 10, 64, None, None, 0, None, None) == L.MLB_OK
+
+
+def test_fused_append_validates_on_the_host(L, mlb):
+    lib = L.lib()
+    fake = 1 << 20  # never dereferenced: every call below is refused before a launch
+    assert ctypes.sizeof(L.AppendRows) == 64
+
+    def call(rows, dtype=2, dh=128):
+        return lib.mlb_paged_attention_append(fake, 0, 0, fake, fake, dtype, 10, 16, 32, 8, dh, 0.1, fake, 0, fake,
+                                              fake, 1, fake, 1, None, 0, None, None, None, 0, fake, 0, 0, None,
+                                              rows, None, None)
+
+    def rows(**kw):
+        r = L.AppendRows()
+        r.k, r.v, r.slot_mapping, r.num_tokens = fake, fake, fake, 1
+        r.k_stride_tok, r.k_stride_head, r.v_stride_tok, r.v_stride_head = 1024, 128, 1024, 128
+        for name, val in kw.items():
+            setattr(r, name, val)
+        return ctypes.byref(r)
+
+    assert call(None) == L.MLB_EINVAL and "null append" in L.last_error()
+    assert call(rows(slot_mapping=None)) == L.MLB_EINVAL
+    assert call(rows(num_tokens=-1)) == L.MLB_EINVAL
+    assert call(rows(), dtype=0) == L.MLB_EUNSUPPORTED and "16-bit" in L.last_error()
+    assert call(rows(), dh=256) == L.MLB_EUNSUPPORTED
+    for bad in (dict(k=fake + 2), dict(v_stride_head=129), dict(k_stride_tok=1028)):
+        assert call(rows(**bad)) == L.MLB_EINVAL and "16-byte" in L.last_error()
+
+
+def test_can_fuse_append_conditions(mlb):
+    """The plan / tensor half of the fused-append condition (the metadata half is append_private)."""
+    ops = mlb.ops
+    pool = torch.zeros(64, 16, 8, 128, dtype=torch.bfloat16)
+    plan_dec = mlb.plan_attention([0, 1, 2], [40, 70], 8, 32, 8, "cpu")
+    k = torch.zeros(2, 8, 128, dtype=torch.bfloat16)
+    assert ops.can_fuse_append(plan_dec, pool, k, k)
+    assert ops.can_fuse_append(plan_dec, pool, torch.zeros(2, 24, 128, dtype=torch.bfloat16)[:, 8:16], k)  # a view
+    assert not ops.can_fuse_append(plan_dec, pool, k.float(), k)  # k / v must be in the pools' dtype
+    assert not ops.can_fuse_append(plan_dec, pool.float(), k.float(), k.float())  # f32 pools
+    assert not ops.can_fuse_append(plan_dec, pool, k[:1], k[:1])  # not the plan's token count
+    assert not ops.can_fuse_append(plan_dec, pool, torch.zeros(2, 8, 132, dtype=torch.bfloat16)[..., :128], k)
+    # a row of >= 16 new tokens becomes query-tile units with host tables: those launches need the append first
+    tables = np.arange(16, dtype=np.int32).reshape(2, 8)
+    plan_pre = mlb.plan_attention([0, 1, 21], [40, 70], 8, 32, 8, "cpu", block_tables_host=tables)
+    k21 = torch.zeros(21, 8, 128, dtype=torch.bfloat16)
+    assert not ops.can_fuse_append(plan_pre, pool, k21, k21)
+    plan_pre_nt = mlb.plan_attention([0, 1, 21], [40, 70], 8, 32, 8, "cpu")  # no tables: 8-column tiles
+    assert ops.can_fuse_append(plan_pre_nt, pool, k21, k21)
 
 
 def plan(mlb, steps, h=32, hkv=8, ppu=0, sms=148, width=None):

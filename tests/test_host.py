@@ -57,6 +57,21 @@ def test_metadata_known_answer():  # tests/test_paged.py:41-50 of the reference,
     assert meta.block_tables.tolist() == [[7, 0], [2, 9]] and meta.logits_index.tolist() == [0, 5]
 
 
+def test_append_private_flag(mlb):
+    """append_private: every block that receives a row is among all sequences' context pages once."""
+    S = mlb.SeqStep
+    build = lambda seqs: mlb.AttentionMetadata.build(seqs, 4, "cpu").append_private
+    assert build([S(3, 1, [7]), S(0, 5, [2, 9])])
+    assert build([S(4, 1, [7, 3]), S(4, 1, [7, 5])])  # a shared prefix block, but the writes go to 3 and 5
+    assert not build([S(2, 1, [7]), S(3, 1, [7])])  # both rows write block 7
+    assert not build([S(2, 1, [7]), S(4, 0, [7])])  # another sequence reads the written block
+    assert not build([S(5, 1, [4, 4])])  # the same block twice in one table
+    assert not build([S(1, 1, [-1])])  # an invalid id: no fusion, the separate append flags it
+    assert build([S(3, 0, [7])])  # nothing written
+    # a block beyond a sequence's context pages is not read by it
+    assert build([S(2, 1, [7]), S(4, 0, [6, 1, 7])])
+
+
 # ---------- block manager: the reference's accounting (tests/test_paged.py:152-163, test_prefix_cache.py:69-93)
 
 
