@@ -635,8 +635,9 @@ def run_ours(args) -> None:
 
 
 def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx) -> dict:
-    """Each step, through the public API with pinned host buffers: AttentionMetadata.build (its own H2D
-    copies); the q/k/v rows of every layer copied host-to-device on a loader stream in 4 growing chunks
+    """Each step, through the public API with pinned host buffers: AttentionMetadata.build and the backend's
+    plan (their own H2D copies, issued on the loader stream ahead of the inputs); the q/k/v rows of every
+    layer copied host-to-device on the loader stream in 4 growing chunks
     (layers [0,1), [1,3), [3,8), [8,L): each lands while the layers before it compute); per layer the
     backend's forward once its chunk is in, and a device-to-host copy of its output on a copier stream
     (layer l's read-back overlaps layer l + 1's attention); the step ends when the last output is on the
@@ -686,11 +687,18 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     step_done = torch.cuda.Event()
     step_done.record(compute)
 
+    inner = backend.inner if world > 1 else backend
+    h_l, hkv_l = q.shape[1] // world, k_pools[0].shape[2]
+
     def step():
-        meta = mlb.AttentionMetadata.build(seqs, BS, dev)
-        loader.wait_event(step_done)  # the previous step has read every layer's inputs
-        with torch.cuda.stream(loader):  # the step's q/k/v rows in a few growing chunks
-            for c, (lo, hi) in enumerate(chunks):
+        loader.wait_event(step_done)  # the previous step has read every layer's inputs, metadata and plan
+        with torch.cuda.stream(loader):
+            # the step's metadata and plan go first in the loader's queue: on the compute stream their small
+            # host-to-device copies queued behind the loader's input chunks (a measured ~0.48 ms at every
+            # step start); layer 0 waits for the first chunk, so for them too
+            meta = mlb.AttentionMetadata.build(seqs, BS, dev)
+            inner.plan(meta, h_l, hkv_l, dev, q.dtype)
+            for c, (lo, hi) in enumerate(chunks):  # then the q/k/v rows in a few growing chunks
                 dev_in[lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer], non_blocking=True)
                 loaded[c].record(loader)
         for l in range(layers):
@@ -719,20 +727,28 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         compute.wait_stream(copier)
         step_done.record(compute)
 
-    for _ in range(max(1, args.warmup)):
+    # warm-up as long as a timed window (and no synchronisation inside it): the host runs ahead of the device
+    # by a growing number of steps, and torch's pinned staging buffers (metadata, plan) grow with that lead;
+    # a short warm-up left their growth to the first timed window
+    for _ in range(max(1, args.warmup) + args.steps):
         step()
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
+    # three timed windows of `steps` steps each, the median reported: the eager path is the host's pace
+    # when the host stalls (other jobs on the machine), and one stall must not stand for the path
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(s.elapsed_time(e), world, dev) / args.steps
+    windows = []
+    for _ in range(3):
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        windows.append(max_over_ranks(s.elapsed_time(e), world, dev) / args.steps)
+    ms = statistics.median(windows)
     if world > 1:
         backend.close()
     total = kv_bytes(ctx, HKV) * layers
@@ -740,6 +756,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     h2d = layers * per_layer + meta_bytes
     d2h = layers * q.numel() * q.element_size()
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+            "window_ms_per_step": [round(w, 4) for w in windows],
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "path": (f"KVHeadShardedBackend(transport={args.transport!r})" if world > 1 else "B200Backend")
                     + ".forward per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "

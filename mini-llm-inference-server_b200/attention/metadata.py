@@ -13,6 +13,7 @@ Example (block size 16): sequence 0 has 3 tokens cached and adds 1; sequence 1 i
 
 from __future__ import annotations
 
+import itertools
 from dataclasses import dataclass
 
 import numpy as np
@@ -82,8 +83,9 @@ class AttentionMetadata:
             raise ValueError(f"{int(nblk[i])} blocks can't hold {int(ends[i])} tokens")
         width = int(nblk.max()) if s else 0
         table = np.zeros((s, width), dtype=np.int64)
-        for i, q in enumerate(seqs):
-            table[i, :len(q.block_ids)] = q.block_ids
+        # every sequence's ids in one pass (row-major order is the mask's order)
+        table[np.arange(width)[None, :] < nblk[:, None]] = np.fromiter(
+            itertools.chain.from_iterable(q.block_ids for q in seqs), dtype=np.int64, count=int(nblk.sum()))
         starts = np.zeros(s + 1, dtype=np.int64)
         np.cumsum(new, out=starts[1:])
         n = int(starts[-1])

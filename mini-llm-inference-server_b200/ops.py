@@ -114,6 +114,7 @@ class AttentionPlan:
     members_host: np.ndarray
     reduce_rows_host: np.ndarray
     reduce_chunks_host: np.ndarray  # [N] pieces per token on the host
+    has_query_tiles: bool = False  # kind-1 shared units (rows of >= 16 new tokens) in the plan
 
 
 def _i32(a) -> np.ndarray:
@@ -167,7 +168,7 @@ def plan_attention(qo_indptr: list[int], seq_lens: list[int], max_blocks: int, n
                          seg[2].view(m, MEMBER_INT32S), seg[3], seg[4], npart.value,
                          max(1, 8 // (num_heads // num_kv_heads)), num_heads, num_kv_heads, n_tok,
                          units[:u].copy(), shared[:sh].copy(), members[:m].copy(), rows[:n_tok].copy(),
-                         chunks[:n_tok].copy())
+                         chunks[:n_tok].copy(), bool(sh and ((shared[:sh, 6] & 0xFF) == 1).any()))
 
 
 class Workspace:
@@ -284,16 +285,17 @@ def can_fuse_append(plan: AttentionPlan, k_cache: torch.Tensor, k: torch.Tensor,
     with head_dim 64 / 128, k / v [N, Hkv, Dh] in the pools' dtype on their device with 16-byte aligned
     rows, N the plan's token count, and no query-tile units (rows of >= 16 new tokens).  The metadata's
     half of the condition is AttentionMetadata.append_private."""
-    if k_cache.dtype not in (torch.float16, torch.bfloat16) or k_cache.shape[3] not in (64, 128):
+    dt = k_cache.dtype
+    if plan.has_query_tiles or (dt is not torch.bfloat16 and dt is not torch.float16) or k_cache.shape[3] not in (64, 128):
         return False
     shape = (plan.num_tokens, k_cache.shape[2], k_cache.shape[3])
     for t in (k, v):
-        if t.dtype != k_cache.dtype or t.device != k_cache.device or tuple(t.shape) != shape:
+        if t.dtype is not dt or t.shape != shape or t.device != k_cache.device:
             return False
-        if t.shape[0] and (t.stride(2) != 1 or t.data_ptr() % 16 or (t.stride(0) * 2) % 16 or (t.stride(1) * 2) % 16):
-            return False
-    if plan.num_shared_units and bool(((plan.shared_host[:, 6] & 0xFF) == 1).any()):
-        return False
+        if shape[0]:
+            s0, s1, s2 = t.stride()
+            if s2 != 1 or (s0 | s1) & 7 or t.data_ptr() & 15:  # 16-byte rows: strides x 2 B multiples of 16
+                return False
     return True
 
 
