@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 5 */
+MLB_API int mlb_abi_version(void);  /* 6 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -249,6 +249,27 @@ MLB_API int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, 
                       int64_t num_tokens, int num_heads, int head_dim,
                       void* out, int64_t out_stride_tok, int64_t out_stride_head, int out_dtype,
                       const mlb_out_targets* out_targets, void* stream);
+
+/*
+ * Device-side expansion of a step's attention metadata: the per-token, per-page and padded-table parts of
+ * AttentionMetadata.build (src/minillm/attention/metadata.py:71-103) computed on the GPU from a compact
+ * upload.  `in` (device int64) holds, back to back:
+ *   ids [num_ids]           every sequence's block ids, concatenated
+ *   ids_indptr [S + 1]      offsets of each sequence's ids in `ids`
+ *   qo_indptr [S + 1]       token offsets (query_start_loc, metadata.py:84)
+ *   seq_lens [S]            context lengths after this step
+ *   kv_indptr [S + 1]       offsets of each sequence's context pages, ceil(seq_len / block_size) each
+ *   kv_last_page_len [S]
+ * (S = num_seqs; every sequence's ids must cover its seq_len).  The call fills
+ *   out64: positions [N] | slot_mapping [N] | block_tables [S, width] | logits_index [S]
+ *   out32: qo_indptr [S + 1] | seq_lens [S] | block_tables [S, width] | kv_indptr [S + 1] |
+ *          kv_indices [num_pages] | kv_last_page_len [S]
+ * with N = num_tokens = qo_indptr[S] and num_pages = kv_indptr[S]: the reference's fields (metadata.py:94-102),
+ * tables padded with block 0 and int32 values the int64 ones truncated, as Tensor.to(torch.int32) does.
+ */
+MLB_API int mlb_build_metadata(const int64_t* in, int64_t num_ids, int num_seqs, int64_t num_tokens,
+                               int64_t num_pages, int width, int block_size, int64_t* out64, int32_t* out32,
+                               void* stream);
 
 /*
  * Block copy for prefix-cache copy-on-write and compaction: pool[dst[i]] = pool[src[i]] for every pool

@@ -21,8 +21,9 @@ DEV_SLOT_RANGE, DEV_BLOCK_RANGE, DEV_WAIT_TIMEOUT, DEV_COPY_RANGE = 1, 2, 4, 8
 EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_attention", "mlb_paged_attention",
            "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc", "mlb_ipc_alloc", "mlb_ipc_open",
            "mlb_ipc_close", "mlb_ipc_free", "mlb_peer_barrier", "mlb_set_programmatic_launch",
-           "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix", "mlb_paged_attention_append")
-ABI_VERSION = 5
+           "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix", "mlb_paged_attention_append",
+           "mlb_build_metadata")
+ABI_VERSION = 6
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 MAX_OUT_DESTS = 8  # MLB_MAX_OUT_DESTS
 IPC_HANDLE_BYTES = 64  # MLB_IPC_HANDLE_BYTES
@@ -92,6 +93,8 @@ _SIGNATURES = {
                                   c_void_p, c_int64, c_int64, c_int, POINTER(OutTargets), c_void_p]),
     "mlb_block_copy": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                                c_void_p]),
+    "mlb_build_metadata": (c_int, [c_void_p, c_int64, c_int, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p,
+                                   c_void_p]),
     "mlb_paged_attention_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
                                             c_int, c_int, c_int, c_float, c_void_p, c_int64, c_void_p, c_void_p,
                                             c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64,

@@ -71,6 +71,9 @@ class AttentionMetadata:
 
     @classmethod
     def build(cls, seqs: list[SeqStep], block_size: int, device: torch.device | str) -> AttentionMetadata:
+        """The step's metadata (metadata.py:71-103).  On a CUDA device the host sends the block ids and
+        O(S) prefix arrays in one upload and `mlb_build_metadata` expands the per-token / per-page arrays
+        and both padded tables on the GPU; elsewhere numpy computes them.  Same values either way."""
         device = torch.device(device)
         s = len(seqs)
         cached = np.fromiter((q.num_cached for q in seqs), dtype=np.int64, count=s)
@@ -82,33 +85,48 @@ class AttentionMetadata:
             i = int(short[0])
             raise ValueError(f"{int(nblk[i])} blocks can't hold {int(ends[i])} tokens")
         width = int(nblk.max()) if s else 0
-        table = np.zeros((s, width), dtype=np.int64)
-        # every sequence's ids in one pass (row-major order is the mask's order)
-        table[np.arange(width)[None, :] < nblk[:, None]] = np.fromiter(
-            itertools.chain.from_iterable(q.block_ids for q in seqs), dtype=np.int64, count=int(nblk.sum()))
+        ids = np.fromiter(itertools.chain.from_iterable(q.block_ids for q in seqs), dtype=np.int64,
+                          count=int(nblk.sum()))
         starts = np.zeros(s + 1, dtype=np.int64)
         np.cumsum(new, out=starts[1:])
         n = int(starts[-1])
-        owner = np.repeat(np.arange(s), new)  # sequence of each new token
-        positions = np.arange(n, dtype=np.int64) - starts[owner] + cached[owner]
-        slots = table[owner, positions // block_size] * block_size + positions % block_size
         used = -(-ends // block_size)  # pages holding context
         kv_indptr = np.zeros(s + 1, dtype=np.int64)
         np.cumsum(used, out=kv_indptr[1:])
-        kv_indices = table[np.arange(width)[None, :] < used[:, None]]  # row-major: sequence by sequence
         last_len = ends - (used - 1) * block_size
-        # the block of every new row must occur once among all sequences' context pages
-        private = n == 0
-        if n and kv_indices.size and int(kv_indices.min()) >= 0:
-            counts = np.bincount(kv_indices)
-            private = bool((counts[table[owner, positions // block_size]] == 1).all())
+        ids_indptr = np.zeros(s + 1, dtype=np.int64)
+        np.cumsum(nblk, out=ids_indptr[1:])
+        owner = np.repeat(np.arange(s), new)  # sequence of each new token
+        positions = np.arange(n, dtype=np.int64) - starts[owner] + cached[owner]
+        written = ids[ids_indptr[owner] + positions // block_size]  # block of every new row
+        if bool((nblk == used).all()):
+            used_ids = ids
+        else:  # the ids beyond each context's last page are not read
+            col = np.arange(ids.size) - np.repeat(ids_indptr[:-1], nblk)
+            used_ids = ids[col < np.repeat(used, nblk)]
+        mask = np.arange(width)[None, :] < nblk[:, None]  # row-major order is the ids' order
+        table32 = np.zeros((s, width), dtype=np.int32)
+        table32[mask] = ids  # truncated to int32 like Tensor.to(torch.int32)
 
-        # two transfers: every int64 tensor in one buffer, every int32 tensor in another
-        i64 = np.concatenate([positions, slots, table.reshape(-1), starts[1:] - 1])
-        i32 = np.concatenate([starts, ends, table.reshape(-1), kv_indptr, kv_indices, last_len]).astype(np.int32)
-        d64, d32 = _to_device(i64, device), _to_device(i32, device)
+        if device.type == "cuda":
+            from .. import ops
+
+            upload = _to_device(np.concatenate([ids, ids_indptr, starts, ends, kv_indptr, last_len]), device)
+            d64 = torch.empty(2 * n + s * width + s, dtype=torch.int64, device=device)
+            d32 = torch.empty(s * width + 4 * s + 2 + int(kv_indptr[-1]), dtype=torch.int32, device=device)
+            if s:
+                ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
+        else:
+            table = np.zeros((s, width), dtype=np.int64)
+            table[mask] = ids
+            slots = written * block_size + positions % block_size
+            kv_indices = table[np.arange(width)[None, :] < used[:, None]]  # row-major: sequence by sequence
+            # two transfers: every int64 tensor in one buffer, every int32 tensor in another
+            i64 = np.concatenate([positions, slots, table.reshape(-1), starts[1:] - 1])
+            i32 = np.concatenate([starts, ends, table.reshape(-1), kv_indptr, kv_indices, last_len]).astype(np.int32)
+            d64, d32 = _to_device(i64, device), _to_device(i32, device)
         o64 = np.cumsum([0, n, n, s * width, s])
-        o32 = np.cumsum([0, s + 1, s, s * width, s + 1, kv_indices.size, s])
+        o32 = np.cumsum([0, s + 1, s, s * width, s + 1, int(kv_indptr[-1]), s])
         return cls(
             block_size=block_size,
             query_start_loc=starts.tolist(),
@@ -123,9 +141,19 @@ class AttentionMetadata:
             kv_indptr=d32[o32[3]:o32[4]],
             kv_indices=d32[o32[4]:o32[5]],
             kv_last_page_len=d32[o32[5]:o32[6]],
-            block_tables_host=table.astype(np.int32),
-            append_private=private,
+            block_tables_host=table32,
+            append_private=_written_private(written, used_ids),
         )
+
+
+def _written_private(written: np.ndarray, used_ids: np.ndarray) -> bool:
+    """Every written block occurs once among all sequences' context pages (`written` is a subset of them)."""
+    if written.size == 0:
+        return True
+    lo, hi = int(used_ids.min()), int(used_ids.max())
+    if lo < 0 or hi >= 1 << 26:  # an invalid id, or ids too large to count densely: keep the separate append
+        return False
+    return bool((np.bincount(used_ids)[written] == 1).all())
 
 
 def _to_device(a: np.ndarray, device: torch.device) -> torch.Tensor:

@@ -29,6 +29,9 @@ cudaError_t launch_splitk_reduce_gather(const float* po, const float* plse, cons
 cudaError_t launch_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
                               const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err, int num_sms,
                               cudaStream_t s);
+cudaError_t launch_build_metadata(const int64_t* in, int64_t num_ids, int num_seqs, int64_t num_tokens,
+                                  int64_t num_pages, int width, int block_size, int64_t* out64, int32_t* out32,
+                                  cudaStream_t s);
 }  // namespace mlb
 
 namespace {
@@ -193,7 +196,7 @@ extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 5; }
+int mlb_abi_version(void) { return 6; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -608,6 +611,19 @@ int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_
   return cuda_status(mlb::launch_block_copy(pools, num_pools, num_blocks, block_bytes, src, dst, num_pairs, err_word,
                                             sm_count(), static_cast<cudaStream_t>(stream)),
                      "block_copy launch");
+}
+
+int mlb_build_metadata(const int64_t* in, int64_t num_ids, int num_seqs, int64_t num_tokens, int64_t num_pages,
+                       int width, int block_size, int64_t* out64, int32_t* out32, void* stream) {
+  if (num_ids < 0 || num_seqs < 0 || num_tokens < 0 || num_pages < 0 || width < 0 || block_size <= 0)
+    return fail(MLB_EINVAL, "build_metadata: bad sizes");
+  if (num_tokens > INT32_MAX || num_pages > INT32_MAX)
+    return fail(MLB_EINVAL, "build_metadata: more than 2^31 tokens or pages (int32 offsets)");
+  if (num_seqs == 0) return MLB_OK;
+  if (!in || !out64 || !out32) return fail(MLB_EINVAL, "build_metadata: null pointer");
+  return cuda_status(mlb::launch_build_metadata(in, num_ids, num_seqs, num_tokens, num_pages, width, block_size, out64,
+                                                out32, static_cast<cudaStream_t>(stream)),
+                     "build_metadata launch");
 }
 
 }  // extern "C"

@@ -341,6 +341,26 @@ def _targets(t: OutTargets | None):
     return ctypes.byref(t) if t is not None else None
 
 
+# ---------------------------------------------------------------- metadata expansion on the device
+
+
+def build_metadata(upload: torch.Tensor, num_ids: int, num_seqs: int, num_tokens: int, num_pages: int, width: int,
+                   block_size: int, out64: torch.Tensor, out32: torch.Tensor) -> None:
+    """mlb_build_metadata: expand a step's compact int64 upload (block ids, ids_indptr, qo_indptr, seq_lens,
+    kv_indptr, kv_last_page_len) into the two buffers AttentionMetadata's device tensors view
+    (metadata.py:71-103's arrays, computed on the GPU)."""
+    s = num_seqs
+    need = {"upload": (upload, torch.long, num_ids + 5 * s + 3),
+            "out64": (out64, torch.long, 2 * num_tokens + s * width + s),
+            "out32": (out32, torch.int32, s * width + 4 * s + 2 + num_pages)}
+    for name, (t, dt, n) in need.items():
+        if t.dtype != dt or not t.is_contiguous() or not t.is_cuda or t.device != upload.device or t.numel() < n:
+            raise ValueError(f"build_metadata: {name} must be a contiguous {dt} CUDA tensor of >= {n} elements")
+    rc = lib().mlb_build_metadata(upload.data_ptr(), num_ids, s, num_tokens, num_pages, width, block_size,
+                                  out64.data_ptr(), out32.data_ptr(), _stream(upload.device))
+    check(rc, "build_metadata")
+
+
 # ---------------------------------------------------------------- K3: block copy
 
 

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 5
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 6
 
 
 def test_plan_record_layouts_match_header(L):
@@ -129,6 +129,17 @@ def test_fused_append_validates_on_the_host(L, mlb):
     assert call(rows(), dh=256) == L.MLB_EUNSUPPORTED
     for bad in (dict(k=fake + 2), dict(v_stride_head=129), dict(k_stride_tok=1028)):
         assert call(rows(**bad)) == L.MLB_EINVAL and "16-byte" in L.last_error()
+
+
+def test_build_metadata_validates_on_the_host(L):
+    lib = L.lib()
+    fake = 1 << 20  # never dereferenced: every call below is refused before a launch (or does nothing)
+    call = lambda *a: lib.mlb_build_metadata(*a, None)
+    assert call(fake, 10, 2, 3, 4, 8, 0, fake, fake) == L.MLB_EINVAL and "bad sizes" in L.last_error()
+    assert call(fake, -1, 2, 3, 4, 8, 16, fake, fake) == L.MLB_EINVAL
+    assert call(fake, 10, 2, 1 << 31, 4, 8, 16, fake, fake) == L.MLB_EINVAL and "2^31" in L.last_error()
+    assert call(None, 10, 2, 3, 4, 8, 16, fake, fake) == L.MLB_EINVAL and "null" in L.last_error()
+    assert call(None, 0, 0, 0, 0, 0, 16, None, None) == L.MLB_OK  # no sequences: nothing to do
 
 
 def test_can_fuse_append_conditions(mlb):
