@@ -382,6 +382,7 @@ def run_ours(args) -> None:
     ops = mlb.ops
     mlb._lib.lib().mlb_set_programmatic_launch(0 if args.no_pdl else 1)
     mlb._lib.lib().mlb_set_tensor_core_prefix(0 if args.no_tc_prefix else 1)
+    mlb._lib.lib().mlb_set_concurrent_prefix(0 if args.serial_prefix else 1)
 
     weak = world > 1 and args.config == 2 and args.scaling == "weak"
     if args.config == 2:
@@ -594,6 +595,7 @@ def run_ours(args) -> None:
                        "programmatic_launch": not args.no_pdl,
                        "append": "fused into the attention launch" if fused else "separate K1 launch",
                        "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
+                       "shared_prefix_beside_per_sequence_kernel": not args.serial_prefix,
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
@@ -824,6 +826,8 @@ def main() -> None:
                     help="plan without host tables: every row on the decode kernel's 8-column units")
     ap.add_argument("--no-fused-append", action="store_true",
                     help="launch the append (K1) before attention even when it could ride in the attention launch")
+    ap.add_argument("--serial-prefix", action="store_true",
+                    help="run the shared-prefix kernel before the per-sequence kernel instead of beside it")
     ap.add_argument("--no-tc-prefix", action="store_true",
                     help="shared-prefix units on the mma.sync kernel instead of tcgen05")
     args = ap.parse_args()

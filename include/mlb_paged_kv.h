@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 6 */
+MLB_API int mlb_abi_version(void);  /* 7 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -65,6 +65,16 @@ MLB_API int mlb_set_programmatic_launch(int enable);
  * Returns the previous setting.
  */
 MLB_API int mlb_set_tensor_core_prefix(int enable);
+
+/*
+ * Shared-prefix units beside the per-sequence units (process-wide, default on): when a plan has both, the
+ * shared-prefix kernel runs on a library-owned side stream of the greatest priority (one per host thread
+ * and device, created on the first such call: make it before any stream capture) while the per-sequence
+ * kernel runs on the caller's stream, forked from and joined back into the caller's stream with events, so
+ * work queued after the call waits for both.  Results are identical either way.  Returns the previous
+ * setting.
+ */
+MLB_API int mlb_set_concurrent_prefix(int enable);
 
 /*
  * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three

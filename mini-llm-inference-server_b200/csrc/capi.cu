@@ -20,6 +20,7 @@ cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh,
 bool shared_prefix_tc_supported(const AttnArgs& a, int dtype, int dh);
 cudaError_t launch_shared_prefix_tc(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s);
 bool tensor_core_prefix();
+bool concurrent_prefix();  // mlb_set_concurrent_prefix
 cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32_t* rrows, const int32_t* rchunks,
                                  int tpt, int64_t ntok, int h, int dh, const mlb_out_targets& out,
                                  int out_dtype, cudaStream_t s);
@@ -93,6 +94,33 @@ int sm_count() {
   int dev = 0, n = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n;
+}
+
+// A side stream of the greatest priority and two events, per host thread and device, created on first use
+// and kept for the thread's life: the shared-prefix kernel runs there beside the per-sequence kernel.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+cudaError_t side_stream(SideStream** out) {
+  constexpr int kMaxDevices = 64;
+  thread_local SideStream pool[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  SideStream& s = pool[dev];
+  if (!s.join) {
+    int least = 0, greatest = 0;
+    if ((e = cudaDeviceGetStreamPriorityRange(&least, &greatest)) != cudaSuccess) return e;
+    if (!s.stream && (e = cudaStreamCreateWithPriority(&s.stream, cudaStreamNonBlocking, greatest)) != cudaSuccess)
+      return e;
+    if (!s.fork && (e = cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming)) != cudaSuccess) return e;
+    if ((e = cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming)) != cudaSuccess) return e;
+  }
+  *out = &s;
+  return cudaSuccess;
 }
 
 struct Group {
@@ -187,16 +215,18 @@ int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
 namespace {
 std::atomic<int> g_programmatic_launch{1};
 std::atomic<int> g_tensor_core_prefix{1};
+std::atomic<int> g_concurrent_prefix{1};
 }  // namespace
 bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
 bool tensor_core_prefix() { return g_tensor_core_prefix.load(std::memory_order_relaxed) != 0; }
+bool concurrent_prefix() { return g_concurrent_prefix.load(std::memory_order_relaxed) != 0; }
 }  // namespace mlb
 
 extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 6; }
+int mlb_abi_version(void) { return 7; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -204,6 +234,10 @@ int mlb_set_programmatic_launch(int enable) {
 
 int mlb_set_tensor_core_prefix(int enable) {
   return mlb::g_tensor_core_prefix.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+}
+
+int mlb_set_concurrent_prefix(int enable) {
+  return mlb::g_concurrent_prefix.exchange(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
@@ -501,11 +535,30 @@ int attention_call(const void* q, int64_t q_stride_tok, int64_t q_stride_head, c
     a.app_slots = app->slot_mapping;
   }
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool tc = num_shared_units > 0 && mlb::tensor_core_prefix() && mlb::shared_prefix_tc_supported(a, dtype, head_dim);
+  auto launch_shared = [&](cudaStream_t s) {
+    return tc ? mlb::launch_shared_prefix_tc(a, dtype, head_dim, num_shared_units, s)
+              : mlb::launch_shared_prefix_attention(a, dtype, head_dim, num_shared_units, s);
+  };
+  if (num_shared_units > 0 && num_units > 0 && mlb::concurrent_prefix()) {
+    // The two kernels write disjoint rows and neither reads what the other writes (a page written by the
+    // fused append is private to its row, never part of a shared unit): fork the shared-prefix kernel onto
+    // a high-priority side stream (its CTAs, one per SM, are placed first), run the per-sequence kernel
+    // beside it on the caller's stream (it fills the free SMs and the shared kernel's tail), and join, so
+    // whatever the caller queues next (the split-K reduction) waits for both.  Captures into CUDA graphs
+    // as a fork and a join.
+    SideStream* ss = nullptr;
+    cudaError_t e = side_stream(&ss);
+    if (e == cudaSuccess) e = cudaEventRecord(ss->fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->stream, ss->fork, 0);
+    if (e == cudaSuccess) e = launch_shared(ss->stream);
+    if (e == cudaSuccess) e = mlb::launch_paged_attention(a, dtype, head_dim, num_units, st);
+    if (e == cudaSuccess) e = cudaEventRecord(ss->join, ss->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ss->join, 0);
+    return cuda_status(e, "paged_attention launch (shared-prefix kernel on a side stream)");
+  }
   if (num_shared_units > 0) {
-    const bool tc = mlb::tensor_core_prefix() && mlb::shared_prefix_tc_supported(a, dtype, head_dim);
-    const int rc = cuda_status(tc ? mlb::launch_shared_prefix_tc(a, dtype, head_dim, num_shared_units, st)
-                                  : mlb::launch_shared_prefix_attention(a, dtype, head_dim, num_shared_units, st),
-                               "shared-prefix attention launch");
+    const int rc = cuda_status(launch_shared(st), "shared-prefix attention launch");
     if (rc != MLB_OK) return rc;
   }
   if (num_units == 0) return MLB_OK;

@@ -139,3 +139,58 @@ def test_programmatic_launch_changes_no_bit(mlb, cuda):
     for (o1, p1), (o2, p2) in zip(zip(*results[0]), zip(*results[1])):
         assert torch.equal(o1.view(torch.int16), o2.view(torch.int16))
         assert torch.equal(p1[0], p2[0]) and torch.equal(p1[1], p2[1])
+
+
+@pytest.mark.parametrize("tc", [1, 0], ids=["tcgen05", "mma_sync"])
+def test_concurrent_prefix_kernel_changes_no_bit(mlb, cuda, tc):
+    """mlb_set_concurrent_prefix: the shared-prefix / query-tile kernel on the library's side stream beside the
+    per-sequence kernel (forked from and joined into the caller's stream) gives the same bits as the two
+    launches in a row, eagerly and replayed from a CUDA graph, layer after layer."""
+    lib = mlb._lib.lib()
+    prev_tc, prev_cc = lib.mlb_set_tensor_core_prefix(tc), lib.mlb_set_concurrent_prefix(1)
+    try:
+        r = random.Random(11)
+        ids = list(range(1500))
+        r.shuffle(ids)
+        prefix, nxt, seqs = ids[:20], 20, []
+        steps = [(20 * 16 + r.randint(0, 60), 1) for _ in range(40)] + [(0, 40), (700, 33), (90, 1), (3000, 1)]
+        for i, (c, n) in enumerate(steps):
+            need = -(-(c + n) // 16)
+            head = prefix if i < 40 else []
+            seqs.append(mlb.SeqStep(c, n, head + ids[nxt:nxt + need - len(head)]))
+            nxt += need - len(head)
+        meta = mlb.AttentionMetadata.build(seqs, 16, cuda)
+        ntok = meta.query_start_loc[-1]
+        g = torch.Generator(device=cuda).manual_seed(2)
+        pools = [(torch.randn(1500, 16, 8, 128, device=cuda, generator=g).to(torch.bfloat16),
+                  torch.randn(1500, 16, 8, 128, device=cuda, generator=g).to(torch.bfloat16)) for _ in range(3)]
+        q = torch.randn(ntok, 32, 128, device=cuda, generator=g).to(torch.bfloat16)
+        k = torch.randn(ntok, 8, 128, device=cuda, generator=g).to(torch.bfloat16)
+        v = torch.randn(ntok, 8, 128, device=cuda, generator=g).to(torch.bfloat16)
+
+        def run(concurrent, graph=False):
+            lib.mlb_set_concurrent_prefix(concurrent)
+            backend = mlb.B200Backend()
+            layers = [(kp.clone(), vp.clone()) for kp, vp in pools]
+            outs = [backend.forward(q, k, v, kp, vp, meta) for kp, vp in layers]  # eager (and warm-up)
+            if not graph:
+                return outs
+            layers = [(kp.clone(), vp.clone()) for kp, vp in pools]
+            torch.cuda.synchronize()
+            cg = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(cg):
+                outs = [backend.forward(q, k, v, kp, vp, meta) for kp, vp in layers]
+            cg.replay()
+            cg.replay()
+            torch.cuda.synchronize()
+            return [o.clone() for o in outs]
+
+        serial = run(0)
+        plan = mlb.B200Backend().plan(meta, 32, 8, cuda)
+        assert plan.num_shared_units > 0 and plan.num_units > 0 and plan.has_query_tiles
+        for got in (run(1), run(1, graph=True)):
+            for a, b in zip(got, serial):
+                assert torch.equal(a, b)
+    finally:
+        lib.mlb_set_tensor_core_prefix(prev_tc)
+        lib.mlb_set_concurrent_prefix(prev_cc)
