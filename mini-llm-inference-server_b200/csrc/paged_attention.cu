@@ -693,23 +693,51 @@ __device__ __forceinline__ void load_f32(const float* p, float (&x)[N]) {
 template <int DH>
 __device__ __forceinline__ void reduce_token_head(const float* po, const float* plse, int64_t r0, int nc, int tpt,
                                                   int h, int head, int lane, float (&acc)[DH / 32]) {
-  constexpr int DPL = DH / 32;
-  float M = kNegInf;
-  for (int c = lane; c < nc; c += 32) M = fmaxf(M, plse[(r0 + static_cast<int64_t>(c) * tpt) * h + head]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+  constexpr int DPL = DH / 32, BATCH = 4;
 #pragma unroll
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
   float lw = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const int64_t row = r0 + static_cast<int64_t>(c) * tpt;
-    const float lse = plse[row * h + head];
-    const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
-    lw += w;
-    float x[DPL];
-    load_f32<DPL>(po + (row * h + head) * DH + lane * DPL, x);
+  if (nc <= 32) {
+    // lane c holds piece c's log2-sum-exp (one round trip for all pieces); max, weights and their sum by
+    // shuffles; the pieces' rows then load BATCH at a time, independent of each other
+    const float lse = lane < nc ? plse[(r0 + static_cast<int64_t>(lane) * tpt) * h + head] : kNegInf;
+    float M = lse;
 #pragma unroll
-    for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, x[i], acc[i]);
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float w_lane = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
+    lw = w_lane;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
+    for (int c0 = 0; c0 < nc; c0 += BATCH) {
+      float x[BATCH][DPL];
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j)
+        if (c0 + j < nc)
+          load_f32<DPL>(po + ((r0 + static_cast<int64_t>(c0 + j) * tpt) * h + head) * DH + lane * DPL, x[j]);
+#pragma unroll
+      for (int j = 0; j < BATCH; ++j) {
+        const float w = __shfl_sync(0xffffffffu, w_lane, (c0 + j) & 31);
+        if (c0 + j < nc) {
+#pragma unroll
+          for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, x[j][i], acc[i]);
+        }
+      }
+    }
+  } else {
+    float M = kNegInf;
+    for (int c = lane; c < nc; c += 32) M = fmaxf(M, plse[(r0 + static_cast<int64_t>(c) * tpt) * h + head]);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    for (int c = 0; c < nc; ++c) {
+      const int64_t row = r0 + static_cast<int64_t>(c) * tpt;
+      const float lse = plse[row * h + head];
+      const float w = (lse == kNegInf || M == kNegInf) ? 0.f : fast_exp2(lse - M);
+      lw += w;
+      float x[DPL];
+      load_f32<DPL>(po + (row * h + head) * DH + lane * DPL, x);
+#pragma unroll
+      for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, x[i], acc[i]);
+    }
   }
   const float inv = lw > 0.f ? 1.f / lw : 0.f;
 #pragma unroll
