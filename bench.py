@@ -684,20 +684,25 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
             dst.copy_(src.cpu())
     dev_views = [views(dev_in, l) for l in range(layers)]
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]
-    backend = sharding.KVHeadShardedBackend(transport=args.transport) if world > 1 else mlb.B200Backend()
     p2p_ring = world > 1 and args.transport == "p2p"
-    # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer, read back
-    # in 4 shrinking chunks (a side-stream copy per layer costs ~60 us of host time: 32 per step made the
-    # step host-bound)
+    # p2p: one gathered-output slot per layer and step, two steps' worth, so a step's outputs are read back
+    # in chunks and no peer rewrites a slot before its read-back (two steps later, after a step-end join)
+    backend = (sharding.KVHeadShardedBackend(transport=args.transport, slots=2 * layers if p2p_ring else 2)
+               if world > 1 else mlb.B200Backend())
+    # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer; p2p: the
+    # step's run of slots; either way read back in 4 shrinking chunks (a side-stream copy per layer costs
+    # ~60 us of host time: 32 per step made the step host-bound)
     direct = world == 1
+    o_edges = sorted({0, layers} | {b for b in (layers // 2, layers - 4, layers - 1) if 0 < b < layers})
+    o_chunks = list(zip(o_edges[:-1], o_edges[1:]))
+    o_last = {hi - 1: (lo, hi) for lo, hi in o_chunks}
     if direct:
         dev_out = torch.empty((layers, *q.shape), dtype=q.dtype, device=dev)
         host_out = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
-        o_edges = sorted({0, layers} | {b for b in (layers // 2, layers - 4, layers - 1) if 0 < b < layers})
-        o_chunks = list(zip(o_edges[:-1], o_edges[1:]))
-        o_last = {hi - 1: (lo, hi) for lo, hi in o_chunks}
         targets = [mlb.ops.out_targets([dev_out[l].data_ptr()], 0, q.shape[1] * q.shape[2], q.shape[2])
                    for l in range(layers)]
+    host_ring = None  # p2p: pinned bytes for one step's slots (allocated once the slots exist)
+    state = {"step": 0}
     compute = torch.cuda.current_stream(dev)
     loader, copier = torch.cuda.Stream(dev), torch.cuda.Stream(dev)  # H2D of inputs, D2H of outputs
     # chunk boundaries: layer 0's inputs alone, then chunks that land while the layers before them compute
@@ -724,12 +729,26 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
             for c, (lo, hi) in enumerate(chunks):  # then the q/k/v rows in a few growing chunks
                 dev_in[lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer], non_blocking=True)
                 loaded[c].record(loader)
+        nonlocal host_ring
+        base = (state["step"] % 2) * layers  # this step's first slot of the p2p ring
+        state["step"] += 1
         for l in range(layers):
             if l in chunk_of:
                 compute.wait_event(loaded[chunk_of[l]])
-            if p2p_ring and l >= 2:  # a p2p-gathered output is a 2-slot ring view: read back before reuse
-                compute.wait_event(done[l - 2])
             qd, kd, vd = dev_views[l]
+            if p2p_ring:
+                backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot base + l
+                if l in o_last:  # a chunk of layers is complete: read its slots back on the side stream
+                    lo, hi = o_last[l]
+                    peers = backend.peers
+                    if host_ring is None:
+                        host_ring = torch.empty(layers * peers.slot_bytes, dtype=torch.uint8).pin_memory()
+                    ready[l].record(compute)
+                    copier.wait_event(ready[l])
+                    with torch.cuda.stream(copier):
+                        host_ring[lo * peers.slot_bytes:hi * peers.slot_bytes].copy_(
+                            peers.slot_bytes_view(base + lo, base + hi), non_blocking=True)
+                continue
             if direct:
                 backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[l])
                 if l in o_last:  # a chunk of layers is complete: read it back on the side stream
@@ -739,14 +758,13 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
                     with torch.cuda.stream(copier):
                         host_out[lo:hi].copy_(dev_out[lo:hi], non_blocking=True)
                 continue
-            out = backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)
+            out = backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh gathered tensor
             ready[l].record(compute)
             copier.wait_event(ready[l])
             with torch.cuda.stream(copier):
                 outs[l].copy_(out, non_blocking=True)
                 done[l].record(copier)
-            if not p2p_ring:  # a fresh tensor from torch's allocator: keep it alive until the copy ran
-                out.record_stream(copier)
+            out.record_stream(copier)  # from torch's allocator: keep it alive until the copy ran
         compute.wait_stream(copier)
         step_done.record(compute)
 
@@ -772,18 +790,18 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         torch.cuda.synchronize()
         windows.append(max_over_ranks(s.elapsed_time(e), world, dev) / args.steps)
     ms = statistics.median(windows)
+    d2h = layers * (backend.peers.slot_bytes if p2p_ring else q.numel() * q.element_size())  # bytes copied
     if world > 1:
         backend.close()
     total = kv_bytes(ctx, HKV) * layers
     meta_bytes = _meta_bytes(mlb, seqs)
     h2d = layers * per_layer + meta_bytes
-    d2h = layers * q.numel() * q.element_size()
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "window_ms_per_step": [round(w, 4) for w in windows],
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "path": (f"KVHeadShardedBackend(transport={args.transport!r})" if world > 1 else "B200Backend")
                     + ".forward per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "
-                      "D2H of the outputs " + ("in 4 chunks" if direct else "per layer")}
+                      "D2H of the outputs " + ("in 4 chunks" if direct or p2p_ring else "per layer")}
 
 
 def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:

@@ -114,6 +114,13 @@ class PeerOutputs:
     def self_dest(self) -> int:
         return self.rank
 
+    def slot_bytes_view(self, lo: int, hi: int) -> torch.Tensor:
+        """This rank's slots [lo, hi) as one contiguous uint8 tensor (slot s at (s - lo) * slot_bytes): a
+        run of outputs can be read back with one copy."""
+        if not 0 <= lo <= hi <= self.slots:
+            raise ValueError(f"PeerOutputs: slots [{lo}, {hi}) outside [0, {self.slots})")
+        return self._bytes[lo * self.slot_bytes: hi * self.slot_bytes]
+
     def output(self, slot: int, num_tokens: int) -> torch.Tensor:
         if num_tokens > self.capacity:
             raise ValueError(f"PeerOutputs: {num_tokens} tokens > capacity {self.capacity}")
@@ -154,13 +161,14 @@ class KVHeadShardedBackend(AttentionBackend):
     step, keeps this rank's heads, runs on this rank's pools and returns the full [N, H, Dh] output.
 
     transport "p2p" (B200Backend inner, CUDA tensors): the output rows go straight into every rank's
-    `PeerOutputs` slot; the returned tensor is a view of that slot, valid until the forward after next.
+    `PeerOutputs` slot; the returned tensor is a view of that slot, valid until `slots` - 1 more forwards
+    have run (forwards rotate through the slots; 2 by default).
     transport "nccl": a fresh tensor from an NCCL (or gloo) all-gather."""
 
     name = "b200_kv_sharded"
 
     def __init__(self, inner: AttentionBackend | None = None, group: dist.ProcessGroup | None = None,
-                 transport: str = "nccl") -> None:
+                 transport: str = "nccl", slots: int = 2) -> None:
         if inner is None:
             from .attention.backend import B200Backend
 
@@ -172,6 +180,9 @@ class KVHeadShardedBackend(AttentionBackend):
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.transport = transport
+        if slots < 2:
+            raise ValueError(f"slots must be >= 2, got {slots}")
+        self.slots = slots
         self.peers: PeerOutputs | None = None
         self._slot = 0
 
@@ -199,7 +210,7 @@ class KVHeadShardedBackend(AttentionBackend):
             if p is not None:
                 p.close()
             self.peers = p = PeerOutputs(1 << max(6, math.ceil(math.log2(max(n, 1)))), h, dh, q.dtype, q.device,
-                                         group=self.group)
+                                         slots=self.slots, group=self.group)
             self._slot = 0
         slot, self._slot = self._slot, (self._slot + 1) % p.slots
         self.inner.forward(q[:, qs], k[:, ks], v[:, ks], k_cache, v_cache, meta, peer_gather=(p, slot, qs.start))
