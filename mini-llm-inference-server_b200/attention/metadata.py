@@ -151,9 +151,12 @@ def _written_private(written: np.ndarray, used_ids: np.ndarray) -> bool:
     if written.size == 0:
         return True
     lo, hi = int(used_ids.min()), int(used_ids.max())
-    if lo < 0 or hi >= 1 << 26:  # an invalid id, or ids too large to count densely: keep the separate append
+    if lo < 0:  # an invalid id: keep the separate append (it flags the slot)
         return False
-    return bool((np.bincount(used_ids)[written] == 1).all())
+    if hi < 4 * used_ids.size + (1 << 16):  # dense counters stay small next to the ids themselves
+        return bool((np.bincount(used_ids)[written] == 1).all())
+    ids, counts = np.unique(used_ids, return_counts=True)  # sparse ids: count by sorting
+    return bool((counts[np.searchsorted(ids, written)] == 1).all())
 
 
 def _to_device(a: np.ndarray, device: torch.device) -> torch.Tensor:

@@ -68,6 +68,8 @@ def test_append_private_flag(mlb):
     assert not build([S(5, 1, [4, 4])])  # the same block twice in one table
     assert not build([S(1, 1, [-1])])  # an invalid id: no fusion, the separate append flags it
     assert build([S(3, 0, [7])])  # nothing written
+    big = 1 << 40  # sparse ids far past the dense-count range
+    assert build([S(2, 1, [big]), S(3, 1, [big + 1])]) and not build([S(2, 1, [big]), S(3, 1, [big])])
     # a block beyond a sequence's context pages is not read by it
     assert build([S(2, 1, [7]), S(4, 0, [6, 1, 7])])
 
