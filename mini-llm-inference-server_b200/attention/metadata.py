@@ -108,14 +108,13 @@ class AttentionMetadata:
         table32 = np.zeros((s, width), dtype=np.int32)
         table32[mask] = ids  # truncated to int32 like Tensor.to(torch.int32)
 
-        if device.type == "cuda":
+        if device.type == "cuda" and s:
             from .. import ops
 
             upload = _to_device(np.concatenate([ids, ids_indptr, starts, ends, kv_indptr, last_len]), device)
             d64 = torch.empty(2 * n + s * width + s, dtype=torch.int64, device=device)
             d32 = torch.empty(s * width + 4 * s + 2 + int(kv_indptr[-1]), dtype=torch.int32, device=device)
-            if s:
-                ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
+            ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
         else:
             table = np.zeros((s, width), dtype=np.int64)
             table[mask] = ids

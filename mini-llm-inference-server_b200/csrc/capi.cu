@@ -551,11 +551,13 @@ int attention_call(const void* q, int64_t q_stride_tok, int64_t q_stride_head, c
     cudaError_t e = side_stream(&ss);
     if (e == cudaSuccess) e = cudaEventRecord(ss->fork, st);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(ss->stream, ss->fork, 0);
-    if (e == cudaSuccess) e = launch_shared(ss->stream);
-    if (e == cudaSuccess) e = mlb::launch_paged_attention(a, dtype, head_dim, num_units, st);
-    if (e == cudaSuccess) e = cudaEventRecord(ss->join, ss->stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, ss->join, 0);
-    return cuda_status(e, "paged_attention launch (shared-prefix kernel on a side stream)");
+    if (e != cudaSuccess) return cuda_status(e, "paged_attention: side stream fork");
+    cudaError_t el = launch_shared(ss->stream);
+    if (el == cudaSuccess) el = mlb::launch_paged_attention(a, dtype, head_dim, num_units, st);
+    // joined whatever happened above, so a stream capture never ends with the side stream still forked
+    cudaError_t ej = cudaEventRecord(ss->join, ss->stream);
+    if (ej == cudaSuccess) ej = cudaStreamWaitEvent(st, ss->join, 0);
+    return cuda_status(el != cudaSuccess ? el : ej, "paged_attention launch (shared-prefix kernel on a side stream)");
   }
   if (num_shared_units > 0) {
     const int rc = cuda_status(launch_shared(st), "shared-prefix attention launch");

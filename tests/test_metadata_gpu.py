@@ -56,11 +56,12 @@ def test_device_build_matches_numpy_on_random_steps(mlb, cuda, seed):
 
 def test_device_build_edge_cases(mlb, cuda):
     S = mlb.SeqStep
+    _same(mlb, [], 16, cuda)  # no rows
     _same(mlb, [S(0, 0, [])], 16, cuda)  # an empty row
     _same(mlb, [S(3, 1, [7]), S(0, 0, []), S(0, 5, [2, 9])], 4, cuda)
     big = [(1 << 31) + 5, (1 << 33) + 1, 3]  # ids past int32: the int32 views truncate as Tensor.to does
     m = _same(mlb, [S(40, 1, big)], 16, cuda)
-    assert m.block_tables.tolist() == [big] and not m.append_private
+    assert m.block_tables.tolist() == [big] and m.append_private  # block 3, written, occurs once
     assert m.slot_mapping.tolist() == [3 * 16 + 8]
     seqs = [S(c, 1, list(range(i * 600, i * 600 + -(-(c + 1) // 16)))) for i, c in enumerate(range(0, 9000, 37))]
     _same(mlb, seqs, 16, cuda)  # 244 rows, ragged tables up to 563 wide
