@@ -383,6 +383,7 @@ def run_ours(args) -> None:
     mlb._lib.lib().mlb_set_programmatic_launch(0 if args.no_pdl else 1)
     mlb._lib.lib().mlb_set_tensor_core_prefix(0 if args.no_tc_prefix else 1)
     mlb._lib.lib().mlb_set_concurrent_prefix(0 if args.serial_prefix else 1)
+    mlb._lib.lib().mlb_set_persistent_attention(1 if args.persistent else 0)
 
     weak = world > 1 and args.config == 2 and args.scaling == "weak"
     if args.config == 2:
@@ -419,9 +420,9 @@ def run_ours(args) -> None:
         seqsteps(wl.append_rows), BS, dev)
     if args.no_query_tiles:  # every row on 8-column work units (no host tables: no query tiles, no cascade)
         plan = ops.plan_attention(meta_att.query_start_loc, meta_att.seq_lens, meta_att.block_tables_i32.shape[1],
-                                  h_l, hkv_l, dev)
+                                  h_l, hkv_l, dev, pages_per_unit=args.pages_per_unit)
     else:
-        plan = mlb.B200Backend().plan(meta_att, h_l, hkv_l, dev)
+        plan = mlb.B200Backend(pages_per_unit=args.pages_per_unit).plan(meta_att, h_l, hkv_l, dev)
     ws = ops.Workspace()
     out_l = torch.empty(n_q, h_l, DH, device=dev, dtype=torch.bfloat16)
     p2p = world > 1 and args.transport == "p2p"
@@ -614,6 +615,7 @@ def run_ours(args) -> None:
                        "append": "fused into the attention launch" if fused else "separate K1 launch",
                        "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
                        "shared_prefix_beside_per_sequence_kernel": not args.serial_prefix,
+                       "persistent_attention": bool(args.persistent), "pages_per_unit": args.pages_per_unit,
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
@@ -687,8 +689,10 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     p2p_ring = world > 1 and args.transport == "p2p"
     # p2p: one gathered-output slot per layer and step, two steps' worth, so a step's outputs are read back
     # in chunks and no peer rewrites a slot before its read-back (two steps later, after a step-end join)
-    backend = (sharding.KVHeadShardedBackend(transport=args.transport, slots=2 * layers if p2p_ring else 2)
-               if world > 1 else mlb.B200Backend())
+    inner_backend = mlb.B200Backend(pages_per_unit=args.pages_per_unit)
+    backend = (sharding.KVHeadShardedBackend(inner_backend, transport=args.transport,
+                                             slots=2 * layers if p2p_ring else 2)
+               if world > 1 else inner_backend)
     # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer; p2p: the
     # step's run of slots; either way read back in 4 shrinking chunks (a side-stream copy per layer costs
     # ~60 us of host time: 32 per step made the step host-bound)
@@ -865,6 +869,9 @@ def main() -> None:
                     help="plan without host tables: every row on the decode kernel's 8-column units")
     ap.add_argument("--no-fused-append", action="store_true",
                     help="launch the append (K1) before attention even when it could ride in the attention launch")
+    ap.add_argument("--persistent", action="store_true",
+                    help="per-sequence units on resident CTAs fed by a work queue (mlb_set_persistent_attention)")
+    ap.add_argument("--pages-per-unit", type=int, default=0, help="split-K unit size in pages (0: the planner's)")
     ap.add_argument("--serial-prefix", action="store_true",
                     help="run the shared-prefix kernel before the per-sequence kernel instead of beside it")
     ap.add_argument("--no-tc-prefix", action="store_true",

@@ -216,17 +216,19 @@ namespace {
 std::atomic<int> g_programmatic_launch{1};
 std::atomic<int> g_tensor_core_prefix{1};
 std::atomic<int> g_concurrent_prefix{1};
+std::atomic<int> g_persistent_attention{0};
 }  // namespace
 bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
 bool tensor_core_prefix() { return g_tensor_core_prefix.load(std::memory_order_relaxed) != 0; }
 bool concurrent_prefix() { return g_concurrent_prefix.load(std::memory_order_relaxed) != 0; }
+bool persistent_attention() { return g_persistent_attention.load(std::memory_order_relaxed) != 0; }
 }  // namespace mlb
 
 extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 7; }
+int mlb_abi_version(void) { return 8; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -238,6 +240,10 @@ int mlb_set_tensor_core_prefix(int enable) {
 
 int mlb_set_concurrent_prefix(int enable) {
   return mlb::g_concurrent_prefix.exchange(enable ? 1 : 0, std::memory_order_relaxed);
+}
+
+int mlb_set_persistent_attention(int enable) {
+  return mlb::g_persistent_attention.exchange(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
