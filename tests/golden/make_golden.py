@@ -27,7 +27,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE))
-sys.path.insert(0, os.environ.get("MINILLM_REF_SRC", "/root/reference/src"))
+if "MINILLM_REF_SRC" not in os.environ:
+    sys.exit("set MINILLM_REF_SRC to the reference's src/ directory (see the docstring)")
+sys.path.insert(0, os.environ["MINILLM_REF_SRC"])
 
 import cases  # noqa: E402
 from minillm.attention.metadata import AttentionMetadata, SeqStep  # noqa: E402
