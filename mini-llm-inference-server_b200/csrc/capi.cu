@@ -59,7 +59,7 @@ bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a)
 
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
 constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
-constexpr int kWaveTenths = 15;      // the auto split aims for 1.5 waves of resident CTAs (measured best)
+constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best)
 constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
