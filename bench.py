@@ -667,8 +667,18 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     backend's forward once its chunk is in, and a device-to-host copy of its output on a copier stream
     (layer l's read-back overlaps layer l + 1's attention); the step ends when the last output is on the
     host.  One GPU: the outputs go into one step-wide device buffer (forward's out_targets) and come back
-    in 4 chunks."""
+    in 4 chunks.  Several GPUs: each rank holds and uploads only its own heads of q/k/v (as a column-parallel
+    QKV projection leaves them) and calls KVHeadShardedBackend.forward_local; it reads back its own heads of
+    the gathered output, so the job reads the whole result back once."""
     layers = len(k_pools)
+    rank = 0
+    if world > 1:
+        import torch.distributed as dist
+
+        rank = dist.get_rank()
+        qs, ks = sharding.head_range(rank, world, q.shape[1]), sharding.head_range(rank, world, k.shape[1])
+        q, k, v = q[:, qs].contiguous(), k[:, ks].contiguous(), v[:, ks].contiguous()
+    n_rows, h_full = q.shape[0], q.shape[1] * world
     sizes = [t.numel() * t.element_size() for t in (q, k, v)]
     per_layer = sum(sizes)
     host_in = torch.empty(layers * per_layer, dtype=torch.uint8).pin_memory()
@@ -685,7 +695,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         for dst, src in zip(views(host_in, l), (q, k, v)):
             dst.copy_(src.cpu())
     dev_views = [views(dev_in, l) for l in range(layers)]
-    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]
+    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]  # this rank's heads
     p2p_ring = world > 1 and args.transport == "p2p"
     # p2p: one gathered-output slot per layer and step, two steps' worth, so a step's outputs are read back
     # in chunks and no peer rewrites a slot before its read-back (two steps later, after a step-end join)
@@ -720,7 +730,8 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     step_done.record(compute)
 
     inner = backend.inner if world > 1 else backend
-    h_l, hkv_l = q.shape[1] // world, k_pools[0].shape[2]
+    h_l, hkv_l = q.shape[1], k_pools[0].shape[2]
+    own = slice(rank * h_l, (rank + 1) * h_l)  # this rank's query heads in the gathered output
 
     def step():
         loader.wait_event(step_done)  # the previous step has read every layer's inputs, metadata and plan
@@ -741,17 +752,19 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
                 compute.wait_event(loaded[chunk_of[l]])
             qd, kd, vd = dev_views[l]
             if p2p_ring:
-                backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot base + l
-                if l in o_last:  # a chunk of layers is complete: read its slots back on the side stream
+                backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot base + l
+                if l in o_last:  # a chunk of layers is complete: read this rank's heads back on the side stream
                     lo, hi = o_last[l]
                     peers = backend.peers
                     if host_ring is None:
-                        host_ring = torch.empty(layers * peers.slot_bytes, dtype=torch.uint8).pin_memory()
+                        host_ring = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
                     ready[l].record(compute)
                     copier.wait_event(ready[l])
                     with torch.cuda.stream(copier):
-                        host_ring[lo * peers.slot_bytes:hi * peers.slot_bytes].copy_(
-                            peers.slot_bytes_view(base + lo, base + hi), non_blocking=True)
+                        nbytes = n_rows * h_full * q.shape[2] * q.element_size()  # a slot's rows (no padding)
+                        rows = peers.slot_bytes_view(base + lo, base + hi).view(hi - lo, peers.slot_bytes)
+                        rows = rows[:, :nbytes].view(q.dtype).view(hi - lo, n_rows, h_full, q.shape[2])[:, :, own]
+                        host_ring[lo:hi].copy_(rows, non_blocking=True)
                 continue
             if direct:
                 backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[l])
@@ -762,11 +775,11 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
                     with torch.cuda.stream(copier):
                         host_out[lo:hi].copy_(dev_out[lo:hi], non_blocking=True)
                 continue
-            out = backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh gathered tensor
+            out = backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh gathered one
             ready[l].record(compute)
             copier.wait_event(ready[l])
             with torch.cuda.stream(copier):
-                outs[l].copy_(out, non_blocking=True)
+                outs[l].copy_(out[:, own], non_blocking=True)
                 done[l].record(copier)
             out.record_stream(copier)  # from torch's allocator: keep it alive until the copy ran
         compute.wait_stream(copier)
@@ -794,7 +807,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         torch.cuda.synchronize()
         windows.append(max_over_ranks(s.elapsed_time(e), world, dev) / args.steps)
     ms = statistics.median(windows)
-    d2h = layers * (backend.peers.slot_bytes if p2p_ring else q.numel() * q.element_size())  # bytes copied
+    d2h = layers * q.numel() * q.element_size()  # bytes read back (this rank's heads on several GPUs)
     if world > 1:
         backend.close()
     total = kv_bytes(ctx, HKV) * layers
@@ -803,9 +816,11 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "window_ms_per_step": [round(w, 4) for w in windows],
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "path": (f"KVHeadShardedBackend(transport={args.transport!r})" if world > 1 else "B200Backend")
-                    + ".forward per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "
-                      "D2H of the outputs " + ("in 4 chunks" if direct or p2p_ring else "per layer")}
+            "path": (f"KVHeadShardedBackend(transport={args.transport!r}).forward_local" if world > 1
+                     else "B200Backend.forward")
+                    + " per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "
+                      "D2H of the outputs " + ("in 4 chunks" if direct or p2p_ring else "per layer")
+                    + ("; each rank uploads and reads back its own heads" if world > 1 else "")}
 
 
 def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:

@@ -202,8 +202,26 @@ class KVHeadShardedBackend(AttentionBackend):
         local = self.inner.forward(q[:, qs], k[:, ks], v[:, ks], k_cache, v_cache, meta)  # [N, H/n, Dh]
         return self._gather(local, dim_heads=1)
 
-    def _forward_p2p(self, q, k, v, k_cache, v_cache, meta, qs, ks):
-        n, h, dh = q.shape
+    def forward_local(self, q_l, k_l, v_l, k_cache, v_cache, meta):
+        """`forward` for a rank that holds only its own heads of the step's rows, as a column-parallel QKV
+        projection leaves them: q_l [N, H/n, Dh] (query heads [r H/n, (r+1) H/n)), k_l / v_l [N, Hkv/n, Dh].
+        Returns the same full [N, H, Dh] output as `forward` on the full tensors, without any rank holding
+        (or uploading) the other ranks' heads."""
+        h = q_l.shape[1] * self.world
+        qs = head_range(self.rank, self.world, h)
+        ks = head_range(self.rank, self.world, k_l.shape[1] * self.world)
+        if k_cache.shape[2] != k_l.shape[1]:
+            raise ValueError(f"rank {self.rank}: pools hold {k_cache.shape[2]} KV heads, k_l {k_l.shape[1]}")
+        if self.transport == "p2p" and self.world > 1:
+            return self._forward_p2p(q_l, k_l, v_l, k_cache, v_cache, meta, qs, ks, local=True)
+        local = self.inner.forward(q_l, k_l, v_l, k_cache, v_cache, meta)
+        return self._gather(local, dim_heads=1)
+
+    def _forward_p2p(self, q, k, v, k_cache, v_cache, meta, qs, ks, local=False):
+        n, dh = q.shape[0], q.shape[2]
+        h = q.shape[1] * self.world if local else q.shape[1]
+        if not local:
+            q, k, v = q[:, qs], k[:, ks], v[:, ks]
         p = self.peers
         if p is None or n > p.capacity or (p.num_heads, p.head_dim, p.dtype) != (h, dh, q.dtype):
             # collective (every rank sees the same step shape): grow to a power of two of tokens
@@ -213,7 +231,7 @@ class KVHeadShardedBackend(AttentionBackend):
                                          slots=self.slots, group=self.group)
             self._slot = 0
         slot, self._slot = self._slot, (self._slot + 1) % p.slots
-        self.inner.forward(q[:, qs], k[:, ks], v[:, ks], k_cache, v_cache, meta, peer_gather=(p, slot, qs.start))
+        self.inner.forward(q, k, v, k_cache, v_cache, meta, peer_gather=(p, slot, qs.start))
         return p.output(slot, n)
 
     def close(self) -> None:

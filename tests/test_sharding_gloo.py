@@ -1,6 +1,7 @@
 """KV-head sharding on CPU ranks (torch.distributed gloo, world size 2 and 4): each rank holds only its KV
 heads' pools, attends with an oracle-backed inner backend, and the all-gathered output equals the
-unsharded oracle.  Also: a rank that dies before the collective makes the others fail fast (host-side
+unsharded oracle, from the full rows (`forward`) and from each rank's own heads (`forward_local`).  Also: a
+rank that dies before the collective makes the others fail fast (host-side
 failure injection; no GPU involved)."""
 
 from __future__ import annotations
@@ -61,6 +62,12 @@ def _worker(rank: int, world: int, port: int, mode: str, result_path: str) -> No
         out = backend.forward(case.q, case.k, case.v, k_pool, v_pool, meta)
         if rank == 0:
             torch.save(out, result_path)
+        # the same step from this rank's own heads only (as a column-parallel QKV projection leaves them)
+        qs = sharding.head_range(rank, world, case.h)
+        k_pool_l = case.k_pool[:, :, ks].contiguous()
+        v_pool_l = case.v_pool[:, :, ks].contiguous()
+        out_l = backend.forward_local(case.q[:, qs], case.k[:, ks], case.v[:, ks], k_pool_l, v_pool_l, meta)
+        assert torch.equal(out_l, out)
         # this rank's slice of the pools was written exactly like the unsharded write
         full_k = case.k_pool.clone()
         oracle.write_kv(full_k, case.v_pool.clone(), meta.slot_mapping, case.k, case.v)
