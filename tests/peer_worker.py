@@ -1,6 +1,7 @@
 """One rank of the two-GPU check in test_peer_gpu.py (run under torchrun): KV-head-sharded forward with the
-p2p output gather equals the NCCL all-gather bit for bit, over several forwards (both slots reused), and
-matches the fp32 oracle within the bf16 tolerance."""
+p2p output gather equals the NCCL all-gather bit for bit, over several forwards (both slots reused), from the
+full rows (`forward`) and from each rank's own heads (`forward_local`), and matches the fp32 oracle within
+the bf16 tolerance."""
 
 from __future__ import annotations
 
@@ -36,11 +37,18 @@ def main() -> None:
         ks = sharding.head_range(rank, world, case.hkv)
         pools = [t[name][:, :, ks].contiguous() for name in ("k_pool", "v_pool", "k_pool", "v_pool")]
         expected = oracle_forward(case, dtype)[0]
+        qs = sharding.head_range(rank, world, case.h)
         for _ in range(3):  # slots 0, 1, 0 ...
             got = p2p.forward(t["q"], t["k"], t["v"], pools[0], pools[1], meta).clone()
             want = nccl.forward(t["q"], t["k"], t["v"], pools[2], pools[3], meta)
             assert torch.equal(got, want), f"rank {rank}: p2p gather differs from NCCL ({case.name})"
             assert_close(got, expected, dtype)
+            # the same step from this rank's own heads only (forward_local), both transports
+            loc = p2p.forward_local(t["q"][:, qs].contiguous(), t["k"][:, ks].contiguous(),
+                                    t["v"][:, ks].contiguous(), pools[0], pools[1], meta).clone()
+            assert torch.equal(loc, want), f"rank {rank}: p2p forward_local differs ({case.name})"
+            loc = nccl.forward_local(t["q"][:, qs], t["k"][:, ks], t["v"][:, ks], pools[2], pools[3], meta)
+            assert torch.equal(loc, want), f"rank {rank}: NCCL forward_local differs ({case.name})"
     p2p.peers.raise_errors()
     p2p.close()
     dist.barrier()
