@@ -450,15 +450,34 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const float nbase = m_used == -__builtin_huge_valf() ? 0.f : -m_used;
       const float sl2 = a.sl2;
       uint32_t pk[kTcTileTokens / 2];
-      float s8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent sum chains
+      // p = 2^(s * scale * log2 e - m): the scale-and-subtract and the row sums run on packed pairs of fp32
+      // (fma.rn.f32x2 / add.f32x2, each lane rounded as fmaf / fadd), halving those instructions; the
+      // exponentials stay on the special-function unit.  4 pair sums = 8 independent sum chains.
+      uint64_t sl2v, nbv, s4[4];
+      asm("mov.b64 %0, {%1, %1};" : "=l"(sl2v) : "f"(sl2));
+      asm("mov.b64 %0, {%1, %1};" : "=l"(nbv) : "f"(nbase));
 #pragma unroll
-      for (int k = 0; k < kTcTileTokens; k += 2) {  // p = 2^(s * scale * log2 e - m): one FFMA + EX2 per key
-        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[k]), sl2, nbase));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[k + 1]), sl2, nbase));
-        s8[(k / 2) % 8] += p0 + p1;
+      for (int i = 0; i < 4; ++i) s4[i] = 0ull;  // +0.0f in both halves
+#pragma unroll
+      for (int k = 0; k < kTcTileTokens; k += 2) {
+        uint64_t sv, xv, pv;
+        asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "r"(sr[k]), "r"(sr[k + 1]));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(xv) : "l"(sv), "l"(sl2v), "l"(nbv));
+        float x0, x1;
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(x0), "=f"(x1) : "l"(xv));
+        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+        asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "f"(p0), "f"(p1));
+        asm("add.f32x2 %0, %0, %1;" : "+l"(s4[(k / 2) % 4]) : "l"(pv));
         pk[k / 2] = pack2<DT>(p0, p1);
       }
-      l += ((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7]));
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float lo, hi;
+        asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(s4[i]));
+        sum += lo + hi;
+      }
+      l += sum;
       tmem_st32(tmem + lanes + col_p(b), pk);
       tmem_st32(tmem + lanes + col_p(b) + 32, pk + 32);
       tmem_wait_st();
