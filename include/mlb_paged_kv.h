@@ -262,7 +262,9 @@ MLB_API int mlb_paged_attention_append(const void* q, int64_t q_stride_tok, int6
  * Split-K reduction: for every token whose reduce_chunks > 1, combine its rows
  * reduce_rows[t] + c * tokens_per_tile (c < reduce_chunks[t]) by their log-sum-exp weights and write
  * out[t] (or every out_targets destination).  Completes mlb_paged_attention; no reference counterpart
- * (the reference never splits).
+ * (the reference never splits).  Under programmatic launch the kernel reads reduce_rows / reduce_chunks
+ * before it waits for the kernel launched just before it on the stream (normally the attention launch):
+ * upload them before that launch, as the plan's other arrays, never from that kernel.
  */
 MLB_API int mlb_splitk_reduce(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
                       const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,

@@ -74,8 +74,11 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // Every kernel of this library begins with griddep_begin().  Launched with programmatic stream
 // serialisation (launch_k), a kernel's CTAs may become resident while its predecessor on the stream is
 // still finishing; griddepcontrol.wait holds them until that grid has completed and its memory is
-// visible, so no input is read early.  Then launch_dependents lets the next kernel's CTAs do the same, so
-// each launch's latency hides behind the tail of the one before.  Launched normally, both are no-ops.
+// visible, so no input is read early (the split-K reductions' plan arrays, uploaded before the attention
+// launch they follow, are the one exception).  Then launch_dependents lets the next kernel's CTAs do the
+// same, so each launch's latency hides behind the tail of the one before.  Launched normally, both are
+// no-ops.  Every kernel triggers only after its own wait, so when a kernel's CTAs run, every grid two or
+// more launches before it on the stream has completed.
 __device__ __forceinline__ void griddep_begin() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

@@ -958,8 +958,12 @@ __device__ __forceinline__ void reduce_token_head(const float* po, const float* 
   for (int i = 0; i < DPL; ++i) acc[i] = 0.f;
   float lw = 0.f;
   if (nc <= 32) {
-    // lane c holds piece c's log2-sum-exp (one round trip for all pieces); max, weights and their sum by
-    // shuffles; the pieces' rows then load BATCH at a time, independent of each other
+    // the first BATCH pieces' rows and lane c's log2-sum-exp of piece c load together (one round trip for
+    // most tokens); max, weights and their sum by shuffles; further pieces then load BATCH at a time
+    float x0[BATCH][DPL];
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j)
+      if (j < nc) load_f32<DPL>(po + ((r0 + static_cast<int64_t>(j) * tpt) * h + head) * DH + lane * DPL, x0[j]);
     const float lse = lane < nc ? plse[(r0 + static_cast<int64_t>(lane) * tpt) * h + head] : kNegInf;
     float M = lse;
 #pragma unroll
@@ -968,7 +972,15 @@ __device__ __forceinline__ void reduce_token_head(const float* po, const float* 
     lw = w_lane;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) lw += __shfl_xor_sync(0xffffffffu, lw, off);
-    for (int c0 = 0; c0 < nc; c0 += BATCH) {
+#pragma unroll
+    for (int j = 0; j < BATCH; ++j) {
+      const float w = __shfl_sync(0xffffffffu, w_lane, j);
+      if (j < nc) {
+#pragma unroll
+        for (int i = 0; i < DPL; ++i) acc[i] = fmaf(w, x0[j][i], acc[i]);
+      }
+    }
+    for (int c0 = BATCH; c0 < nc; c0 += BATCH) {
       float x[BATCH][DPL];
 #pragma unroll
       for (int j = 0; j < BATCH; ++j)
@@ -1011,16 +1023,19 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* po, con
                                                             int64_t ntok, int h, const mlb_out_targets out,
                                                             int out_vec) {
   constexpr int DPL = DH / 32;
-  griddep_begin();
   const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (wid >= ntok * h) return;
-  const int64_t tok = wid / h;
+  const bool live = wid < ntok * h;
+  const int64_t tok = live ? wid / h : 0;
   const int head = static_cast<int>(wid % h);
-  const int nc = rchunks[tok];
+  // The plan's reduce arrays are uploaded before the attention launch and not written by it: read them
+  // before the wait, while the attention grid drains (one round trip fewer after it)
+  const int nc = live ? rchunks[tok] : 0;
+  const int r0 = live ? rrows[tok] : 0;
+  griddep_begin();
   if (nc <= 1) return;
   float acc[DPL];
-  reduce_token_head<DH>(po, plse, rrows[tok], nc, tpt, h, head, lane, acc);
+  reduce_token_head<DH>(po, plse, r0, nc, tpt, h, head, lane, acc);
   store_out_n<OUT_DT, DPL>(out, out_vec != 0, tok, head, lane * DPL, acc);
 }
 
@@ -1036,16 +1051,18 @@ __global__ void __launch_bounds__(256) splitk_reduce_gather_kernel(const float* 
                                                                    const mlb_out_targets out, int out_vec,
                                                                    int self) {
   constexpr int DPL = DH / 32;
-  griddep_begin();
   const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (wid >= ntok * h) return;
-  const int64_t tok = wid / h;
+  const bool live = wid < ntok * h;
+  const int64_t tok = live ? wid / h : 0;
   const int head = static_cast<int>(wid % h);
-  const int nc = rchunks ? rchunks[tok] : 1;
+  const int nc = live && rchunks ? rchunks[tok] : 1;  // plan arrays: read before the wait, as above
+  const int r0 = live && rchunks ? rrows[tok] : 0;
+  griddep_begin();
+  if (!live) return;
   if (nc > 1) {
     float acc[DPL];
-    reduce_token_head<DH>(po, plse, rrows[tok], nc, tpt, h, head, lane, acc);
+    reduce_token_head<DH>(po, plse, r0, nc, tpt, h, head, lane, acc);
     store_out_n<OUT_DT, DPL>(out, out_vec != 0, tok, head, lane * DPL, acc);
   } else {
     copy_out_n<OUT_DT, DPL>(out, out_vec != 0, self, tok, head, lane * DPL);
