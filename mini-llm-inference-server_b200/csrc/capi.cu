@@ -62,6 +62,10 @@ constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (sh
 constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best)
 constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
+// SM time of one shared-prefix tile (128 query columns x 128 keys) in page-heads streamed by the per-sequence
+// kernel (head_dim 128; measured on config 4: ~2 us per tile per SM against ~0.1 us per 8 KB page-head)
+constexpr int kTilePageHeads = 19;
+constexpr int kMinSharedSmPct = 25;  // the shared-prefix kernel gets at least this share of the SMs
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
 constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages
 constexpr int kPrefillMinTokens = 16;   // multi-token rows this long go to tensor-core query tiles ...
@@ -318,30 +322,38 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   for (size_t g = 0; g < groups.size(); ++g)
     if (groups[g].tile == 0) seq_group[groups[g].seq] = static_cast<int>(g);
   const int per_cta = std::max(1, kSharedColumns / group_size);  // member rows per shared unit
+  for (const ShareSet& set : sets)
+    for (int s : set.seqs) groups[seq_group[s]].start = set.pages;  // members' own pages follow the prefix
+  int64_t rest = 0;  // pages left to the per-sequence kernel
+  for (const Group& g : groups) rest += g.pages - g.start;
+  // The shared-prefix kernel runs beside the per-sequence kernel, one CTA per SM: it gets the share of the
+  // SMs that balances the two kernels' estimated SM time (all of them when no per-sequence work is left)
+  int64_t tc_work = 0;
+  for (const ShareSet& set : sets)
+    tc_work += (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta * num_kv_heads *
+               ((set.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit) * kTilePageHeads;
+  const int64_t priv_work = rest * num_kv_heads;
+  const int64_t share_pct =
+      tc_work > 0 ? std::max<int64_t>(kMinSharedSmPct, 100 * tc_work / (tc_work + priv_work)) : 100;
   struct SetPlan {
     int pieces, per;
   };
   std::vector<SetPlan> set_plans;
   for (const ShareSet& set : sets) {
     const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
-    // as many pieces as keep every CTA in one wave, each a whole number of 8-page (128-key) tiles
-    const int64_t target = static_cast<int64_t>(num_sms) * kSharedCtasPerSm;
+    // as many pieces as keep every CTA in one wave of that share, each a whole number of 8-page (128-key)
+    // tiles
+    const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(num_sms) * kSharedCtasPerSm * share_pct / 100);
     int64_t pieces = std::max<int64_t>(1, target / (blocks * num_kv_heads));
     pieces = std::min<int64_t>(pieces, std::max(1, set.pages / kMinPagesPerUnit));
     int per = static_cast<int>((set.pages + pieces - 1) / pieces);
     per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;
     pieces = (set.pages + per - 1) / per;
     set_plans.push_back({static_cast<int>(pieces), per});
-    for (int s : set.seqs) {
-      Group& g = groups[seq_group[s]];
-      g.start = set.pages;
-      g.shared_pieces = static_cast<int>(pieces);
-    }
+    for (int s : set.seqs) groups[seq_group[s]].shared_pieces = static_cast<int>(pieces);
   }
 
   // ---- regular units over each group's pages [start, pages)
-  int64_t rest = 0;
-  for (const Group& g : groups) rest += g.pages - g.start;
   int64_t chunk = pages_per_unit;
   if (chunk <= 0) {
     const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaveTenths / 10;
