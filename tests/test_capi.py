@@ -278,6 +278,40 @@ def test_planner_finds_shared_prefixes(mlb):
     assert plain.num_shared_units == 0
 
 
+def _prefix_step(suffix_lo: int, suffix_hi: int, rows: int = 128, prefix_pages: int = 512, seed: int = 0):
+    """BASELINE config 4's shape: `rows` decode rows sharing `prefix_pages` full pages, own suffixes."""
+    r = random.Random(seed)
+    prefix = list(range(prefix_pages))
+    nxt, lens, tables = prefix_pages + 1, [], []
+    for _ in range(rows):
+        ctx = prefix_pages * 16 + r.randint(suffix_lo, suffix_hi) + 1
+        own = -(-ctx // 16) - prefix_pages
+        tables.append(prefix + list(range(nxt, nxt + own)))
+        nxt += own
+        lens.append(ctx)
+    host = np.zeros((rows, max(len(t) for t in tables)), dtype=np.int32)
+    for i, t in enumerate(tables):
+        host[i, :len(t)] = t
+    return list(range(rows + 1)), lens, host
+
+
+def test_planner_balances_shared_ctas_against_private_work(mlb):
+    """The shared-prefix kernel runs beside the per-sequence kernel, one CTA per SM: the planner gives it the
+    share of the SMs that balances the two (config 4: 3 pieces x 4 row blocks x 8 KV heads = 96 CTAs, the
+    measured best of 64 / 96 / 128), every SM when the rows have almost no pages of their own, and fewer as
+    their own pages grow.  Every shared page stays covered once per member whatever the piece count."""
+    ctas = {}
+    for name, lo, hi in (("config4", 64, 512), ("tiny", 0, 15), ("long", 512, 2048)):
+        qo, lens, host = _prefix_step(lo, hi)
+        p = mlb.plan_attention(qo, lens, host.shape[1], 32, 8, "cpu", num_sms=148, block_tables_host=host)
+        su = p.shared_host
+        ctas[name] = p.num_shared_units * 8
+        pieces = sorted({(int(x[2]), int(x[3])) for x in su})
+        assert pieces[0][0] == 0 and pieces[-1][1] == 512 and all(a[1] == b[0] for a, b in zip(pieces, pieces[1:]))
+        assert ctas[name] <= 148
+    assert ctas == {"config4": 96, "tiny": 128, "long": 32}
+
+
 @pytest.mark.parametrize("h,hkv", [(32, 8), (8, 8), (16, 2), (12, 4)])
 def test_planner_makes_query_tiles_for_prefill_rows(mlb, h, hkv):
     """With host tables, rows of >= 16 new tokens become kind-1 query tiles of 128 / group tokens over the
