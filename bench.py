@@ -682,7 +682,11 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     sizes = [t.numel() * t.element_size() for t in (q, k, v)]
     per_layer = sum(sizes)
     host_in = torch.empty(layers * per_layer, dtype=torch.uint8).pin_memory()
-    dev_in = torch.empty(layers * per_layer, dtype=torch.uint8, device=dev)
+    direct = world == 1
+    # one GPU: inputs, outputs and each step's metadata are double-buffered, so step n + 1's uploads (and its
+    # metadata and plan) run while step n computes; several GPUs: one set, each step waits for the last
+    nbuf = 2 if direct else 1
+    dev_in = [torch.empty(layers * per_layer, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
 
     def views(buf, l):
         out, off = [], l * per_layer
@@ -694,7 +698,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     for l in range(layers):
         for dst, src in zip(views(host_in, l), (q, k, v)):
             dst.copy_(src.cpu())
-    dev_views = [views(dev_in, l) for l in range(layers)]
+    dev_views = [[views(dev_in[b], l) for l in range(layers)] for b in range(nbuf)]
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]  # this rank's heads
     p2p_ring = world > 1 and args.transport == "p2p"
     # p2p: one gathered-output slot per layer and step, two steps' worth, so a step's outputs are read back
@@ -706,15 +710,14 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer; p2p: the
     # step's run of slots; either way read back in 4 shrinking chunks (a side-stream copy per layer costs
     # ~60 us of host time: 32 per step made the step host-bound)
-    direct = world == 1
     o_edges = sorted({0, layers} | {b for b in (layers // 2, layers - 4, layers - 1) if 0 < b < layers})
     o_chunks = list(zip(o_edges[:-1], o_edges[1:]))
     o_last = {hi - 1: (lo, hi) for lo, hi in o_chunks}
     if direct:
-        dev_out = torch.empty((layers, *q.shape), dtype=q.dtype, device=dev)
+        dev_out = [torch.empty((layers, *q.shape), dtype=q.dtype, device=dev) for _ in range(nbuf)]
         host_out = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
-        targets = [mlb.ops.out_targets([dev_out[l].data_ptr()], 0, q.shape[1] * q.shape[2], q.shape[2])
-                   for l in range(layers)]
+        targets = [[mlb.ops.out_targets([dev_out[b][l].data_ptr()], 0, q.shape[1] * q.shape[2], q.shape[2])
+                    for l in range(layers)] for b in range(nbuf)]
     host_ring = None  # p2p: pinned bytes for one step's slots (allocated once the slots exist)
     state = {"step": 0}
     compute = torch.cuda.current_stream(dev)
@@ -726,15 +729,19 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     loaded = [torch.cuda.Event() for _ in chunks]  # inputs of a chunk of layers on the device
     done = [torch.cuda.Event() for _ in range(layers)]  # output l read back
     ready = [torch.cuda.Event() for _ in range(layers)]  # output l computed
-    step_done = torch.cuda.Event()
-    step_done.record(compute)
+    comp_done = [torch.cuda.Event() for _ in range(nbuf)]  # the last step on buffer b has finished computing
+    io_done = [torch.cuda.Event() for _ in range(nbuf)]  # ... and its outputs are on the host (one GPU)
+    for ev in comp_done + io_done:
+        ev.record(compute)
+    metas = [None] * nbuf  # each buffer's metadata, alive until the buffer's next turn
 
     inner = backend.inner if world > 1 else backend
     h_l, hkv_l = q.shape[1], k_pools[0].shape[2]
     own = slice(rank * h_l, (rank + 1) * h_l)  # this rank's query heads in the gathered output
 
     def step():
-        loader.wait_event(step_done)  # the previous step has read every layer's inputs, metadata and plan
+        b = state["step"] % nbuf
+        loader.wait_event(comp_done[b])  # the last step on buffer b has read its inputs, metadata and plan
         with torch.cuda.stream(loader):
             # the step's metadata and plan go first in the loader's queue: on the compute stream their small
             # host-to-device copies queued behind the loader's input chunks (a measured ~0.48 ms at every
@@ -742,15 +749,19 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
             meta = mlb.AttentionMetadata.build(seqs, BS, dev)
             inner.plan(meta, h_l, hkv_l, dev, q.dtype)
             for c, (lo, hi) in enumerate(chunks):  # then the q/k/v rows in a few growing chunks
-                dev_in[lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer], non_blocking=True)
+                dev_in[b][lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer],
+                                                               non_blocking=True)
                 loaded[c].record(loader)
+        metas[b] = meta  # the device tensors it holds (and the plan's) stay unreused until comp_done[b]
+        if direct:
+            compute.wait_event(io_done[b])  # buffer b's outputs of two steps back have been read back
         nonlocal host_ring
         base = (state["step"] % 2) * layers  # this step's first slot of the p2p ring
         state["step"] += 1
         for l in range(layers):
             if l in chunk_of:
                 compute.wait_event(loaded[chunk_of[l]])
-            qd, kd, vd = dev_views[l]
+            qd, kd, vd = dev_views[b][l]
             if p2p_ring:
                 backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot base + l
                 if l in o_last:  # a chunk of layers is complete: read this rank's heads back on the side stream
@@ -767,13 +778,13 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
                         host_ring[lo:hi].copy_(rows, non_blocking=True)
                 continue
             if direct:
-                backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[l])
+                backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[b][l])
                 if l in o_last:  # a chunk of layers is complete: read it back on the side stream
                     lo, hi = o_last[l]
                     ready[l].record(compute)
                     copier.wait_event(ready[l])
                     with torch.cuda.stream(copier):
-                        host_out[lo:hi].copy_(dev_out[lo:hi], non_blocking=True)
+                        host_out[lo:hi].copy_(dev_out[b][lo:hi], non_blocking=True)
                 continue
             out = backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh gathered one
             ready[l].record(compute)
@@ -782,8 +793,11 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
                 outs[l].copy_(out[:, own], non_blocking=True)
                 done[l].record(copier)
             out.record_stream(copier)  # from torch's allocator: keep it alive until the copy ran
-        compute.wait_stream(copier)
-        step_done.record(compute)
+        if direct:
+            io_done[b].record(copier)
+        else:
+            compute.wait_stream(copier)
+        comp_done[b].record(compute)
 
     # warm-up as long as a timed window (and no synchronisation inside it): the host runs ahead of the device
     # by a growing number of steps, and torch's pinned staging buffers (metadata, plan) grow with that lead;
@@ -803,6 +817,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         s.record()
         for _ in range(args.steps):
             step()
+        compute.wait_stream(copier)  # the window ends when the last step's outputs are on the host
         e.record()
         torch.cuda.synchronize()
         windows.append(max_over_ranks(s.elapsed_time(e), world, dev) / args.steps)
