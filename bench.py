@@ -383,7 +383,6 @@ def run_ours(args) -> None:
     mlb._lib.lib().mlb_set_programmatic_launch(0 if args.no_pdl else 1)
     mlb._lib.lib().mlb_set_tensor_core_prefix(0 if args.no_tc_prefix else 1)
     mlb._lib.lib().mlb_set_concurrent_prefix(0 if args.serial_prefix else 1)
-    mlb._lib.lib().mlb_set_persistent_attention(1 if args.persistent else 0)
 
     weak = world > 1 and args.config == 2 and args.scaling == "weak"
     if args.config == 2:
@@ -615,7 +614,7 @@ def run_ours(args) -> None:
                        "append": "fused into the attention launch" if fused else "separate K1 launch",
                        "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
                        "shared_prefix_beside_per_sequence_kernel": not args.serial_prefix,
-                       "persistent_attention": bool(args.persistent), "pages_per_unit": args.pages_per_unit,
+                       "pages_per_unit": args.pages_per_unit,
                        "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
                        "partial_rows": plan.num_partial_rows, **wl.info},
             "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
@@ -899,8 +898,6 @@ def main() -> None:
                     help="plan without host tables: every row on the decode kernel's 8-column units")
     ap.add_argument("--no-fused-append", action="store_true",
                     help="launch the append (K1) before attention even when it could ride in the attention launch")
-    ap.add_argument("--persistent", action="store_true",
-                    help="per-sequence units on resident CTAs fed by a work queue (mlb_set_persistent_attention)")
     ap.add_argument("--pages-per-unit", type=int, default=0, help="split-K unit size in pages (0: the planner's)")
     ap.add_argument("--serial-prefix", action="store_true",
                     help="run the shared-prefix kernel before the per-sequence kernel instead of beside it")

@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 8 */
+MLB_API int mlb_abi_version(void);  /* 9 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -75,16 +75,6 @@ MLB_API int mlb_set_tensor_core_prefix(int enable);
  * setting.
  */
 MLB_API int mlb_set_concurrent_prefix(int enable);
-
-/*
- * Persistent per-sequence attention (process-wide, default off): 16-bit pools run the per-sequence units on
- * resident CTAs that take (unit, KV head) items from a work queue in plan order, prefetching each next
- * item's first pages while they finish the current one, instead of one CTA per item.  Same plan, same
- * results bit for bit.  The queue is a library-owned device word pair per (device, stream), reset by each
- * launch's last CTA; the first persistent launch on a device looks up its address (cudaGetSymbolAddress):
- * make it before any stream capture.  Returns the previous setting.
- */
-MLB_API int mlb_set_persistent_attention(int enable);
 
 /*
  * KV append.  Replaces write_kv (src/minillm/attention/paged_torch_ref.py:23-28), shared by all three

@@ -36,6 +36,14 @@ struct AttnArgs {
   const int64_t* app_slots;
 };
 
+// Query tokens per 8-column tile of the per-sequence kernel (columns = tokens x query heads of one KV head).
+// The planner numbers partial rows with it and the split-K reduction reads them with it: every entry point
+// takes it from here.
+inline int tokens_per_tile(int num_heads, int num_kv_heads) {
+  const int group = num_heads / num_kv_heads;
+  return group >= 8 ? 1 : 8 / group;
+}
+
 // True when every destination row start is 16-byte aligned (bases and both strides), so a run of
 // consecutive elements of one row can go out as one packed store.
 inline bool out_vec_ok(const mlb_out_targets& t, int elt_bytes) {

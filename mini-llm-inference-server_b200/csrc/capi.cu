@@ -71,8 +71,6 @@ constexpr int kMinSharePages = 8;    // ... sharing at least this many full page
 constexpr int kPrefillMinTokens = 16;   // multi-token rows this long go to tensor-core query tiles ...
 constexpr int kPrefillPiecePages = 128;  // ... split into pieces of at most this many pages (16 MMA tiles)
 
-int tokens_per_tile(int h, int hkv) { return std::max(1, 8 / (h / hkv)); }
-
 // The destinations of a call's final rows: its own `out`, or the caller's targets (checked).
 int resolve_targets(const char* what, void* out, int64_t st, int64_t sh, const mlb_out_targets* t,
                     mlb_out_targets* r) {
@@ -190,7 +188,7 @@ std::vector<ShareSet> find_shared_prefixes(const int32_t* qo, const int32_t* len
 // Enumerate (sequence, query tile) groups and the pages each must read; validates the step.
 int plan_groups(const int32_t* qo, const int32_t* lens, int num_seqs, int max_blocks, int h, int hkv, int bs,
                 std::vector<Group>& groups, int64_t* total_pages) {
-  const int tpt = tokens_per_tile(h, hkv);
+  const int tpt = mlb::tokens_per_tile(h, hkv);
   *total_pages = 0;
   groups.clear();
   for (int s = 0; s < num_seqs; ++s) {
@@ -220,19 +218,17 @@ namespace {
 std::atomic<int> g_programmatic_launch{1};
 std::atomic<int> g_tensor_core_prefix{1};
 std::atomic<int> g_concurrent_prefix{1};
-std::atomic<int> g_persistent_attention{0};
 }  // namespace
 bool programmatic_launch() { return g_programmatic_launch.load(std::memory_order_relaxed) != 0; }
 bool tensor_core_prefix() { return g_tensor_core_prefix.load(std::memory_order_relaxed) != 0; }
 bool concurrent_prefix() { return g_concurrent_prefix.load(std::memory_order_relaxed) != 0; }
-bool persistent_attention() { return g_persistent_attention.load(std::memory_order_relaxed) != 0; }
 }  // namespace mlb
 
 extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 8; }
+int mlb_abi_version(void) { return 9; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -244,10 +240,6 @@ int mlb_set_tensor_core_prefix(int enable) {
 
 int mlb_set_concurrent_prefix(int enable) {
   return mlb::g_concurrent_prefix.exchange(enable ? 1 : 0, std::memory_order_relaxed);
-}
-
-int mlb_set_persistent_attention(int enable) {
-  return mlb::g_persistent_attention.exchange(enable ? 1 : 0, std::memory_order_relaxed);
 }
 
 int mlb_kv_append(void* k_cache, void* v_cache, int cache_dtype, int64_t num_blocks, int block_size,
@@ -299,7 +291,7 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   int rc = plan_groups(qo_indptr, seq_lens, num_seqs, max_blocks_per_seq, num_heads, num_kv_heads, block_size, groups,
                        &total);
   if (rc != MLB_OK) return rc;
-  const int tpt = tokens_per_tile(num_heads, num_kv_heads);
+  const int tpt = mlb::tokens_per_tile(num_heads, num_kv_heads);
   const int group_size = num_heads / num_kv_heads;
 
   // ---- multi-token rows (prefill chunks on cache) of >= kPrefillMinTokens tokens: with host tables
@@ -528,7 +520,7 @@ int attention_call(const void* q, int64_t q_stride_tok, int64_t q_stride_head, c
   a.h = num_heads;
   a.hkv = num_kv_heads;
   a.group = num_heads / num_kv_heads;
-  a.tile_tokens = tokens_per_tile(num_heads, num_kv_heads);
+  a.tile_tokens = mlb::tokens_per_tile(num_heads, num_kv_heads);
   a.sl2 = scale * mlb::kLog2e;
   a.bt = block_tables;
   a.bt_stride = bt_stride;

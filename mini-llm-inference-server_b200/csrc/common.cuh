@@ -85,7 +85,6 @@ __device__ __forceinline__ void griddep_begin() {
 }
 
 bool programmatic_launch();  // host: the library-wide setting (mlb_set_programmatic_launch)
-bool persistent_attention();  // host: mlb_set_persistent_attention
 
 // kernel<<<grid, block, smem, s>>>(args...), with programmatic stream serialisation when enabled
 template <typename... KArgs, typename... Args>

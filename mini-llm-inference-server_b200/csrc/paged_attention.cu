@@ -22,8 +22,6 @@
 // f32 pools take a CUDA-core path with the same decomposition (fp32 accuracy, 1e-5).
 #include <algorithm>
 #include <climits>
-#include <mutex>
-#include <unordered_map>
 
 #include "attn_args.cuh"
 
@@ -367,263 +365,6 @@ __global__ void __launch_bounds__(NW * 32) paged_attn_mma_kernel(AttnArgs a) {
     sl_w[w] = sm_w[w] + 8;
   }
   merge_and_store<DH, DT, NW>(a, ui, kvh, so_w, sm_w, sl_w);
-}
-
-// ------------------------------------------------------------------ K2a, persistent
-
-// Work queue of the persistent kernel: per stream slot {next item, CTAs done}.  A launch takes items with
-// atomicAdd on the first word; the last CTA to finish puts both words back to 0, so every launch (and
-// every replay of a captured one) starts from an empty queue.  Launches on one stream run one after the
-// other, so a slot per stream is enough.
-constexpr int kQueueSlots = 256;
-__device__ int g_attn_queue[kQueueSlots * 2];
-
-// The same per-warp pipeline and arithmetic as paged_attn_mma_kernel (bit-identical results for the same
-// plan), but each CTA stays resident and takes (unit, KV head) items from the queue until it is empty.
-// Thread 0 takes the next item when the current one starts, so a CTA holds one item ahead and the queue
-// stays dynamic; each warp prefetches its first page of that next item while it finishes the current one,
-// so a unit boundary costs no page latency: the merge of the finished item (through the ring slot its
-// last page used) overlaps the page in flight.  Items come in plan order, largest first.
-template <int DT, int DH, int STAGES, int NW>
-__global__ void __launch_bounds__(NW * 32) paged_attn_persistent_kernel(AttnArgs a, int* queue, int n_items) {
-  static_assert(STAGES == 2, "the merge stash takes the slot of the warp's last page; the other holds the next item's");
-  constexpr int ROWB = DH * 2 + 16;
-  constexpr int TILE = 16 * ROWB;
-  constexpr int STAGE = 2 * TILE;
-  constexpr int KSTEPS = DH / 16;
-  constexpr int CH_ROW = DH * 2 / 16;
-  constexpr int CH_LANE = 2 * 16 * CH_ROW / 32;
-  static_assert(8 * DH * 4 + 64 <= STAGE, "merge state must fit in one ring slot");
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int s_first;        // the CTA's first item
-  __shared__ volatile int s_nxt;  // the item after the current one (-1 until thread 0's atomicAdd returns)
-  __shared__ int s_stash[NW];    // ring slot holding each warp's merge state
-  griddep_begin();
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint8_t* ring = smem + warp * STAGES * STAGE;
-  const uint32_t ring_u32 = smem_u32(ring);
-  const int64_t row_stride = static_cast<int64_t>(a.hkv) * DH * 2;
-  const uint32_t k_off = ((lane & 7) + 8 * ((lane >> 3) & 1)) * ROWB + (lane >> 4) * 16;
-  const uint32_t v_off = ((lane & 7) + 8 * (lane >> 4)) * ROWB + ((lane >> 3) & 1) * 16;
-  const int r0 = lane >> 2;
-  const int j0 = (lane & 3) * 2, j1 = j0 + 1;
-
-  if (threadIdx.x == 0) {
-    s_first = atomicAdd(queue, 1);
-    s_nxt = -1;
-  }
-  __syncthreads();
-  int cur = s_first;
-
-  // this warp's share of an item: pages pb, pb + NW, ... of the unit's range, `n` of them
-  struct Share {
-    UnitInfo ui;
-    const int32_t* table;
-    int pb, n, kvh;
-  };
-  auto share_of = [&](int item) -> Share {
-    Share sh{};
-    sh.table = a.bt;
-    if (item >= n_items) return sh;
-    sh.ui = unit_info(a, item / a.hkv);
-    sh.table = a.bt + static_cast<int64_t>(sh.ui.seq) * a.bt_stride;
-    sh.pb = sh.ui.pb + warp;
-    sh.n = sh.pb < sh.ui.pe ? (sh.ui.pe - sh.pb + NW - 1) / NW : 0;
-    sh.kvh = item % a.hkv;
-    return sh;
-  };
-  // block ids of a share, 32 pages per window (lane i holds page 32 w + i)
-  auto window = [&](const Share& sh, int w) -> int {
-    const int i = w * 32 + lane;
-    return i < sh.n ? __ldg(sh.table + sh.pb + i * NW) : 0;
-  };
-  uint32_t bad_mask = 0;  // bit s: the page in slot s had a block id outside the pool
-  // copy one page of KV head kvh (block id bid) into ring slot s; one commit group per call
-  auto issue_page = [&](int bid, int kvh, int s) {
-    const bool ok = bid >= 0 && bid < a.num_blocks;
-    bad_mask = ok ? (bad_mask & ~(1u << s)) : (bad_mask | (1u << s));
-    if (!ok) {
-      if (lane == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-    } else {
-      const int64_t page_off = (static_cast<int64_t>(bid) * kBlockSize * a.hkv + kvh) * (DH * 2);
-      uint8_t* slot = ring + s * STAGE;
-#pragma unroll
-      for (int c = 0; c < CH_LANE; ++c) {
-        const int e = c * 32 + lane;
-        const int kv = e / (16 * CH_ROW), row = (e / CH_ROW) % 16, ch = e % CH_ROW;
-        const char* src = (kv ? a.v_cache : a.k_cache) + page_off + row * row_stride + ch * 16;
-        cp_async16(slot + kv * TILE + row * ROWB + ch * 16, src);
-      }
-    }
-    cp_async_commit();
-  };
-  // the next item, once thread 0's atomicAdd has returned (bounded wait on shared memory)
-  auto next_item = [&]() -> int {
-    int v = s_nxt;
-    for (uint32_t spin = 0; v < 0 && spin < (1u << 24); ++spin) v = s_nxt;
-    if (v < 0) {  // never seen in practice: the atomicAdd returns within microseconds
-      if (lane == 0) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
-      return n_items;
-    }
-    return v;
-  };
-
-  Share sc = share_of(cur);
-  int wc = window(sc, 0), wc_next = window(sc, 1);
-  int slot0 = 0;         // ring slot of the current item's first page
-  bool pending = false;  // the current item's first page is already issued (by the previous item)
-
-  while (cur < n_items) {
-    const UnitInfo& ui = sc.ui;
-    const int kvh = sc.kvh;
-    if (!pending && sc.n > 0) issue_page(__shfl_sync(0xffffffffu, wc, 0), kvh, slot0);
-
-    uint32_t qb[KSTEPS][2];
-    {
-      const int n = lane >> 2, c2 = (lane & 3) * 2;
-      const bool live = n < ui.ncols;
-      const int tok = ui.q0 + ui.t0 + (live ? n / a.group : 0);
-      const int head = kvh * a.group + (live ? n % a.group : 0);
-      const uint16_t* qrow = reinterpret_cast<const uint16_t*>(a.q) + static_cast<int64_t>(tok) * a.q_st +
-                             static_cast<int64_t>(head) * a.q_sh;
-#pragma unroll
-      for (int ks = 0; ks < KSTEPS; ++ks) {
-        if (live) {
-          const int d = ks * 16 + c2;
-          qb[ks][0] = static_cast<uint32_t>(__ldg(qrow + d)) | (static_cast<uint32_t>(__ldg(qrow + d + 1)) << 16);
-          qb[ks][1] = static_cast<uint32_t>(__ldg(qrow + d + 8)) | (static_cast<uint32_t>(__ldg(qrow + d + 9)) << 16);
-        } else {
-          qb[ks][0] = qb[ks][1] = 0u;
-        }
-      }
-    }
-    const int lim0 = column_limit(a, ui, j0), lim1 = column_limit(a, ui, j1);
-    float o[DH / 16][4];
-#pragma unroll
-    for (int mt = 0; mt < DH / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
-
-    // The next item is taken late, when the unit's last 3 x NW pages begin (warp 0, which always has the most
-    // pages, takes it; the warps interleave pages, so all reach that point together), so that a CTA holds
-    // few pages of reserved work and the queue stays dynamic; learned there, its record and first block id
-    // are back when this warp's last page prefetches that item's first page.  A warp without pages here
-    // waits for warp 0's take.
-    int nxt = n_items;
-    Share sn{};
-    int wn = 0;
-    const int thr = max(ui.pb, ui.pe - 3 * NW);  // first unit page of the take
-    const int learn_at = sc.n > 0 ? max(0, min(sc.n - 1, (thr - sc.pb + NW - 1) / NW)) : -1;
-    auto learn = [&]() {
-      if (warp == 0 && lane == 0) s_nxt = atomicAdd(queue, 1);
-      nxt = next_item();
-      sn = share_of(nxt);
-      wn = window(sn, 0);
-    };
-    if (learn_at < 0) learn();
-    int s = slot0, win = 0;
-    bool next_pending = false;
-    for (int i = 0; i < sc.n; ++i) {
-      if (i == learn_at) learn();
-      // prefetch: this item's page i + 1, else the next item's first page, else nothing (an empty group)
-      if (i + 1 < sc.n) {
-        if (((i + 1) >> 5) != win) {
-          ++win;
-          wc = wc_next;
-          wc_next = window(sc, win + 1);
-        }
-        issue_page(__shfl_sync(0xffffffffu, wc, (i + 1) & 31), kvh, s ^ 1);
-      } else if (sn.n > 0) {
-        issue_page(__shfl_sync(0xffffffffu, wn, 0), sn.kvh, s ^ 1);
-        next_pending = true;
-      } else {
-        cp_async_commit();
-      }
-      cp_async_wait<1>();  // page i (the group before the newest) has landed for this lane
-      __syncwarp();        // ... and for every other lane
-      const int page = sc.pb + i * NW;
-      if (a.app_k) take_new_rows<DH, ROWB, TILE>(a, ui, kvh, ring + s * STAGE, page * kBlockSize, lane);
-      if (!((bad_mask >> s) & 1u)) {
-        const int tok_base = page * kBlockSize;
-        uint8_t* vt = ring + s * STAGE + TILE;
-        const int live_rows = ui.L - tok_base;
-        if (live_rows < 16) {  // rows past the context end: P is 0 there, but 0 * NaN is NaN
-          const int r_begin = live_rows < 0 ? 0 : live_rows;
-          for (int e = lane; e < (16 - r_begin) * CH_ROW; e += 32) {
-            const int r = r_begin + e / CH_ROW, c = e % CH_ROW;
-            *reinterpret_cast<uint4*>(vt + r * ROWB + c * 16) = make_uint4(0u, 0u, 0u, 0u);
-          }
-          __syncwarp();
-        }
-        attend_page<DT, DH>(ring_u32 + s * STAGE + k_off, ring_u32 + s * STAGE + TILE + v_off, qb, tok_base + r0,
-                            lim0, lim1, a.sl2, o, m0, m1, l0, l1);
-      }
-      __syncwarp();  // every lane is done with slot s before it is refilled
-      s ^= 1;
-    }
-    // s: the slot after this item's last page; it holds the next item's first page when one was issued.
-    // The other slot (the last page's, or an idle one) takes the merge state.
-    const int stash = s ^ 1;
-#pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      l0 += __shfl_xor_sync(0xffffffffu, l0, off);
-      l1 += __shfl_xor_sync(0xffffffffu, l1, off);
-    }
-    float* so = reinterpret_cast<float*>(ring + stash * STAGE);
-    float* sm = so + 8 * DH;
-    float* sl = sm + 8;
-#pragma unroll
-    for (int mt = 0; mt < DH / 16; ++mt) {
-      const int d = mt * 16 + r0;
-      so[j0 * DH + d] = o[mt][0];
-      so[j1 * DH + d] = o[mt][1];
-      so[j0 * DH + d + 8] = o[mt][2];
-      so[j1 * DH + d + 8] = o[mt][3];
-    }
-    if (lane < 4) {
-      sm[j0] = m0;
-      sm[j1] = m1;
-      sl[j0] = l0;
-      sl[j1] = l1;
-    }
-    if (lane == 0) s_stash[warp] = stash;
-    __syncthreads();
-    // every warp read s_nxt before this barrier; cleared before the next, so no warp of the next item sees
-    // this item's value (warp 0 writes the next one after that barrier)
-    if (threadIdx.x == 0) s_nxt = -1;
-    {
-      const float* so_w[NW];
-      const float* sm_w[NW];
-      const float* sl_w[NW];
-#pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        so_w[w] = reinterpret_cast<const float*>(smem + (w * STAGES + s_stash[w]) * STAGE);
-        sm_w[w] = so_w[w] + 8 * DH;
-        sl_w[w] = sm_w[w] + 8;
-      }
-      merge_and_store<DH, DT, NW>(a, ui, kvh, so_w, sm_w, sl_w);
-    }
-    __syncthreads();  // every merge read is done before a stash slot is refilled
-    // the next item becomes current; its first page sits in slot s when it was issued
-    cur = nxt;
-    sc = sn;
-    wc = wn;
-    wc_next = window(sc, 1);
-    slot0 = next_pending ? s : 0;
-    pending = next_pending;
-  }
-  cp_async_wait<0>();
-
-  // the last CTA out leaves an empty queue for the next launch
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(queue + 1, 1) == static_cast<int>(gridDim.x) - 1) {
-      queue[0] = 0;
-      queue[1] = 0;
-      __threadfence();
-    }
-  }
 }
 
 // ------------------------------------------------------------------ shared prefixes (K2s)
@@ -1092,55 +833,6 @@ cudaError_t launch_mma(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
   return launch_k(k, dim3(static_cast<unsigned>(ctas)), dim3(NW * 32), bytes, s, a);
 }
 
-// The queue words of a (device, stream): a slot of g_attn_queue, assigned on the stream's first launch and
-// kept (nullptr once a device has used all kQueueSlots: the caller falls back to the one-shot kernel).
-// The symbol's device address is looked up on the first call per device: make it before any capture.
-int* queue_for(cudaStream_t s, cudaError_t* err) {
-  static std::mutex mu;
-  static std::unordered_map<uint64_t, int> slot_of;
-  static int used[64] = {};
-  static int* base[64] = {};
-  int dev = 0;
-  *err = cudaGetDevice(&dev);
-  if (*err != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!base[dev]) {
-    *err = cudaGetSymbolAddress(reinterpret_cast<void**>(&base[dev]), g_attn_queue);
-    if (*err != cudaSuccess) {
-      base[dev] = nullptr;
-      return nullptr;
-    }
-  }
-  const uint64_t key = (static_cast<uint64_t>(dev) << 56) ^ static_cast<uint64_t>(reinterpret_cast<uintptr_t>(s));
-  auto it = slot_of.find(key);
-  if (it == slot_of.end()) {
-    if (used[dev] >= kQueueSlots) return nullptr;
-    it = slot_of.emplace(key, used[dev]++).first;
-  }
-  return base[dev] + 2 * it->second;
-}
-
-template <int DT, int DH, int STAGES, int NW>
-cudaError_t launch_persistent(const AttnArgs& a, int64_t items, int* queue, cudaStream_t s) {
-  constexpr int bytes = NW * STAGES * 2 * 16 * (DH * 2 + 16);
-  static unsigned long long done = 0;
-  static int per_sm[64] = {};
-  auto k = paged_attn_persistent_kernel<DT, DH, STAGES, NW>;
-  cudaError_t e = set_smem(k, bytes, done);
-  if (e != cudaSuccess) return e;
-  int dev = 0, sms = 148;
-  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
-  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-  int occ = dev < 64 ? __atomic_load_n(&per_sm[dev], __ATOMIC_RELAXED) : 0;
-  if (occ == 0) {
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k, NW * 32, bytes)) != cudaSuccess) return e;
-    if (occ < 1) occ = 1;
-    if (dev < 64) __atomic_store_n(&per_sm[dev], occ, __ATOMIC_RELAXED);
-  }
-  const int64_t grid = std::min<int64_t>(items, static_cast<int64_t>(sms) * occ);
-  return launch_k(k, dim3(static_cast<unsigned>(grid)), dim3(NW * 32), bytes, s, a, queue, static_cast<int>(items));
-}
-
 template <int DH>
 cudaError_t launch_f32(const AttnArgs& a, int64_t ctas, cudaStream_t s) {
   constexpr int bytes = (8 * DH + kWarps * (8 * DH + 16)) * 4;
@@ -1178,18 +870,6 @@ cudaError_t launch_shared_prefix_attention(const AttnArgs& a, int dtype, int dh,
 
 cudaError_t launch_paged_attention(const AttnArgs& a, int dtype, int dh, int64_t num_units, cudaStream_t s) {
   const int64_t ctas = num_units * a.hkv;
-  if (persistent_attention() && (dtype == MLB_BF16 || dtype == MLB_F16) && ctas <= INT32_MAX) {
-    cudaError_t e = cudaSuccess;
-    int* queue = queue_for(s, &e);
-    if (e != cudaSuccess) return e;
-    if (queue) {  // else: every queue slot of the device is taken; the one-shot kernel below
-#define MLB_PERSIST(T, D)                                                           \
-  if (dtype == T && dh == D) return launch_persistent<T, D, 2, 4>(a, ctas, queue, s);
-      MLB_PERSIST(MLB_BF16, 64) MLB_PERSIST(MLB_BF16, 128) MLB_PERSIST(MLB_BF16, 256)
-      MLB_PERSIST(MLB_F16, 64) MLB_PERSIST(MLB_F16, 128) MLB_PERSIST(MLB_F16, 256)
-#undef MLB_PERSIST
-    }
-  }
   if (dtype == MLB_BF16) {
     if (dh == 64) return launch_mma<MLB_BF16, 64, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);
     if (dh == 128) return launch_mma<MLB_BF16, 128, MLB_ATTN_STAGES, MLB_ATTN_WARPS>(a, ctas, s);

@@ -71,8 +71,16 @@ int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int64_t q_s
                                 const int32_t* reduce_rows, const int32_t* reduce_chunks, int64_t num_tokens,
                                 void* out, int64_t out_stride_tok, int64_t out_stride_head, int32_t* err_word,
                                 void* stream) {
-  if (num_partial_rows < 0 || num_heads <= 0 || head_dim <= 0 || num_kv_heads <= 0)
+  if (num_partial_rows < 0 || num_heads <= 0 || head_dim <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads)
     return noalloc_fail(MLB_EINVAL, "paged_attention_noalloc: bad sizes");
+  // Bound the row count before multiplying, so a huge caller-supplied count cannot wrap the byte total
+  // below the array size: one row takes num_heads x (head_dim + 1) floats.
+  const size_t row_bytes = static_cast<size_t>(num_heads) * (static_cast<size_t>(head_dim) + 1) * sizeof(float);
+  if (static_cast<uint64_t>(num_partial_rows) > kNoallocScratchBytes / row_bytes)
+    return noalloc_fail(MLB_ENOSPACE, "paged_attention_noalloc: the plan's " + std::to_string(num_partial_rows) +
+                                          " split-K rows do not fit the " + std::to_string(kNoallocScratchBytes) +
+                                          "-byte static array; use mlb_paged_attention with a workspace or a "
+                                          "larger pages_per_unit");
   const size_t o_bytes = static_cast<size_t>(num_partial_rows) * num_heads * head_dim * sizeof(float);
   const size_t lse_bytes = static_cast<size_t>(num_partial_rows) * num_heads * sizeof(float);
   const size_t lse_off = (o_bytes + 255) & ~size_t(255);
@@ -100,9 +108,8 @@ int mlb_paged_attention_noalloc(const void* q, int64_t q_stride_tok, int64_t q_s
                                      po, plse, num_partial_rows, out, out_stride_tok, out_stride_head, nullptr,
                                      err_word, stream);
   if (rc != MLB_OK || num_partial_rows == 0 || num_tokens == 0) return rc;  // mlb_last_error() says why
-  const int group = num_heads / num_kv_heads;
-  const int tpt = group >= 8 ? 1 : 8 / group;  // query tokens per tile, as the planner sets it
-  return mlb_splitk_reduce(po, plse, num_partial_rows, reduce_rows, reduce_chunks, tpt, num_tokens, num_heads,
+  return mlb_splitk_reduce(po, plse, num_partial_rows, reduce_rows, reduce_chunks,
+                           mlb::tokens_per_tile(num_heads, num_kv_heads), num_tokens, num_heads,
                            head_dim, out, out_stride_tok, out_stride_head, dtype, nullptr, stream);
 }
 

@@ -34,6 +34,18 @@ def bits(x: torch.Tensor) -> torch.Tensor:
     return x.view(torch.int32) if x.element_size() == 4 else x.view(torch.int16)
 
 
+def max_abs(got: torch.Tensor, expected: torch.Tensor) -> float:
+    """Largest elementwise |got - expected| (NaN if either holds a NaN where the other does not agree)."""
+    g, e = got.float().cpu(), expected.float().cpu()
+    if g.shape != e.shape:
+        raise AssertionError(f"shapes differ: {tuple(g.shape)} vs {tuple(e.shape)}")
+    return (g - e).abs().max().item() if g.numel() else 0.0
+
+
 def assert_close(got: torch.Tensor, expected: torch.Tensor, dtype) -> None:
+    """The north star's bar, max-abs <= 2e-2 (16-bit) or 1e-5 (fp32) against the fp32 oracle with no relative
+    term, and beside it the reference's own form of the check (tests/test_kernels.py:59: atol = rtol)."""
     tol = TOL[dtype]
     torch.testing.assert_close(got.float().cpu(), expected.float().cpu(), atol=tol, rtol=tol)
+    err = max_abs(got, expected)
+    assert err <= tol, f"max |diff| {err:.3g} > {tol} ({dtype})"

@@ -50,7 +50,7 @@ def test_backend_matches_reference_on_a_mixed_step(mlb, cuda, dtype):
     got = backend.forward(q, k, v, k_pool, v_pool, meta)
     assert torch.equal(k_pool.cpu(), ref_k) and torch.equal(v_pool.cpu(), ref_v)  # identical writes
     assert got.dtype == q.dtype and got.shape == q.shape
-    torch.testing.assert_close(got.float().cpu(), expected, atol=2e-2, rtol=2e-2)
+    assert_close(got, expected, dtype)
 
 
 def test_backend_on_a_decode_only_step(mlb, cuda):
@@ -60,7 +60,7 @@ def test_backend_on_a_decode_only_step(mlb, cuda):
     q, k, v = q[:3], k[:3], v[:3]
     expected, _, _ = reference(q, k, v, k_pool, v_pool, seqs)
     got = mlb.B200Backend().forward(q, k, v, k_pool, v_pool, meta)
-    torch.testing.assert_close(got.float().cpu(), expected, atol=2e-2, rtol=2e-2)
+    assert_close(got, expected, torch.bfloat16)
 
 
 def test_plan_is_built_once_per_step_and_reused_by_every_layer(mlb, cuda):

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 8
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 9
 
 
 def test_plan_record_layouts_match_header(L):
@@ -102,6 +102,20 @@ def test_invalid_arguments_return_status_without_launching(L):
         L.check(rc, "paged_attention")
     # zero work is a successful no-op
     assert lib.mlb_block_copy(None, 0, 10, 64, None, None, 0, None, None) == L.MLB_OK
+
+
+def test_noalloc_rejects_row_counts_that_would_wrap_the_size_check(L):
+    """A huge split-K row count must be refused before its byte total is computed: rows x 32 heads x 129
+    floats x 4 B for rows = 2^60 wraps a 64-bit size to a small number.  Refused on the host, no launch."""
+    lib = L.lib()
+    for rows in (1 << 60, (1 << 63) - 1, L.NOALLOC_SCRATCH_BYTES):
+        rc = lib.mlb_paged_attention_noalloc(None, 0, 0, None, None, 2, 10, 16, 32, 8, 128, 0.1, None, 0, None,
+                                             None, 1, None, 1, None, 0, None, rows, None, None, 1, None, 0, 0,
+                                             None, None)
+        assert rc == L.MLB_ENOSPACE and "static array" in L.last_error(), rows
+    rc = lib.mlb_paged_attention_noalloc(None, 0, 0, None, None, 2, 10, 16, 30, 8, 128, 0.1, None, 0, None, None, 1,
+                                         None, 1, None, 0, None, 4, None, None, 1, None, 0, 0, None, None)
+    assert rc == L.MLB_EINVAL  # 30 query heads do not group over 8 KV heads
 
 
 def test_fused_append_validates_on_the_host(L, mlb):

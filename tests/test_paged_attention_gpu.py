@@ -37,7 +37,7 @@ def test_golden_cases(mlb, cuda, case, dtype):
     assert_close(out, expected, dtype)
     assert torch.equal(t["k_pool"].cpu(), k_after) and torch.equal(t["v_pool"].cpu(), v_after)
     if dtype == torch.float32:  # straight against the reference's own output
-        torch.testing.assert_close(out.cpu(), torch.from_numpy(ATTN[f"{case.name}.out"]), atol=1e-5, rtol=1e-5)
+        assert_close(out, torch.from_numpy(ATTN[f"{case.name}.out"]), dtype)
 
 
 @pytest.mark.parametrize("dtype", DTYPES, ids=str)
