@@ -145,6 +145,46 @@ class AttentionMetadata:
         )
 
 
+def host_view(meta) -> tuple[np.ndarray, bool]:
+    """(int32 block tables on the host, append_private) for a metadata object that carries only the
+    reference's fields (minillm.attention.metadata.AttentionMetadata, metadata.py:36-52): its device
+    `block_tables_i32` and `slot_mapping` are copied back (one synchronisation), and `append_private` holds
+    only if every slot is the one the tables give (block_ids[p // bs] * bs + p % bs, as the reference's build
+    makes it) and every written block is read by its own row alone.  This package's AttentionMetadata
+    carries both already and needs no copy."""
+    bs = int(meta.block_size)
+    qo = np.asarray(meta.query_start_loc, dtype=np.int64)
+    lens = np.asarray(meta.seq_lens, dtype=np.int64)
+    tables_t = meta.block_tables_i32
+    slots_t = meta.slot_mapping
+    if tables_t.is_cuda:  # both copies queued, then one wait
+        t_host = torch.empty(tables_t.shape, dtype=torch.int32, pin_memory=True)
+        s_host = torch.empty(slots_t.shape, dtype=torch.int64, pin_memory=True)
+        t_host.copy_(tables_t, non_blocking=True)
+        s_host.copy_(slots_t, non_blocking=True)
+        torch.cuda.current_stream(tables_t.device).synchronize()
+    else:
+        t_host, s_host = tables_t.to(torch.int32), slots_t.to(torch.int64)
+    tables = t_host.numpy().copy()
+    slots = s_host.numpy()
+    s = lens.size
+    new = np.diff(qo)
+    n = int(qo[-1]) if s else 0
+    if s == 0 or n == 0 or slots.shape != (n,):
+        return tables, n == 0
+    owner = np.repeat(np.arange(s), new)
+    positions = np.arange(n, dtype=np.int64) - qo[owner] + (lens - new)[owner]
+    page = positions // bs
+    if tables.ndim != 2 or tables.shape[0] != s or (page >= tables.shape[1]).any() or (positions < 0).any():
+        return tables, False
+    written = tables[owner, page].astype(np.int64)
+    if not np.array_equal(written * bs + positions % bs, slots):
+        return tables, False
+    used = -(-lens // bs)
+    used_ids = tables[np.arange(tables.shape[1])[None, :] < used[:, None]].astype(np.int64)
+    return tables, _written_private(written, used_ids)
+
+
 def _written_private(written: np.ndarray, used_ids: np.ndarray) -> bool:
     """Every written block occurs once among all sequences' context pages (`written` is a subset of them)."""
     if written.size == 0:

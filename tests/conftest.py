@@ -9,6 +9,7 @@
 from __future__ import annotations
 
 import importlib
+import os
 import sys
 from pathlib import Path
 
@@ -21,6 +22,15 @@ for p in (str(REPO), str(GOLDEN)):
         sys.path.insert(0, p)
 
 PACKAGE = "mini-llm-inference-server_b200"
+
+
+def reference_src() -> Path | None:
+    """The reference's `src/` directory, when its source tree is at hand (MINILLM_REF_SRC, or a checkout named
+    `reference` beside this repository): CPU tests then pin fixtures and adapters against the reference's
+    live objects.  The GPU box has no copy, and no GPU test uses it."""
+    env = os.environ.get("MINILLM_REF_SRC")
+    cand = Path(env) if env else REPO.parent / "reference" / "src"
+    return cand if (cand / "minillm" / "attention" / "metadata.py").is_file() else None
 
 
 def pytest_configure(config):

@@ -11,11 +11,15 @@ It imports the reference's own `write_kv`, `TorchRefBackend.forward` (write + pa
 - append_cast.npz fp32 rows written into bf16 and fp16 pools by the reference: the stored bit patterns
 - metadata.json   AttentionMetadata fields for a set of ragged steps (incl. tests/test_paged.py:41-50)
 - prefix.json     root and block hashes (incl. tests/test_prefix_cache.py:33-40)
+- interface.json  the field names of the reference's AttentionMetadata dataclass and the abstract methods of
+                  its AttentionBackend: the object shape an unmodified reference engine hands a backend
 Nothing here runs on the GPU box; the tests only read the files it wrote.
 """
 
 from __future__ import annotations
 
+import dataclasses
+import inspect
 import json
 import os
 import random
@@ -32,6 +36,7 @@ if "MINILLM_REF_SRC" not in os.environ:
 sys.path.insert(0, os.environ["MINILLM_REF_SRC"])
 
 import cases  # noqa: E402
+from minillm.attention.base import AttentionBackend  # noqa: E402
 from minillm.attention.metadata import AttentionMetadata, SeqStep  # noqa: E402
 from minillm.attention.paged_torch_ref import write_kv  # noqa: E402
 from minillm.attention.torch_ref import TorchRefBackend  # noqa: E402
@@ -124,6 +129,12 @@ def prefix_golden() -> dict:
     return {"keys": keys, "roots": roots, "chains": chains, "block_100_115": single}
 
 
+def interface_golden() -> dict:
+    return {"metadata_fields": [f.name for f in dataclasses.fields(AttentionMetadata)],
+            "backend_abstract_methods": sorted(AttentionBackend.__abstractmethods__),
+            "forward_parameters": list(inspect.signature(AttentionBackend.forward).parameters)}
+
+
 def main() -> None:
     torch.manual_seed(0)
     print("attention (reference TorchRefBackend.forward, fp32 CPU):")
@@ -131,6 +142,7 @@ def main() -> None:
     np.savez_compressed(HERE / "append_cast.npz", **append_golden())
     (HERE / "metadata.json").write_text(json.dumps(metadata_golden()) + "\n")
     (HERE / "prefix.json").write_text(json.dumps(prefix_golden(), ensure_ascii=False) + "\n")
+    (HERE / "interface.json").write_text(json.dumps(interface_golden()) + "\n")
     for f in sorted(HERE.glob("*.npz")) + sorted(HERE.glob("*.json")):
         print(f"  wrote {f.name}: {f.stat().st_size} bytes")
 

@@ -194,3 +194,77 @@ def test_concurrent_prefix_kernel_changes_no_bit(mlb, cuda, tc):
     finally:
         lib.mlb_set_tensor_core_prefix(prev_tc)
         lib.mlb_set_concurrent_prefix(prev_cc)
+
+
+def _reference_shaped(meta):
+    """An object with exactly the reference's AttentionMetadata fields (tests/golden/interface.json, made by
+    running the reference): what an unmodified reference engine hands the backend."""
+    import json
+    import types
+
+    from conftest import GOLDEN
+
+    fields = json.loads((GOLDEN / "interface.json").read_text())["metadata_fields"]
+    return types.SimpleNamespace(**{f: getattr(meta, f) for f in fields})
+
+
+@pytest.mark.parametrize("kind", ["decode", "shared_prefix", "mixed"])
+def test_reference_metadata_object_keeps_every_fast_path(mlb, cuda, kind):
+    """The reference's metadata object (no host tables, no append_private): the backend derives them once per
+    step, so the plan, the fused append and therefore every bit of the pools and outputs equal the run with
+    this package's metadata, over 3 layers; both within the north star's bar of the oracle.  With
+    derive_host_tables off, every row runs on 8-column units and the append launches first: pools still
+    bit-identical, outputs within the bar."""
+    r = random.Random(5)
+    ids = list(range(1200))
+    r.shuffle(ids)
+    if kind == "decode":
+        steps = [(c, 1) for c in (17, 300, 2047, 64, 999, 5)]
+        prefix = []
+    elif kind == "shared_prefix":
+        steps = [(30 * 16 + r.randint(0, 50), 1) for _ in range(12)]
+        prefix = ids[:30]
+    else:
+        steps = [(0, 37), (90, 1), (40, 25), (0, 1), (300, 1), (1000, 70)]
+        prefix = []
+    nxt, seqs = len(prefix), []
+    for c, n in steps:
+        need = -(-(c + n) // 16)
+        own = need - len(prefix)
+        seqs.append(mlb.SeqStep(c, n, prefix + ids[nxt:nxt + own]))
+        nxt += own
+    meta = mlb.AttentionMetadata.build(seqs, 16, cuda)
+    ntok = meta.query_start_loc[-1]
+    g = torch.Generator(device=cuda).manual_seed(8)
+    pools = [(torch.randn(1200, 16, 8, 128, device=cuda, generator=g).to(torch.bfloat16),
+              torch.randn(1200, 16, 8, 128, device=cuda, generator=g).to(torch.bfloat16)) for _ in range(3)]
+    q = torch.randn(ntok, 32, 128, device=cuda, generator=g).to(torch.bfloat16)
+    k = torch.randn(ntok, 8, 128, device=cuda, generator=g).to(torch.bfloat16)
+    v = torch.randn(ntok, 8, 128, device=cuda, generator=g).to(torch.bfloat16)
+
+    def run(m, **kw):
+        backend = mlb.B200Backend(**kw)
+        layers = [(kp.clone(), vp.clone()) for kp, vp in pools]
+        outs = [backend.forward(q, k, v, kp, vp, m) for kp, vp in layers]
+        torch.cuda.synchronize()
+        return backend, outs, layers
+
+    b_own, o_own, p_own = run(meta)
+    ref_meta = _reference_shaped(meta)
+    b_ref, o_ref, p_ref = run(ref_meta)
+    assert b_ref._plan.num_shared_units == b_own._plan.num_shared_units
+    assert b_ref.last_append_fused == b_own.last_append_fused == (kind != "mixed")
+    if kind == "shared_prefix":
+        assert b_ref._plan.num_shared_units > 0
+    for a, b in zip(o_ref, o_own):
+        assert torch.equal(a, b)
+    for (ka, va), (kb, vb) in zip(p_ref, p_own):
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+    expected, ref_k, ref_v = reference(q, k, v, pools[0][0], pools[0][1], seqs)
+    assert torch.equal(p_ref[0][0].cpu(), ref_k) and torch.equal(p_ref[0][1].cpu(), ref_v)
+    assert_close(o_ref[0], expected, torch.bfloat16)
+    b_off, o_off, p_off = run(_reference_shaped(meta), derive_host_tables=False)
+    assert b_off._plan.num_shared_units == 0 and not b_off.last_append_fused
+    for (ka, va), (kb, vb) in zip(p_off, p_own):
+        assert torch.equal(ka, kb) and torch.equal(va, vb)
+    assert_close(o_off[0], expected, torch.bfloat16)

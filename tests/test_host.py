@@ -159,17 +159,17 @@ def test_compaction_matches_oracle_plan_and_keeps_accounting(mlb, seed):
         bm.free(t)
     bm.check(tables)
     before = [list(t) for t in tables]
-    cached = list(bm._cached)
+    cached = bm.cached_blocks()
     src, dst, expect = oracle.compact_plan(before + [cached], 200)
     got_src, got_dst = bm.compact(tables)
     assert (got_src, got_dst) == (src, dst)
     assert tables == expect[:-1]
     bm.check(tables)
-    live = {b for t in tables for b in t} | set(bm._cached)
+    live = {b for t in tables for b in t} | set(bm.cached_blocks())
     assert live == set(range(len(live)))
     for b_old, b_new in zip(src, dst):  # prefix names follow the moved blocks
         assert not pc.is_cached(b_old) or b_old in live
-    assert all(pc.is_cached(b) for b in bm._cached)
+    assert all(pc.is_cached(b) for b in bm.cached_blocks())
 
 
 # ---------- prefix-cache index
