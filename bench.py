@@ -36,6 +36,7 @@ import statistics
 import subprocess
 import sys
 import time
+import types
 from datetime import timedelta
 from pathlib import Path
 
@@ -367,6 +368,295 @@ METRIC = "Llama-3.1-8B paged decode attn: KV-read GB/s vs HBM peak, seqs/s; appe
 # ----------------------------------------------------------------------------- our arm
 
 
+@dataclass
+class Rig:
+    """One workload's device state on this rank: its layer pools (this rank's KV heads), the step's q/k/v,
+    metadata, plan, workspace and output transport."""
+
+    wl: Workload
+    layers: int
+    rank: int
+    world: int
+    dev: torch.device
+    hkv_l: int
+    h_l: int
+    qs: slice
+    ks: slice
+    k_pools: list
+    v_pools: list
+    q: torch.Tensor  # the step's full rows [n_q, H, Dh] (every rank holds the same)
+    q_l: torch.Tensor  # this rank's heads
+    k_l: torch.Tensor
+    v_l: torch.Tensor
+    meta_att: object
+    meta_app: object
+    plan: object
+    ws: object
+    out_l: torch.Tensor
+    p2p: bool
+    peers: object
+    gathered: torch.Tensor | None
+    copies: int
+    ptrs: torch.Tensor | None
+    src: torch.Tensor | None
+    dst: torch.Tensor | None
+    fused: bool
+    n_q: int
+    n_app: int
+    ops: object
+    pdl: bool = True
+
+    @property
+    def launches_per_layer(self) -> int:
+        # [append,] attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
+        # [+ p2p barrier]
+        return ((1 if self.fused else 2) + (1 if self.plan.num_shared_units else 0)
+                + (1 if self.plan.num_partial_rows or self.p2p else 0) + (1 if self.p2p else 0))
+
+
+def make_rig(args, mlb, sharding, wl: Workload, dev, rank: int, world: int, layers: int) -> Rig:
+    ops = mlb.ops
+    hkv_l, h_l = HKV // world, H // world
+    n_app, n_q = sum(n for _, n, _ in wl.append_rows), sum(n for _, n, _ in wl.attend_rows)
+    nb = wl.num_blocks
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    k_pools, v_pools = [], []
+    for l in range(layers):  # layer 0 drawn, the others copies of it (separate memory, the same cost to read)
+        for pools in (k_pools, v_pools):
+            p = torch.empty(nb, BS, hkv_l, DH, device=dev, dtype=torch.bfloat16)
+            if l == 0:
+                p.normal_(0.0, wl.kv_scale, generator=g)
+            else:
+                p.copy_(pools[0])
+            pools.append(p)
+    gq = torch.Generator(device=dev).manual_seed(7)  # the same full q/k/v on every rank
+    q = torch.randn(n_q, H, DH, device=dev, generator=gq).to(torch.bfloat16)
+    k = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
+    v = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
+    qs, ks = sharding.head_range(rank, world, H), sharding.head_range(rank, world, HKV)
+    q_l, k_l, v_l = q[:, qs], k[:, ks], v[:, ks]
+
+    def seqsteps(rows):
+        return [mlb.SeqStep(c, n, b) for c, n, b in rows]
+
+    meta_att = mlb.AttentionMetadata.build(seqsteps(wl.attend_rows), BS, dev)
+    meta_app = meta_att if wl.append_rows is wl.attend_rows else mlb.AttentionMetadata.build(
+        seqsteps(wl.append_rows), BS, dev)
+    if args.no_query_tiles:  # every row on 8-column work units (no host tables: no query tiles, no cascade)
+        plan = ops.plan_attention(meta_att.query_start_loc, meta_att.seq_lens, meta_att.block_tables_i32.shape[1],
+                                  h_l, hkv_l, dev, pages_per_unit=args.pages_per_unit)
+    else:
+        plan = mlb.B200Backend(pages_per_unit=args.pages_per_unit).plan(meta_att, h_l, hkv_l, dev)
+    p2p = world > 1 and args.transport == "p2p"
+    copies = len(wl.copy_src)
+    ptrs = src = dst = None
+    if copies:
+        ptrs = ops.pool_pointer_table(k_pools + v_pools)
+        src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
+        dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
+    # the append rides in the attention launch when every written block is private to its row (the backend's
+    # rule: B200Backend.forward); otherwise K1 runs first
+    fused = (not args.no_fused_append and meta_app is meta_att and meta_att.append_private
+             and ops.can_fuse_append(plan, k_pools[0], k_l, v_l))
+    return Rig(wl, layers, rank, world, dev, hkv_l, h_l, qs, ks, k_pools, v_pools, q, q_l, k_l, v_l, meta_att,
+               meta_app, plan, ops.Workspace(), torch.empty(n_q, h_l, DH, device=dev, dtype=torch.bfloat16), p2p,
+               sharding.PeerOutputs(n_q, H, DH, torch.bfloat16, dev) if p2p else None,
+               torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None,
+               copies, ptrs, src, dst, fused, n_q, n_app, ops, not args.no_pdl)
+
+
+def attend(r: Rig, l: int) -> None:
+    slot = l % r.peers.slots if r.p2p else 0
+    r.ops.attention_partials(r.q_l, r.k_pools[l], r.v_pools[l], r.meta_att.block_tables_i32, r.meta_att.seq_lens_i32,
+                             r.meta_att.qo_indptr, r.plan, r.ws, r.out_l,
+                             targets=r.peers.local_targets(slot, r.qs.start) if r.p2p else None,
+                             append=(r.k_l, r.v_l, r.meta_app.slot_mapping) if r.fused else None)
+
+
+def gather_step(r: Rig, l: int) -> None:
+    """The layer's split-K reduction and output all-gather: p2p = the reduction storing every row into every
+    rank's buffer + the flag barrier; NCCL = the local reduction + all_gather_into_tensor."""
+    if r.p2p:
+        slot = l % r.peers.slots
+        r.ops.splitk_reduce_gather(r.plan, r.ws, r.peers.targets(slot, r.qs.start), r.peers.self_dest,
+                                   torch.bfloat16, DH, r.dev)
+        r.peers.barrier()
+        return
+    r.ops.splitk_reduce(r.plan, r.ws, r.out_l)
+    if r.world > 1:
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(r.gathered, r.out_l)
+
+
+def layer_step(r: Rig, l: int, ev=None) -> None:
+    if not r.fused:
+        r.ops.kv_append(r.k_pools[l], r.v_pools[l], r.meta_app.slot_mapping, r.k_l, r.v_l)
+    if ev is not None:
+        ev[0].record()
+    attend(r, l)
+    if ev is not None:
+        ev[1].record()
+    gather_step(r, l)
+
+
+def full_step(r: Rig) -> None:
+    if r.copies:  # COW / compaction: one launch over every layer's K and V pools
+        r.ops.block_copy(r.ptrs, r.k_pools[0], r.src, r.dst)
+    for l in range(r.layers):
+        layer_step(r, l)
+
+
+def sync_all(world: int) -> None:
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def events(n: int = 2):
+    return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
+
+
+def measure(r: Rig, args, sample_clocks: bool = True) -> dict:
+    """Device timings of one rig, max over ranks: the whole step as a replayed CUDA graph (value), every
+    layer's attention launch back to back (the roofline's duration), the gather + barrier of every layer alone
+    (several GPUs), and the block copy alone."""
+    w = r.world
+    for _ in range(args.warmup):  # NCCL communicators, kernel attributes, the workspace
+        full_step(r)
+    sync_all(w)
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph):
+        full_step(r)
+    step_graph.replay()
+    sync_all(w)
+    start, end = events()
+    clocks = ClockSampler(r.dev.index) if sample_clocks else None
+    if clocks:
+        clocks.__enter__()
+    start.record()
+    for _ in range(args.steps):
+        step_graph.replay()
+    end.record()
+    sync_all(w)
+    if clocks:
+        clocks.__exit__(None, None, None)
+    res = {"ms_per_step": max_over_ranks(start.elapsed_time(end), w, r.dev) / args.steps,
+           "clocks": clocks.summary() if clocks else None}
+    del step_graph
+    # every layer's attention launch back to back, nothing between them, bracketed by two events on the
+    # launching stream: with programmatic dependent launch each launch's start hides behind its predecessor's
+    # tail, so the mean is the kernel's own duration
+    b0, b1 = events()
+    sync_all(w)
+    b0.record()
+    for _ in range(args.kernel_steps):
+        for l in range(r.layers):
+            attend(r, l)
+    b1.record()
+    sync_all(w)
+    res["attn_ms"] = max_over_ranks(b0.elapsed_time(b1), w, r.dev) / (args.kernel_steps * r.layers)
+    if w > 1:  # the reduction + all-gather (+ barrier) of every layer alone, replayed from a graph
+        gather_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gather_graph):
+            for l in range(r.layers):
+                gather_step(r, l)
+        gather_graph.replay()
+        g0, g1 = events()
+        sync_all(w)
+        g0.record()
+        for _ in range(args.kernel_steps):
+            gather_graph.replay()
+        g1.record()
+        sync_all(w)
+        res["gather_ms"] = max_over_ranks(g0.elapsed_time(g1), w, r.dev) / (args.kernel_steps * r.layers)
+        del gather_graph
+    if r.copies:
+        c0, c1 = events()
+        sync_all(w)
+        c0.record()
+        for _ in range(3):
+            r.ops.block_copy(r.ptrs, r.k_pools[0], r.src, r.dst)
+        c1.record()
+        sync_all(w)
+        res["copy_ms"] = max_over_ranks(c0.elapsed_time(c1) / 3, w, r.dev)
+    return res
+
+
+def spot_check(r: Rig, sample: list[int]) -> float:
+    """Run the last layer's full step once more and compare `sample` sequences of this rank's heads of the
+    (gathered) output with a plain torch fp32 attention over the same pages, read back from the device.  The
+    pools already hold the step's appended rows (every timed step wrote the same rows).  Returns the max-abs
+    error over ranks; the bar is 2e-2 (bf16)."""
+    last = r.layers - 1
+    if r.copies:
+        r.ops.block_copy(r.ptrs, r.k_pools[0], r.src, r.dst)
+    layer_step(r, last)
+    torch.cuda.synchronize()
+    if r.p2p:
+        got = r.peers.output(last % r.peers.slots, r.n_q)[:, r.qs]
+    elif r.world > 1:
+        got = r.gathered.view(r.world, r.n_q, r.h_l, DH)[r.rank]
+    else:
+        got = r.out_l
+    starts = r.meta_att.query_start_loc
+    err = 0.0
+    group = r.h_l // r.hkv_l
+    for s in sample:
+        c, n, blocks = r.wl.attend_rows[s]
+        length = c + n
+        ids = torch.tensor(blocks[:-(-length // BS)], device=r.dev, dtype=torch.long)
+        kk = r.k_pools[last][ids].reshape(-1, r.hkv_l, DH)[:length].float()  # [L, hkv, Dh]
+        vv = r.v_pools[last][ids].reshape(-1, r.hkv_l, DH)[:length].float()
+        qq = r.q_l[starts[s]:starts[s + 1]].float()  # [n, h, Dh]
+        kh = kk.repeat_interleave(group, dim=1).permute(1, 0, 2)  # [h, L, Dh]
+        vh = vv.repeat_interleave(group, dim=1).permute(1, 0, 2)
+        scores = torch.einsum("nhd,hld->hnl", qq, kh) / math.sqrt(DH)
+        causal = torch.arange(length, device=r.dev)[None, :] <= (length - n + torch.arange(n, device=r.dev))[:, None]
+        scores = scores.masked_fill(~causal[None], float("-inf"))
+        want = torch.einsum("hnl,hld->nhd", torch.softmax(scores, dim=-1), vh)
+        err = max(err, (got[starts[s]:starts[s + 1]].float() - want).abs().max().item())
+    return max_over_ranks(err, r.world, r.dev)
+
+
+def release(r: Rig) -> None:
+    if r.peers is not None:
+        r.peers.close()
+    r.k_pools.clear()
+    r.v_pools.clear()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def workload_summary(r: Rig, t: dict, peak: float, check: float, sample: list[int]) -> dict:
+    """One sub-object of the bench line: the workload's step, attention and (several GPUs) gather figures."""
+    ctx = r.wl.attend_ctx
+    per_rank = kv_bytes(ctx, r.hkv_l)
+    achieved = per_rank / (t["attn_ms"] * 1e-3) / 1e9
+    out = {"workload": f"{r.wl.name}: {r.wl.describe}", "layers": r.layers,
+           "value": round(per_rank * r.layers * r.world / (t["ms_per_step"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+           "ms_per_step": round(t["ms_per_step"], 4), "attention_us_per_rank": round(t["attn_ms"] * 1e3, 2),
+           "roofline_frac_per_rank": round(achieved / peak, 4), "kv_heads_per_rank": r.hkv_l,
+           "attend_rows": len(r.wl.attend_rows), "sum_ctx": int(np.sum(ctx)),
+           "units_per_layer": r.plan.num_units, "shared_units_per_layer": r.plan.num_shared_units,
+           "append": "fused into the attention launch" if r.fused else "separate K1 launch",
+           "spot_check_max_abs": round(check, 5), "spot_check_rows": sample, "spot_check_bar": 2e-2,
+           "spot_check_passed": bool(check <= 2e-2), **{k: v for k, v in r.wl.info.items() if k != "evicted"}}
+    if "gather_ms" in t:
+        out["gather_barrier_us_per_layer"] = round(t["gather_ms"] * 1e3, 2)
+    if r.wl.name == "config 4":  # shared prefix: HBM sees each shared block once per launch
+        unique = r.wl.unique_pages() * BS * 2 * r.hkv_l * DH * 2
+        out["unique_frac_per_rank"] = round(unique / (t["attn_ms"] * 1e-3) / 1e9 / peak, 4)
+    if r.copies:
+        moved = r.copies * 2 * r.layers * BS * r.hkv_l * DH * 2
+        out["block_copy"] = {"pairs": r.copies, "us": round(t["copy_ms"] * 1e3, 2),
+                             "gbs_read_plus_write_per_rank": round(2 * moved / (t["copy_ms"] * 1e-3) / 1e9, 1)}
+    return out
+
+
 def run_ours(args) -> None:
     rank, world, local = dist_env()
     if world != args.gpus:
@@ -392,220 +682,120 @@ def run_ours(args) -> None:
     else:
         wl = WORKLOADS[args.config]()
     layers = args.layers or wl.layers
-    hkv_l, h_l = HKV // world, H // world
-    n_app, n_att = sum(n for _, n, _ in wl.append_rows), len(wl.attend_rows)
-    n_q = sum(n for _, n, _ in wl.attend_rows)  # query tokens (one per decode row; a prefill row has many)
-    nb = wl.num_blocks
+    r = make_rig(args, mlb, sharding, wl, dev, rank, world, layers)
+    peak, peak_kind = measured_peak()
 
-    g = torch.Generator(device=dev).manual_seed(100 + rank)
-    k_pools, v_pools = [], []
-    for _ in range(layers):
-        for pools in (k_pools, v_pools):
-            p = torch.empty(nb, BS, hkv_l, DH, device=dev, dtype=torch.bfloat16)
-            p.normal_(0.0, wl.kv_scale, generator=g)
-            pools.append(p)
-    gq = torch.Generator(device=dev).manual_seed(7)  # the same full q/k/v on every rank
-    q = torch.randn(n_q, H, DH, device=dev, generator=gq).to(torch.bfloat16)
-    k = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
-    v = (torch.randn(n_app, HKV, DH, device=dev, generator=gq) * wl.kv_scale).to(torch.bfloat16)
-    qs, ks = sharding.head_range(rank, world, H), sharding.head_range(rank, world, HKV)
-    q_l, k_l, v_l = q[:, qs], k[:, ks], v[:, ks]
+    t = measure(r, args)
+    ms_per_step = t["ms_per_step"]
+    attn_avg_ms = t["attn_ms"]
 
-    def seqsteps(rows):
-        return [mlb.SeqStep(c, n, b) for c, n, b in rows]
-
-    meta_att = mlb.AttentionMetadata.build(seqsteps(wl.attend_rows), BS, dev)
-    meta_app = meta_att if wl.append_rows is wl.attend_rows else mlb.AttentionMetadata.build(
-        seqsteps(wl.append_rows), BS, dev)
-    if args.no_query_tiles:  # every row on 8-column work units (no host tables: no query tiles, no cascade)
-        plan = ops.plan_attention(meta_att.query_start_loc, meta_att.seq_lens, meta_att.block_tables_i32.shape[1],
-                                  h_l, hkv_l, dev, pages_per_unit=args.pages_per_unit)
-    else:
-        plan = mlb.B200Backend(pages_per_unit=args.pages_per_unit).plan(meta_att, h_l, hkv_l, dev)
-    ws = ops.Workspace()
-    out_l = torch.empty(n_q, h_l, DH, device=dev, dtype=torch.bfloat16)
-    p2p = world > 1 and args.transport == "p2p"
-    gathered = torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None
-    peers = sharding.PeerOutputs(n_q, H, DH, torch.bfloat16, dev) if p2p else None
-    copies = len(wl.copy_src)
-    if copies:
-        ptrs = ops.pool_pointer_table(k_pools + v_pools)
-        src = torch.tensor(wl.copy_src, dtype=torch.int32, device=dev)
-        dst = torch.tensor(wl.copy_dst, dtype=torch.int32, device=dev)
-    # the append rides in the attention launch when every written block is private to its row (the backend's
-    # rule: B200Backend.forward); otherwise K1 runs first
-    fused = (not args.no_fused_append and meta_app is meta_att and meta_att.append_private
-             and ops.can_fuse_append(plan, k_pools[0], k_l, v_l))
-    append = (k_l, v_l, meta_app.slot_mapping) if fused else None
-    # [append,] attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
-    # [+ p2p barrier]
-    launches_per_layer = ((1 if fused else 2) + (1 if plan.num_shared_units else 0)
-                          + (1 if plan.num_partial_rows or p2p else 0) + (1 if p2p else 0))
-
-    def attend(l):
-        slot = l % peers.slots if p2p else 0
-        ops.attention_partials(q_l, k_pools[l], v_pools[l], meta_att.block_tables_i32, meta_att.seq_lens_i32,
-                               meta_att.qo_indptr, plan, ws, out_l,
-                               targets=peers.local_targets(slot, qs.start) if p2p else None, append=append)
-
-    def layer_step(l, ev=None):
-        if not fused:
-            ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
-        if ev is not None:
-            ev[0].record()
-        attend(l)
-        if ev is not None:
-            ev[1].record()
-        slot = l % peers.slots if p2p else 0
-        if p2p:  # reduction + every row into every rank's buffer (one launch), then the flag barrier
-            ops.splitk_reduce_gather(plan, ws, peers.targets(slot, qs.start), peers.self_dest, torch.bfloat16, DH, dev)
-            peers.barrier()
-        else:
-            ops.splitk_reduce(plan, ws, out_l)
-        if world > 1 and not p2p:
-            import torch.distributed as dist
-
-            dist.all_gather_into_tensor(gathered, out_l)
-
-    def full_step():
-        if copies:  # COW / compaction: one launch over every layer's K and V pools
-            ops.block_copy(ptrs, k_pools[0], src, dst)
-        for l in range(layers):
-            layer_step(l)
-
-    def barrier():
-        torch.cuda.synchronize()
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # --- warm-up (eager): NCCL communicators, kernel attributes, the workspace
-    for _ in range(args.warmup):
-        full_step()
-    barrier()
-
-    # --- value: the whole step (block copies, then every layer's append, attention, reduction [, all-gather])
-    # as one CUDA graph, replayed; device time between events, max over ranks.  A decode step is what
-    # serving engines capture in a graph, and it keeps the device time from hiding behind Python launches.
-    step_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(step_graph):
-        full_step()
-    step_graph.replay()
-    barrier()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            step_graph.replay()
-        end.record()
-        barrier()
-    ms_per_step = max_over_ranks(start.elapsed_time(end), world, dev) / args.steps
-
-    # --- roofline of the dominant kernel: every attention launch of eager steps bracketed by events on the
-    # launching stream
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(layers)]
-           for _ in range(args.kernel_steps)]
-    barrier()
+    # --- the older per-launch figure: events around each attention launch inside eager steps (they also hold
+    # the launch latency an event between two kernels exposes)
+    evs = [[events() for _ in range(layers)] for _ in range(args.kernel_steps)]
+    sync_all(world)
     for s in range(args.kernel_steps):
         for l in range(layers):
-            layer_step(l, evs[s][l])
-    barrier()
-    attn_launch_ms = max_over_ranks(statistics.mean(e0.elapsed_time(e1) for st in evs for e0, e1 in st), world,
-                                    dev)
-    # the same attention launches back to back, every layer's, nothing between them, bracketed by two events on
-    # the launching stream: each launch's start latency hides behind its predecessor's tail (programmatic
-    # dependent launch), so the mean is the kernel's own duration.  The per-launch events above also hold the
-    # launch latency they expose (an event between two kernels ends their programmatic overlap).
-    b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    b0.record()
-    for _ in range(args.kernel_steps):
-        for l in range(layers):
-            attend(l)
-    b1.record()
-    barrier()
-    attn_avg_ms = max_over_ranks(b0.elapsed_time(b1), world, dev) / (args.kernel_steps * layers)
-
-    # --- the block copy alone (COW / compaction bytes moved)
-    copy_ms = None
-    if copies:
-        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        c0.record()
-        for _ in range(3):
-            ops.block_copy(ptrs, k_pools[0], src, dst)
-        c1.record()
-        barrier()
-        copy_ms = max_over_ranks(c0.elapsed_time(c1) / 3, world, dev)
+            layer_step(r, l, evs[s][l])
+    sync_all(world)
+    attn_launch_ms = max_over_ranks(statistics.mean(e0.elapsed_time(e1) for st in evs for e0, e1 in st), world, dev)
 
     # --- append kernel alone (append GB/s): K1 over the layer pools, captured in a CUDA graph so the
     # launch-bound kernel is timed on the device, not behind the Python launch path
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
         for l in range(layers):
-            ops.kv_append(k_pools[l], v_pools[l], meta_app.slot_mapping, k_l, v_l)
+            ops.kv_append(r.k_pools[l], r.v_pools[l], r.meta_app.slot_mapping, r.k_l, r.v_l)
     graph.replay()
-    ap_s, ap_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
+    ap_s, ap_e = events()
+    sync_all(world)
     reps = 20
     ap_s.record()
     for _ in range(reps):
         graph.replay()
     ap_e.record()
-    barrier()
-    del graph, step_graph  # graphs holding NCCL work go before the process group
-    if p2p:  # the kernels' NVLink stores must have assembled exactly what an NCCL all-gather does
+    sync_all(world)
+    del graph
+    append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
+    append_bytes = 2 * 2 * r.n_app * r.hkv_l * DH * 2  # K and V rows read + written, bf16
+    if r.p2p:  # the kernels' NVLink stores must have assembled exactly what an NCCL all-gather does
         import torch.distributed as dist
 
-        peers.raise_errors()
+        r.peers.raise_errors()
         last = layers - 1
-        got = peers.output(last % peers.slots, n_q).clone()
-        ops.attention_partials(q_l, k_pools[last], v_pools[last], meta_att.block_tables_i32, meta_att.seq_lens_i32,
-                               meta_att.qo_indptr, plan, ws, out_l)
-        ops.splitk_reduce(plan, ws, out_l)
-        flat = torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16)
-        dist.all_gather_into_tensor(flat, out_l)
-        want = flat.view(world, n_q, h_l, DH).movedim(0, 1).reshape(n_q, H, DH)
+        got = r.peers.output(last % r.peers.slots, r.n_q).clone()
+        ops.attention_partials(r.q_l, r.k_pools[last], r.v_pools[last], r.meta_att.block_tables_i32,
+                               r.meta_att.seq_lens_i32, r.meta_att.qo_indptr, r.plan, r.ws, r.out_l)
+        ops.splitk_reduce(r.plan, r.ws, r.out_l)
+        flat = torch.empty(world * r.n_q, r.h_l, DH, device=dev, dtype=torch.bfloat16)
+        dist.all_gather_into_tensor(flat, r.out_l)
+        want = flat.view(world, r.n_q, r.h_l, DH).movedim(0, 1).reshape(r.n_q, H, DH)
         if not torch.equal(got, want):
             raise SystemExit(f"rank {rank}: p2p-gathered output differs from the NCCL all-gather")
         del got, want, flat
-    append_ms = max_over_ranks(ap_s.elapsed_time(ap_e) / (reps * layers), world, dev)
-    append_bytes = 2 * 2 * n_app * hkv_l * DH * 2  # K and V rows read + written, bf16
+    sample = [0, len(wl.attend_rows) // 2, len(wl.attend_rows) - 1]
+    check = spot_check(r, sample)
 
-    # --- optional GPU comparison: FlashInfer's paged decode on the same pools, called as the reference's
-    # FlashInfer backend calls it (attention/flashinfer_backend.py:48-58: NHD, plan once, run per layer)
+    # --- GPU comparison: FlashInfer's paged decode on the same pools, called as the reference's FlashInfer
+    # backend calls it (attention/flashinfer_backend.py:48-58: NHD, plan once, run per layer)
     flashinfer = None
-    if args.flashinfer and world == 1:
-        flashinfer = run_flashinfer(meta_att, q, k_pools, v_pools, wl.attend_ctx, layers, args.kernel_steps, dev)
+    if world == 1 and args.config == 2 and not args.no_flashinfer:
+        flashinfer = run_flashinfer(r.meta_att, r.q, r.k_pools, r.v_pools, wl.attend_ctx, layers, args.kernel_steps,
+                                    dev, r.out_l, attn_avg_ms)
 
     # --- end to end through the public API with host buffers (metadata build + H2D in, D2H out)
-    e2e = None
+    e2e = e2e_ref = None
     if not args.no_e2e and args.config == 2:
-        e2e = run_e2e(args, mlb, sharding, seqsteps(wl.attend_rows), q, k, v, k_pools, v_pools, dev, world,
-                      wl.attend_ctx)
+        e2e = run_e2e(args, mlb, sharding, wl, r.q_l, r.k_l, r.v_l, r.k_pools, r.v_pools, dev, world)
+        if world == 1 and not args.no_reference_meta:  # the same loop with the reference's metadata object
+            e2e_ref = run_e2e(args, mlb, sharding, wl, r.q_l, r.k_l, r.v_l, r.k_pools, r.v_pools, dev, world,
+                              reference_meta=True)
 
     ctx = wl.attend_ctx
-    bytes_rank_layer = kv_bytes(ctx, hkv_l)
+    bytes_rank_layer = kv_bytes(ctx, r.hkv_l)
     value = bytes_rank_layer * layers * world / (ms_per_step * 1e-3) / 1e9
-    peak, peak_kind = measured_peak()
     achieved = bytes_rank_layer / (attn_avg_ms * 1e-3) / 1e9
+    headline = {"gather_ms": t.get("gather_ms"), "copy_ms": t.get("copy_ms")}
+    launches = r.launches_per_layer * layers * args.steps + (args.steps if r.copies else 0)
+    fused, plan, n_q, n_app, copies = r.fused, r.plan, r.n_q, r.n_app, r.copies
+    release(r)
+    del r
+
+    # --- the other BASELINE configs (one GPU) and strong KV-head sharding (several GPUs), one rig at a time
+    extra = {}
+    if world == 1 and args.config == 2 and not args.no_configs:
+        for c in (3, 4, 5):
+            cwl = WORKLOADS[c]()
+            cr = make_rig(args, mlb, sharding, cwl, dev, rank, world, cwl.layers)
+            ct = measure(cr, args, sample_clocks=False)
+            cs = [0, len(cwl.attend_rows) - 1]
+            extra[f"config_{c}"] = workload_summary(cr, ct, peak, spot_check(cr, cs), cs)
+            release(cr)
+            del cr
+    if world > 1 and args.config == 2 and not args.no_strong:
+        for name, swl in (("config_2_batch_64", config2(args.batch)), ("config_5", config5())):
+            sr = make_rig(args, mlb, sharding, swl, dev, rank, world, swl.layers)
+            st = measure(sr, args, sample_clocks=False)
+            ss = [0, len(swl.attend_rows) - 1]
+            extra[name] = workload_summary(sr, st, peak, spot_check(sr, ss), ss)
+            release(sr)
+            del sr
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == 2:
         torch.set_num_threads(os.cpu_count() or 1)
         cpu = run_cpu_baseline(wl, args.cpu_sample_seqs, reps=args.cpu_reps)
 
     if rank == 0:
+        p2p = world > 1 and args.transport == "p2p"
         line = {
             "metric": METRIC if args.config == 2 else f"{wl.name}: paged decode attn KV-read GB/s (step incl. "
                                                         f"appends{' and block copies' if copies else ''})",
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "weak" if weak else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "attend_rows": n_att,
-                       "query_tokens": n_q,
-                       "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)), "pool_blocks": nb,
+            "config": {"workload": f"{wl.name}: {wl.describe}", "layers": layers, "attend_rows": len(wl.attend_rows),
+                       "query_tokens": n_q, "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)),
+                       "pool_blocks": wl.num_blocks,
                        "parallelism": (f"kv-head shard x{world}, output gather: "
                                        + ("kernel NVLink stores + flag barrier" if p2p else "NCCL all-gather"))
                                       if world > 1 else "single GPU",
@@ -615,9 +805,9 @@ def run_ours(args) -> None:
                        "shared_prefix_kernel": "mma.sync" if args.no_tc_prefix else "tcgen05",
                        "shared_prefix_beside_per_sequence_kernel": not args.serial_prefix,
                        "pages_per_unit": args.pages_per_unit,
-                       "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * hkv_l,
+                       "units_per_layer": plan.num_units, "ctas_per_layer": plan.num_units * (HKV // world),
                        "partial_rows": plan.num_partial_rows, **wl.info},
-            "seqs_per_s": round(n_att / (ms_per_step * 1e-3 / layers), 1),
+            "seqs_per_s": round(len(wl.attend_rows) / (ms_per_step * 1e-3 / layers), 1),
             "append_gbs": round(append_bytes / (append_ms * 1e-3) / 1e9, 2),  # K1 alone (graph of its launches)
             "append_us": round(append_ms * 1e3, 2),
             "attention_us": round(attn_avg_ms * 1e3, 2),  # back-to-back launches (the roofline's duration)
@@ -627,64 +817,76 @@ def run_ours(args) -> None:
                          "traffic": profiled_traffic() if args.config == 2 and world == 1 else None,
                          "algorithmic_bytes": bytes_rank_layer,
                          "kernel": "paged_attn_mma_kernel<bf16, Dh 128, 2 slots, 4 warps>"},
-            "gpu_launches": launches_per_layer * layers * args.steps + (args.steps if copies else 0),
+            "spot_check_max_abs": round(check, 5), "spot_check_passed": bool(check <= 2e-2),
+            "gpu_launches": launches,
             "timing": "value: CUDA-graph replays of the step; roofline: every layer's attention launch back to back "
                       "between two CUDA events (mean per launch); attention_us_single_launch_events: events around "
                       "each launch inside eager steps",
-            "clocks": clocks.summary(),
+            "clocks": t["clocks"],
         }
-        if args.config == 4:  # shared prefix: HBM sees each shared block once per launch
-            unique = wl.unique_pages() * BS * 2 * hkv_l * DH * 2
+        if world > 1:
+            line["roofline"]["traffic_note"] = ("DRAM traffic is captured with ncu on one GPU (config 2, N=1); not "
+                                                "captured per rank at N>1")
+            line["gather_barrier_us_per_layer"] = round(headline["gather_ms"] * 1e3, 2)
+        if args.config == 4:
+            unique = wl.unique_pages() * BS * 2 * (HKV // world) * DH * 2
             line["roofline"]["unique_bytes"] = unique
             line["roofline"]["unique_gbs"] = round(unique / (attn_avg_ms * 1e-3) / 1e9, 1)
             line["roofline"]["unique_frac"] = round(unique / (attn_avg_ms * 1e-3) / 1e9 / peak, 4)
         if copies:
-            moved = copies * 2 * layers * BS * hkv_l * DH * 2  # blocks x (K, V) x layers, each read and written
-            line["block_copy"] = {"pairs": copies, "us": round(copy_ms * 1e3, 2),
-                                  "gbs_read_plus_write": round(2 * moved / (copy_ms * 1e-3) / 1e9, 1)}
+            moved = copies * 2 * layers * BS * (HKV // world) * DH * 2
+            line["block_copy"] = {"pairs": copies, "us": round(headline["copy_ms"] * 1e3, 2),
+                                  "gbs_read_plus_write": round(2 * moved / (headline["copy_ms"] * 1e-3) / 1e9, 1)}
         if e2e:
             line["e2e"] = e2e
+        if e2e_ref:
+            line["e2e_reference_metadata"] = e2e_ref
         if flashinfer:
             line["flashinfer_decode"] = flashinfer
+        if world == 1 and extra:
+            line["configs"] = extra
+        if world > 1 and extra:
+            line["strong"] = extra
         if cpu:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
-        if peers is not None:
-            peers.close()
         dist.barrier()
         dist.destroy_process_group()
 
 
-def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ctx) -> dict:
-    """Each step, through the public API with pinned host buffers: AttentionMetadata.build and the backend's
-    plan (their own H2D copies, issued on the loader stream ahead of the inputs); the q/k/v rows of every
-    layer copied host-to-device on the loader stream in 4 growing chunks
-    (layers [0,1), [1,3), [3,8), [8,L): each lands while the layers before it compute); per layer the
-    backend's forward once its chunk is in, and a device-to-host copy of its output on a copier stream
-    (layer l's read-back overlaps layer l + 1's attention); the step ends when the last output is on the
-    host.  One GPU: the outputs go into one step-wide device buffer (forward's out_targets) and come back
-    in 4 chunks.  Several GPUs: each rank holds and uploads only its own heads of q/k/v (as a column-parallel
-    QKV projection leaves them) and calls KVHeadShardedBackend.forward_local; it reads back its own heads of
-    the gathered output, so the job reads the whole result back once."""
+def run_e2e(args, mlb, sharding, wl: Workload, q, k, v, k_pools, v_pools, dev, world,
+            reference_meta: bool = False) -> dict:
+    """Each step, through the public API with pinned host buffers: the step's metadata
+    (AttentionMetadata.build_arrays from the engine's block-table arrays) and the backend's plan, with their
+    own H2D copies, issued on the loader stream ahead of the inputs; the q/k/v rows of every layer copied
+    host-to-device on the loader stream in 4 growing chunks (layers [0,1), [1,3), [3,8), [8,L): each lands
+    while the layers before it compute); per layer the backend's forward once its chunk is in; the outputs
+    read back device-to-host on a copier stream in 4 chunks; the step ends when the last output is on the
+    host.  Inputs, outputs and metadata are double-buffered, so step n + 1's uploads run while step n
+    computes.  One GPU: the outputs go into a step-wide device buffer (forward's out_targets).  Several GPUs:
+    each rank holds and uploads only its own heads (q [N, H/n, Dh], k / v [N, Hkv/n, Dh], as a column-parallel
+    QKV projection leaves them), calls KVHeadShardedBackend.forward_local and reads back its own heads of the
+    gathered output, so the job reads the whole result back once.
+    reference_meta: hand the backend an object with only the reference's AttentionMetadata fields (what an
+    unmodified reference engine passes), so it derives the host tables itself (one device-to-host copy and
+    host synchronisation per step)."""
     layers = len(k_pools)
     rank = 0
     if world > 1:
         import torch.distributed as dist
 
         rank = dist.get_rank()
-        qs, ks = sharding.head_range(rank, world, q.shape[1]), sharding.head_range(rank, world, k.shape[1])
-        q, k, v = q[:, qs].contiguous(), k[:, ks].contiguous(), v[:, ks].contiguous()
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()  # this rank's heads
     n_rows, h_full = q.shape[0], q.shape[1] * world
     sizes = [t.numel() * t.element_size() for t in (q, k, v)]
     per_layer = sum(sizes)
     host_in = torch.empty(layers * per_layer, dtype=torch.uint8).pin_memory()
     direct = world == 1
-    # one GPU: inputs, outputs and each step's metadata are double-buffered, so step n + 1's uploads (and its
-    # metadata and plan) run while step n computes; several GPUs: one set, each step waits for the last
-    nbuf = 2 if direct else 1
+    p2p_ring = world > 1 and args.transport == "p2p"
+    nbuf = 2
     dev_in = [torch.empty(layers * per_layer, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
 
     def views(buf, l):
@@ -698,27 +900,28 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         for dst, src in zip(views(host_in, l), (q, k, v)):
             dst.copy_(src.cpu())
     dev_views = [[views(dev_in[b], l) for l in range(layers)] for b in range(nbuf)]
-    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(layers)]  # this rank's heads
-    p2p_ring = world > 1 and args.transport == "p2p"
-    # p2p: one gathered-output slot per layer and step, two steps' worth, so a step's outputs are read back
-    # in chunks and no peer rewrites a slot before its read-back (two steps later, after a step-end join)
+    # the engine's block tables as arrays (AttentionMetadata.build_arrays skips the per-list conversion)
+    rows = wl.attend_rows
+    arrays = (np.array([c for c, _, _ in rows], dtype=np.int64), np.array([n for _, n, _ in rows], dtype=np.int64),
+              np.concatenate([np.asarray(b, dtype=np.int64) for _, _, b in rows]),
+              np.array([len(b) for _, _, b in rows], dtype=np.int64))
+    fields = importlib.import_module(PACKAGE + ".attention.metadata").REFERENCE_FIELDS
     inner_backend = mlb.B200Backend(pages_per_unit=args.pages_per_unit)
+    # p2p: one gathered-output slot per layer and step, two steps' worth: step n writes slots of parity n % 2
     backend = (sharding.KVHeadShardedBackend(inner_backend, transport=args.transport,
                                              slots=2 * layers if p2p_ring else 2)
                if world > 1 else inner_backend)
-    # one GPU: forward(out_targets=...) writes each layer's rows into one step-wide device buffer; p2p: the
-    # step's run of slots; either way read back in 4 shrinking chunks (a side-stream copy per layer costs
-    # ~60 us of host time: 32 per step made the step host-bound)
+    # outputs come back in 4 shrinking chunks (a side-stream copy per layer costs ~60 us of host time: 32 per
+    # step made the step host-bound)
     o_edges = sorted({0, layers} | {b for b in (layers // 2, layers - 4, layers - 1) if 0 < b < layers})
     o_chunks = list(zip(o_edges[:-1], o_edges[1:]))
     o_last = {hi - 1: (lo, hi) for lo, hi in o_chunks}
+    host_out = [torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory() for _ in range(nbuf)]
     if direct:
         dev_out = [torch.empty((layers, *q.shape), dtype=q.dtype, device=dev) for _ in range(nbuf)]
-        host_out = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
         targets = [[mlb.ops.out_targets([dev_out[b][l].data_ptr()], 0, q.shape[1] * q.shape[2], q.shape[2])
                     for l in range(layers)] for b in range(nbuf)]
-    host_ring = None  # p2p: pinned bytes for one step's slots (allocated once the slots exist)
-    state = {"step": 0}
+    state = {"step": 0, "host_ms": 0.0}
     compute = torch.cuda.current_stream(dev)
     loader, copier = torch.cuda.Stream(dev), torch.cuda.Stream(dev)  # H2D of inputs, D2H of outputs
     # chunk boundaries: layer 0's inputs alone, then chunks that land while the layers before them compute
@@ -726,76 +929,71 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     chunks = list(zip(edges[:-1], edges[1:]))
     chunk_of = {lo: c for c, (lo, _) in enumerate(chunks)}
     loaded = [torch.cuda.Event() for _ in chunks]  # inputs of a chunk of layers on the device
-    done = [torch.cuda.Event() for _ in range(layers)]  # output l read back
     ready = [torch.cuda.Event() for _ in range(layers)]  # output l computed
     comp_done = [torch.cuda.Event() for _ in range(nbuf)]  # the last step on buffer b has finished computing
-    io_done = [torch.cuda.Event() for _ in range(nbuf)]  # ... and its outputs are on the host (one GPU)
+    io_done = [torch.cuda.Event() for _ in range(nbuf)]  # ... and its outputs are on the host
     for ev in comp_done + io_done:
         ev.record(compute)
     metas = [None] * nbuf  # each buffer's metadata, alive until the buffer's next turn
-
     inner = backend.inner if world > 1 else backend
     h_l, hkv_l = q.shape[1], k_pools[0].shape[2]
     own = slice(rank * h_l, (rank + 1) * h_l)  # this rank's query heads in the gathered output
 
     def step():
         b = state["step"] % nbuf
+        prev = (state["step"] - 1) % nbuf
         loader.wait_event(comp_done[b])  # the last step on buffer b has read its inputs, metadata and plan
+        t0 = time.perf_counter()
         with torch.cuda.stream(loader):
             # the step's metadata and plan go first in the loader's queue: on the compute stream their small
             # host-to-device copies queued behind the loader's input chunks (a measured ~0.48 ms at every
             # step start); layer 0 waits for the first chunk, so for them too
-            meta = mlb.AttentionMetadata.build(seqs, BS, dev)
+            meta = mlb.AttentionMetadata.build_arrays(*arrays, BS, dev)
+            if reference_meta:
+                meta = types.SimpleNamespace(**{f: getattr(meta, f) for f in fields})
             inner.plan(meta, h_l, hkv_l, dev, q.dtype)
             for c, (lo, hi) in enumerate(chunks):  # then the q/k/v rows in a few growing chunks
                 dev_in[b][lo * per_layer:hi * per_layer].copy_(host_in[lo * per_layer:hi * per_layer],
                                                                non_blocking=True)
                 loaded[c].record(loader)
+        state["host_ms"] += (time.perf_counter() - t0) * 1e3
         metas[b] = meta  # the device tensors it holds (and the plan's) stay unreused until comp_done[b]
-        if direct:
-            compute.wait_event(io_done[b])  # buffer b's outputs of two steps back have been read back
-        nonlocal host_ring
-        base = (state["step"] % 2) * layers  # this step's first slot of the p2p ring
+        compute.wait_event(io_done[b])  # buffer b's outputs of two steps back have been read back
         state["step"] += 1
         for l in range(layers):
             if l in chunk_of:
                 compute.wait_event(loaded[chunk_of[l]])
+            if p2p_ring and l == layers - 1:
+                # the peers rewrite this rank's slots of the previous step's parity during the next step, which
+                # none of them starts before this layer's barrier: the previous read-back must be done by then
+                compute.wait_event(io_done[prev])
             qd, kd, vd = dev_views[b][l]
-            if p2p_ring:
-                backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot base + l
-                if l in o_last:  # a chunk of layers is complete: read this rank's heads back on the side stream
-                    lo, hi = o_last[l]
-                    peers = backend.peers
-                    if host_ring is None:
-                        host_ring = torch.empty((layers, *q.shape), dtype=q.dtype).pin_memory()
-                    ready[l].record(compute)
-                    copier.wait_event(ready[l])
-                    with torch.cuda.stream(copier):
-                        nbytes = n_rows * h_full * q.shape[2] * q.element_size()  # a slot's rows (no padding)
-                        rows = peers.slot_bytes_view(base + lo, base + hi).view(hi - lo, peers.slot_bytes)
-                        rows = rows[:, :nbytes].view(q.dtype).view(hi - lo, n_rows, h_full, q.shape[2])[:, :, own]
-                        host_ring[lo:hi].copy_(rows, non_blocking=True)
-                continue
             if direct:
                 backend.forward(qd, kd, vd, k_pools[l], v_pools[l], meta, out_targets=targets[b][l])
-                if l in o_last:  # a chunk of layers is complete: read it back on the side stream
-                    lo, hi = o_last[l]
-                    ready[l].record(compute)
-                    copier.wait_event(ready[l])
-                    with torch.cuda.stream(copier):
-                        host_out[lo:hi].copy_(dev_out[b][lo:hi], non_blocking=True)
+            elif p2p_ring:
+                backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # lands in slot b * layers + l
+            else:
+                out = backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh tensor
+                ready[l].record(compute)
+                copier.wait_event(ready[l])
+                with torch.cuda.stream(copier):
+                    host_out[b][l].copy_(out[:, own], non_blocking=True)
+                out.record_stream(copier)  # from torch's allocator: keep it alive until the copy ran
                 continue
-            out = backend.forward_local(qd, kd, vd, k_pools[l], v_pools[l], meta)  # NCCL: a fresh gathered one
-            ready[l].record(compute)
-            copier.wait_event(ready[l])
-            with torch.cuda.stream(copier):
-                outs[l].copy_(out[:, own], non_blocking=True)
-                done[l].record(copier)
-            out.record_stream(copier)  # from torch's allocator: keep it alive until the copy ran
-        if direct:
-            io_done[b].record(copier)
-        else:
-            compute.wait_stream(copier)
+            if l in o_last:  # a chunk of layers is complete: read it back on the side stream
+                lo, hi = o_last[l]
+                ready[l].record(compute)
+                copier.wait_event(ready[l])
+                with torch.cuda.stream(copier):
+                    if direct:
+                        host_out[b][lo:hi].copy_(dev_out[b][lo:hi], non_blocking=True)
+                    else:
+                        peers = backend.peers
+                        nbytes = n_rows * h_full * q.shape[2] * q.element_size()  # a slot's rows (no padding)
+                        raw = peers.slot_bytes_view(b * layers + lo, b * layers + hi).view(hi - lo, peers.slot_bytes)
+                        got = raw[:, :nbytes].view(q.dtype).view(hi - lo, n_rows, h_full, q.shape[2])[:, :, own]
+                        host_out[b][lo:hi].copy_(got, non_blocking=True)
+        io_done[b].record(copier)
         comp_done[b].record(compute)
 
     # warm-up as long as a timed window (and no synchronisation inside it): the host runs ahead of the device
@@ -812,6 +1010,7 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
     # when the host stalls (other jobs on the machine), and one stall must not stand for the path
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     windows = []
+    state["host_ms"] = 0.0
     for _ in range(3):
         s.record()
         for _ in range(args.steps):
@@ -821,38 +1020,55 @@ def run_e2e(args, mlb, sharding, seqs, q, k, v, k_pools, v_pools, dev, world, ct
         torch.cuda.synchronize()
         windows.append(max_over_ranks(s.elapsed_time(e), world, dev) / args.steps)
     ms = statistics.median(windows)
+    host_build_ms = max_over_ranks(state["host_ms"] / (3 * args.steps), world, dev)
     d2h = layers * q.numel() * q.element_size()  # bytes read back (this rank's heads on several GPUs)
     if world > 1:
         backend.close()
-    total = kv_bytes(ctx, HKV) * layers
-    meta_bytes = _meta_bytes(mlb, seqs)
-    h2d = layers * per_layer + meta_bytes
+    total = kv_bytes(wl.attend_ctx, HKV) * layers
+    p = inner._plan
+    plan_bytes = sum(a.nbytes for a in (p.units_host, p.shared_host, p.members_host, p.reduce_rows_host,
+                                        p.reduce_chunks_host))
+    h2d = layers * per_layer + _meta_upload_bytes(arrays) + plan_bytes
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "window_ms_per_step": [round(w, 4) for w in windows],
+            "host_build_plan_ms_per_step": round(host_build_ms, 3),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "metadata": ("reference-shaped object (the reference's AttentionMetadata fields only): host tables "
+                         "derived by the backend" if reference_meta else "AttentionMetadata.build_arrays"),
             "path": (f"KVHeadShardedBackend(transport={args.transport!r}).forward_local" if world > 1
                      else "B200Backend.forward")
-                    + " per layer; pinned host I/O on side streams: H2D of the step's q/k/v in 4 chunks, "
-                      "D2H of the outputs " + ("in 4 chunks" if direct or p2p_ring else "per layer")
+                    + " per layer; pinned host I/O on side streams, double-buffered: H2D of the step's q/k/v in 4 "
+                      "chunks, D2H of the outputs " + ("in 4 chunks" if direct or p2p_ring else "per layer")
                     + ("; each rank uploads and reads back its own heads" if world > 1 else "")}
 
 
-def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:
-    """FlashInfer BatchDecodeWithPagedKVCacheWrapper on the same pages (the reference's CUDA backend)."""
+def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev, ours_out, ours_ms) -> dict:
+    """FlashInfer BatchDecodeWithPagedKVCacheWrapper on the same pages, called as the reference's FlashInfer
+    backend calls it (attention/flashinfer_backend.py:48-58): the reference's CUDA path, timed per launch with
+    events, beside this build's attention on the same pools; its last layer's output is compared with ours."""
     try:
         import flashinfer
     except ImportError as e:
         return {"unavailable": f"flashinfer not importable: {e}"}
+    try:
+        return _time_flashinfer(flashinfer, meta, q, k_pools, v_pools, ctx, layers, steps, dev, ours_out, ours_ms)
+    except Exception as e:  # a JIT build or plan failure of the library: reported, not fatal to the bench
+        return {"unavailable": f"flashinfer {flashinfer.__version__}: {type(e).__name__}: {str(e)[:200]}"}
+
+
+def _time_flashinfer(flashinfer, meta, q, k_pools, v_pools, ctx, layers, steps, dev, ours_out, ours_ms) -> dict:
+    t0 = time.perf_counter()
     ws = torch.empty(128 * 2**20, dtype=torch.uint8, device=dev)
     w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(ws, kv_layout="NHD")
     w.plan(meta.kv_indptr, meta.kv_indices, meta.kv_last_page_len, H, HKV, DH, BS, pos_encoding_mode="NONE",
            q_data_type=q.dtype, kv_data_type=k_pools[0].dtype)
     out = w.run(q, (k_pools[0], v_pools[0]))
     torch.cuda.synchronize()
+    setup_s = time.perf_counter() - t0
     evs = []
     for _ in range(steps):
         for l in range(layers):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0, e1 = events()
             e0.record()
             w.run(q, (k_pools[l], v_pools[l]), out=out)
             e1.record()
@@ -860,15 +1076,19 @@ def run_flashinfer(meta, q, k_pools, v_pools, ctx, layers, steps, dev) -> dict:
     torch.cuda.synchronize()
     us = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs) * 1e3
     nbytes = kv_bytes(ctx, HKV)
+    diff = (out.float() - ours_out.float()).abs().max().item()  # out holds the last layer's output
     return {"attention_us": round(us, 2), "gbs": round(nbytes / us / 1e3, 1), "version": flashinfer.__version__,
+            "ours_attention_us": round(ours_ms * 1e3, 2), "flashinfer_over_ours_time": round(us / (ours_ms * 1e3), 3),
+            "max_abs_vs_ours": round(diff, 5), "setup_s": round(setup_s, 1),
+            "timing": "events around each launch (ours: back to back, the roofline's duration)",
             "call": "BatchDecodeWithPagedKVCacheWrapper(NHD).plan(kv_indptr, kv_indices, kv_last_page_len, ...).run"}
 
 
-def _meta_bytes(mlb, seqs) -> int:
-    m = mlb.AttentionMetadata.build(seqs, BS, "cpu")
-    return sum(t.numel() * t.element_size() for t in (m.positions, m.slot_mapping, m.block_tables, m.logits_index,
-                                                      m.qo_indptr, m.seq_lens_i32, m.block_tables_i32, m.kv_indptr,
-                                                      m.kv_indices, m.kv_last_page_len))
+def _meta_upload_bytes(arrays) -> int:
+    """Host-to-device bytes of a step's metadata on the CUDA path: the compact int64 upload that
+    mlb_build_metadata expands (block ids, their offsets and the per-sequence prefix arrays)."""
+    cached, new, ids, nblk = arrays
+    return 8 * (ids.size + 5 * cached.size + 3)
 
 
 def main() -> None:
@@ -889,7 +1109,14 @@ def main() -> None:
     ap.add_argument("--cpu-sample-seqs", type=int, default=16)
     ap.add_argument("--cpu-reps", type=int, default=10)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--flashinfer", action="store_true", help="also time FlashInfer's decode on the same pages")
+    ap.add_argument("--no-flashinfer", action="store_true",
+                    help="N=1, config 2: skip timing FlashInfer's decode (the reference's CUDA backend) on the same pages")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="N=1, config 2: skip the configs 3 / 4 / 5 sub-objects of the line")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="N>1, config 2: skip the strong KV-head sharding sub-objects (config 2 batch 64, config 5)")
+    ap.add_argument("--no-reference-meta", action="store_true",
+                    help="N=1: skip the e2e run with the reference's metadata object")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--attend-chunks", action="store_true",

@@ -110,8 +110,10 @@ typedef struct {
 } mlb_work_unit;
 
 /*
- * Units of query-tile work for the tensor-core kernel (one CTA per (unit, KV head), up to 128 query
- * columns = tokens x query heads of one KV head), of two kinds (reserved[0] & 0xff):
+ * Units of query-tile work for the tensor-core kernel (up to 128 query columns = tokens x query heads of
+ * one KV head each).  They come in PAIRS: units 2i and 2i + 1 cover the same pages of the same table row,
+ * with the same kind and piece, and one tensor-core CTA per (pair, KV head) loads each K / V tile once for
+ * both (member_count 0 marks an empty partner).  num_shared_units is even.  Two kinds (reserved[0] & 0xff):
  * kind 0, a shared prefix (a prefix-cache hit seen by many decode rows): pages [page_begin, page_end) are
  *   the same blocks in the tables of members [member_begin, member_begin + member_count) of the members
  *   array (member_count <= 128 / group), and the table row of sequence `table_seq` holds them.  Each page
@@ -120,7 +122,7 @@ typedef struct {
  * kind 1, a query tile of a multi-token row (a prefill chunk on cache): tokens member_begin ..
  *   member_begin + member_count - 1 (global token indices, member_count <= 128 / group) of sequence
  *   table_seq against its pages [page_begin, page_end), causal (token i of the row sees keys up to its own
- *   position).  piece < 0: the unit covers every key its tokens see and writes the final rows; otherwise
+ *   position; a pair of neighbouring tiles covers the later tile's keys).  piece < 0: the unit covers every key its tokens see and writes the final rows; otherwise
  *   it is piece `piece` of (reserved[0] >> 8) and token m's partial row is
  *   reserved[1] + (m * pieces + piece) * tokens_per_tile.
  */

@@ -2,6 +2,7 @@
 // dispatch to the kernels, and error reporting by status code + mlb_last_error().  No exception and no
 // device allocation crosses or happens behind this boundary.
 #include <algorithm>
+#include <array>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -62,8 +63,8 @@ constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (sh
 constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best)
 constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
-// SM time of one shared-prefix tile (128 query columns x 128 keys) in page-heads streamed by the per-sequence
-// kernel (head_dim 128; measured on config 4: ~2 us per tile per SM against ~0.1 us per 8 KB page-head)
+// SM time of one key tile (128 keys) of a tensor-core CTA, which carries a pair of 128-column query tiles,
+// in page-heads streamed by the per-sequence kernel (head_dim 128; ~0.1 us per 8 KB page-head)
 constexpr int kTilePageHeads = 19;
 constexpr int kMinSharedSmPct = 25;  // the shared-prefix kernel gets at least this share of the SMs
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
@@ -321,9 +322,14 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   // The shared-prefix kernel runs beside the per-sequence kernel, one CTA per SM: it gets the share of the
   // SMs that balances the two kernels' estimated SM time (all of them when no per-sequence work is left)
   int64_t tc_work = 0;
+  // a tensor-core CTA takes a pair of member blocks (two query tiles over the same pages)
+  auto pairs_of = [&](const ShareSet& set) {
+    const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
+    return (blocks + 1) / 2;
+  };
   for (const ShareSet& set : sets)
-    tc_work += (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta * num_kv_heads *
-               ((set.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit) * kTilePageHeads;
+    tc_work += pairs_of(set) * num_kv_heads * ((set.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit) *
+               kTilePageHeads;
   const int64_t priv_work = rest * num_kv_heads;
   const int64_t share_pct =
       tc_work > 0 ? std::max<int64_t>(kMinSharedSmPct, 100 * tc_work / (tc_work + priv_work)) : 100;
@@ -332,11 +338,10 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   };
   std::vector<SetPlan> set_plans;
   for (const ShareSet& set : sets) {
-    const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
     // as many pieces as keep every CTA in one wave of that share, each a whole number of 8-page (128-key)
     // tiles
     const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(num_sms) * kSharedCtasPerSm * share_pct / 100);
-    int64_t pieces = std::max<int64_t>(1, target / (blocks * num_kv_heads));
+    int64_t pieces = std::max<int64_t>(1, target / (pairs_of(set) * num_kv_heads));
     pieces = std::min<int64_t>(pieces, std::max(1, set.pages / kMinPagesPerUnit));
     int per = static_cast<int>((set.pages + pieces - 1) / pieces);
     per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;
@@ -387,39 +392,47 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   }
   // ---- query tiles of the prefill rows (mlb_shared_unit of kind 1): 128 / group consecutive tokens of one
   // sequence over the keys its last token sees (causal), in pieces of <= kPrefillPiecePages pages whose
-  // partial rows are token-major: row(token i, piece p) = part_base + (i * pieces + p) * tpt
-  std::vector<mlb_shared_unit> punits;
+  // partial rows are token-major: row(token i, piece p) = part_base + (i * pieces + p) * tpt.  Neighbouring
+  // tiles go in pairs over the later tile's keys (one tensor-core CTA takes both; the earlier tile's causal
+  // limit masks the few keys it does not see); a row's last odd tile gets an empty partner.
+  std::vector<std::array<mlb_shared_unit, 2>> tile_pairs;
   const int tile_tokens = std::max(1, kSharedColumns / group_size);
   for (int s : prefill_seqs) {
     const int n = qo_indptr[s + 1] - qo_indptr[s], L = seq_lens[s];
-    for (int t0 = 0; t0 < n; t0 += tile_tokens) {
-      const int ntok = std::min(tile_tokens, n - t0);
-      const int key_end = L - n + t0 + ntok;  // keys 0 .. key_end - 1: what the tile's last token sees
+    for (int t0 = 0; t0 < n; t0 += 2 * tile_tokens) {
+      const int ntok[2] = {std::min(tile_tokens, n - t0), std::max(0, std::min(tile_tokens, n - t0 - tile_tokens))};
+      const int key_end = L - n + t0 + ntok[0] + ntok[1];  // keys 0 .. key_end - 1: the pair's last token
       const int pages = (key_end + block_size - 1) / block_size;
       int pieces = std::min(255, std::max(1, (pages + kPrefillPiecePages - 1) / kPrefillPiecePages));
       int per = (pages + pieces - 1) / pieces;
       per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;  // whole 8-page MMA tiles
       pieces = (pages + per - 1) / per;
-      const int64_t part_base = pieces > 1 ? rows : -1;
-      if (pieces > 1) rows += static_cast<int64_t>(ntok) * pieces * tpt;
+      int64_t part_base[2] = {-1, -1};
+      for (int h = 0; h < 2; ++h)
+        if (pieces > 1 && ntok[h] > 0) part_base[h] = rows, rows += static_cast<int64_t>(ntok[h]) * pieces * tpt;
       for (int p = 0; p < pieces; ++p) {
-        mlb_shared_unit u{};
-        u.member_begin = qo_indptr[s] + t0;  // kind 1: the tile's first token
-        u.member_count = ntok;
-        u.page_begin = p * per;
-        u.page_end = std::min(pages, (p + 1) * per);
-        u.piece = pieces > 1 ? p : -1;
-        u.table_seq = s;
-        u.reserved[0] = 1 | (pieces << 8);
-        u.reserved[1] = static_cast<int32_t>(part_base);
-        punits.push_back(u);
+        std::array<mlb_shared_unit, 2> pair{};
+        for (int h = 0; h < 2; ++h) {
+          mlb_shared_unit& u = pair[h];
+          u.member_begin = qo_indptr[s] + t0 + h * tile_tokens;  // kind 1: the tile's first token
+          u.member_count = ntok[h];
+          u.page_begin = p * per;
+          u.page_end = std::min(pages, (p + 1) * per);
+          u.piece = pieces > 1 ? p : -1;
+          u.table_seq = s;
+          u.reserved[0] = 1 | (pieces << 8);
+          u.reserved[1] = static_cast<int32_t>(part_base[h]);
+        }
+        tile_pairs.push_back(pair);
       }
       if (reduce_rows && reduce_chunks)
-        for (int i = 0; i < ntok; ++i) {
-          const int64_t tok = qo_indptr[s] + t0 + i;
-          reduce_rows[tok] = pieces > 1 ? static_cast<int32_t>(part_base + static_cast<int64_t>(i) * pieces * tpt) : -1;
-          reduce_chunks[tok] = pieces;
-        }
+        for (int h = 0; h < 2; ++h)
+          for (int i = 0; i < ntok[h]; ++i) {
+            const int64_t tok = qo_indptr[s] + t0 + h * tile_tokens + i;
+            reduce_rows[tok] =
+                pieces > 1 ? static_cast<int32_t>(part_base[h] + static_cast<int64_t>(i) * pieces * tpt) : -1;
+            reduce_chunks[tok] = pieces;
+          }
     }
   }
   if (rows > INT32_MAX) return fail(MLB_EINVAL, "plan: too many partial rows");
@@ -428,7 +441,10 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
     return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);
   });
 
-  std::vector<mlb_shared_unit> sunits;
+  // shared-prefix units: per piece, the member blocks in pairs (an odd last block gets an empty partner);
+  // every pair of units (2i, 2i + 1) covers the same pages of the same table row, and pairs are ordered
+  // largest first as whole pairs
+  std::vector<std::array<mlb_shared_unit, 2>> pairs;
   std::vector<mlb_share_member> mems;
   for (size_t k = 0; k < sets.size(); ++k) {
     const ShareSet& set = sets[k];
@@ -437,21 +453,28 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
       mems.push_back({s, qo_indptr[s], static_cast<int32_t>(base[seq_group[s]]), 0});
     const int nm = static_cast<int>(set.seqs.size());
     for (int piece = 0; piece < set_plans[k].pieces; ++piece)
-      for (int m = 0; m < nm; m += per_cta) {
-        mlb_shared_unit u{};
-        u.member_begin = first + m;
-        u.member_count = std::min(per_cta, nm - m);
-        u.page_begin = piece * set_plans[k].per;
-        u.page_end = std::min(set.pages, (piece + 1) * set_plans[k].per);
-        u.piece = piece;
-        u.table_seq = set.seqs[0];
-        sunits.push_back(u);
+      for (int m = 0; m < nm; m += 2 * per_cta) {
+        std::array<mlb_shared_unit, 2> pair{};
+        for (int h = 0; h < 2; ++h) {
+          mlb_shared_unit& u = pair[h];
+          u.member_begin = first + std::min(nm, m + h * per_cta);
+          u.member_count = std::max(0, std::min(per_cta, nm - m - h * per_cta));
+          u.page_begin = piece * set_plans[k].per;
+          u.page_end = std::min(set.pages, (piece + 1) * set_plans[k].per);
+          u.piece = piece;
+          u.table_seq = set.seqs[0];
+        }
+        pairs.push_back(pair);
       }
   }
-  sunits.insert(sunits.end(), punits.begin(), punits.end());
-  std::stable_sort(sunits.begin(), sunits.end(), [](const mlb_shared_unit& x, const mlb_shared_unit& y) {
-    return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);  // largest first
-  });
+  pairs.insert(pairs.end(), tile_pairs.begin(), tile_pairs.end());
+  std::stable_sort(pairs.begin(), pairs.end(),
+                   [](const std::array<mlb_shared_unit, 2>& x, const std::array<mlb_shared_unit, 2>& y) {
+                     return (x[0].page_end - x[0].page_begin) > (y[0].page_end - y[0].page_begin);  // largest first
+                   });
+  std::vector<mlb_shared_unit> sunits;
+  sunits.reserve(2 * pairs.size());
+  for (const auto& pair : pairs) sunits.insert(sunits.end(), pair.begin(), pair.end());
   *num_units = static_cast<int64_t>(out.size());
   *num_shared_units = static_cast<int64_t>(sunits.size());
   *num_members = static_cast<int64_t>(mems.size());
@@ -503,6 +526,9 @@ int attention_call(const void* q, int64_t q_stride_tok, int64_t q_stride_head, c
     return rc;
   if (num_shared_units > 0 && (!shared_units || dtype == MLB_F32))  // members: only kind-0 units read them
     return fail(MLB_EINVAL, "paged_attention: query-tile units need their array and a 16-bit pool");
+  if (num_shared_units % 2)
+    return fail(MLB_EINVAL, "paged_attention: query-tile units come in pairs (%lld units)",
+                static_cast<long long>(num_shared_units));
   if (num_partial_rows > 0 && (!partial_o || !partial_lse))
     return fail(MLB_EINVAL, "paged_attention: the plan has %lld partial rows but no workspace",
                 static_cast<long long>(num_partial_rows));

@@ -1,30 +1,37 @@
-// K2s on the 5th-generation tensor cores: shared-prefix (cascade) attention with tcgen05.mma, TMEM
-// accumulators and an mbarrier pipeline.
+// K2s on the 5th-generation tensor cores: shared-prefix (cascade) attention and prefill query tiles with
+// tcgen05.mma, TMEM accumulators and an mbarrier pipeline.
 //
-// A shared unit is a run of prefix pages that every member row's block table holds (same block ids), for
-// up to 128 / group member rows, i.e. up to 128 query columns of one KV head.  That is a small
-// FlashAttention forward: S = Q . K^T over the pages, online softmax, O = P . V, with M = 128 query
-// columns (the TMEM lanes) per CTA and 128 keys (8 pages) per tile.
+// A unit is up to 128 query columns of one KV head over a run of pages: a shared prefix that every member
+// row's block table holds (kind 0, 128 / group member rows, every key visible), or consecutive tokens of one
+// multi-token row (kind 1, causal keys).  That is a small FlashAttention forward: S = Q . K^T over the pages,
+// online softmax, O = P . V, with M = 128 query columns (the TMEM lanes) and 128 keys (8 pages) per tile.
 //
-// Roles in one CTA of 256 threads (1 CTA per SM: ~225 KB of shared memory, all 512 TMEM columns):
+// One CTA takes a PAIR of units over the same pages (the planner makes them: two member blocks of one
+// prefix piece, or two neighbouring tiles of one row over the later tile's keys), so every K / V tile is
+// loaded once for 256 query columns and two softmax warpgroups work side by side: while one exponentiates
+// its tile's scores, the tensor core runs the other tile's products.
+//
+// Roles in one CTA of 384 threads (1 CTA per SM: two Q tiles + 2 (Dh 128) or 4 (Dh 64) K/V stages of shared
+// memory, all 512 TMEM columns):
 // - warps 0, 2, 3: the producers (one lane per page).  Each page of a tile is 2 x Dh/64 TMA boxes (tensor
 //   maps over the K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle), landing in the K-major
-//   layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts the bytes
-//   (expect_tx).  A block id out of range gets a slot coordinate past the pool's end: TMA fills zeros
-//   there and the softmax masks the page.  3 stages.  (16-byte cp.async from 96 threads measured 3.8 us
-//   per 64 KB tile here: too few loads in flight.)
-// - warp 1, one thread: the MMA issuer.  Per tile j: S_j = Q . K_j^T into TMEM buffer j % 2 (K = Dh in
-//   steps of 16), committed to s_full; then O += P_{j-1} . V_{j-1} with P read from TMEM (A operand) and
-//   V as an MN-major B operand (one k-step of 16 keys per loaded page, so pages past the unit's end are
-//   never read), committed to the stage's "empty" barrier and to o_done.  Issuing S_j
-//   before O_{j-1} lets the tensor core compute the next scores while the softmax warps work.
-// - warps 4-7 (a warpgroup; thread = one query column = one TMEM lane): read the S row from TMEM, mask,
-//   running max in the exp2 domain, P = 2^(s - m) packed to 16 bits into TMEM buffer j % 2, row sums in
-//   fp32.  O is rescaled (TMEM load / scale / store) only when a row's max grows by more than 8 (a factor
-//   256 of headroom keeps P and the sums finite), which after the first tiles is rare.  At the end (the
-//   "final" barrier, committed behind the last MMA) every column's normalised O row and log2-sum-exp go
-//   to its split-K partial row, merged by the reduction.
-// TMEM columns: S0 [0,128), S1 [128,256), O [256, 256 + Dh), P0 [384,448), P1 [448,512).
+//   layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts the bytes (expect_tx).
+//   A block id out of range gets a slot coordinate past the pool's end: TMA fills zeros there and the
+//   softmax masks the page.  No multicast.
+// - warp 1, one thread: the MMA issuer.  Per tile j and query tile x (A, then B): O_x += P_x(j) . V_j with
+//   P read from TMEM (A operand) and V as an MN-major B operand (one k-step of 16 keys per loaded page, so
+//   pages past the unit's end are never read), then S_x(j+1) = Q_x . K_{j+1}^T, committed to s_full[x]; the
+//   stage is released (empty) once both products of tile j are issued.
+// - warps 4-7 (tile A) and 8-11 (tile B), one thread = one query column = one TMEM lane: pass 1 reads the S
+//   row from TMEM 32 columns at a time for the masked running max (exp2 domain); pass 2 reads it again and
+//   writes P = 2^(s - m), packed to 16 bits, over the first 64 columns of the same S buffer; row sums in
+//   fp32.  Two passes keep a thread under 168 registers (384 threads on one SM).  O is rescaled (TMEM load /
+//   scale / store) only when a row's max grows by more than 8 (a factor 256 of headroom keeps P and the
+//   sums finite), which after the first tiles is rare; s_full[x] of tile j is committed after P_x(j-1) . V,
+//   so O_x is quiet then.  At the end (the "final" barrier, committed behind the last MMA) every column's
+//   normalised O row and log2-sum-exp go to its split-K partial row, merged by the reduction (an unsplit
+//   query tile stores its final rows).
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B [256 + Dh, 256 + 2 Dh).
 //
 // Every wait is bounded (time and polls); on expiry the CTA raises MLB_DEV_WAIT_TIMEOUT, drains its own
 // copies and MMAs, frees TMEM and returns.
@@ -42,26 +49,32 @@ namespace mlb {
 
 namespace {
 
-constexpr int kTcThreads = 256;
-constexpr int kTcStages = 3;
-constexpr int kTcRows = 128;        // query columns per CTA = MMA M = TMEM lanes
+constexpr int kTcThreads = 384;     // 12 warps: 3 producers, the MMA issuer, two softmax warpgroups
+constexpr int kTcRows = 128;        // query columns per tile = MMA M = TMEM lanes
 constexpr int kTcTileTokens = 128;  // keys per tile = N of S = Q . K^T
 constexpr int kTcTilePages = kTcTileTokens / kBlockSize;
 constexpr int kTcProducerWarps = 3;  // warps 0, 2, 3
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
-__device__ __forceinline__ uint32_t col_s(int b) { return b ? 128u : 0u; }    // S buffers
-__device__ __forceinline__ uint32_t col_p(int b) { return b ? 448u : 384u; }  // P buffers (16-bit pairs)
+// TMEM columns: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B after it; P_x (16-bit pairs) over the
+// first 64 columns of S_x
+__device__ __forceinline__ uint32_t col_s(int x) { return x ? 128u : 0u; }
+template <int DH>
+__device__ __forceinline__ uint32_t col_o(int x) {
+  return 256u + (x ? static_cast<uint32_t>(DH) : 0u);
+}
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
 template <int DH>
 struct TcLayout {
+  static constexpr int kStages = DH == 128 ? 2 : 4;  // K + V stages that fit beside the two Q tiles
   static constexpr int kTileBytes = kTcTileTokens * DH * 2;  // one K or V tile, [DH/64][128][64] swizzled
-  static constexpr int kQBytes = kTcRows * DH * 2;
+  static constexpr int kQBytes = kTcRows * DH * 2;           // one query tile
   static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kBarOffset = kQBytes + kTcStages * kStageBytes;
-  // barriers: full[3], empty[3], s_full[2], p_full[2], o_done, final; then the TMEM base and the abort flag
-  static constexpr int kBytes = kBarOffset + 16 * 8 + 16;
+  static constexpr int kStageOffset = 2 * kQBytes;
+  static constexpr int kBarOffset = kStageOffset + kStages * kStageBytes;
+  // barriers: full[S], empty[S], s_full[2], p_full[2], final, q_ready; then the TMEM base and the abort flag
+  static constexpr int kNumBars = 2 * kStages + 6;
+  static constexpr int kBytes = kBarOffset + 8 * kNumBars + 16;
   static constexpr int kLaunchBytes = kBytes + 1024;  // slack to align the base to 1024 (swizzle atoms)
 };
 
@@ -144,6 +157,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+// 32 lanes x 16 consecutive 32-bit columns
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // The compiler takes a tcgen05.ld's destination registers as written by the ld itself, so arithmetic on them
 // may be scheduled above tcgen05.wait::ld (the wait's memory clobber orders memory, not registers).  This
@@ -192,55 +214,57 @@ template <int DT, int DH>
 __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tk,
                                                                           const __grid_constant__ CUtensorMap tv) {
   using L = TcLayout<DH>;
+  constexpr int NS = L::kStages;
   constexpr int CH = DH * 2 / 16;  // 16-byte chunks per row
   constexpr uint32_t kFmt = DT == MLB_BF16 ? 1u : 0u;
   constexpr uint32_t kIdescS = f16_idesc(kFmt, false, kTcRows, kTcTileTokens);
   constexpr uint32_t kIdescO = f16_idesc(kFmt, true, kTcRows, DH);
+  constexpr float kNegInfF = -__builtin_huge_valf();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* full = bars;
-  uint64_t* empty = bars + 3;
-  uint64_t* s_full = bars + 6;
-  uint64_t* p_full = bars + 8;
-  uint64_t* o_done = bars + 10;
-  uint64_t* final_bar = bars + 11;
-  uint64_t* q_ready = bars + 12;  // the Q tile is in shared memory (arrived by the 128 softmax threads)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 16) + 1;
-  const uint32_t q_smem = smem_u32(smem);
-  const uint32_t stage_smem = q_smem + L::kQBytes;
+  uint64_t* full = bars;                   // [NS] a stage's K and V tiles have landed
+  uint64_t* empty = bars + NS;             // [NS] every MMA reading the stage has completed
+  uint64_t* s_full = bars + 2 * NS;        // [2] S_x of the next tile (and P_x . V of the one before) complete
+  uint64_t* p_full = bars + 2 * NS + 2;    // [2] P_x written into TMEM (128 softmax threads of tile x)
+  uint64_t* final_bar = bars + 2 * NS + 4;  // every MMA of the CTA has completed
+  uint64_t* q_ready = bars + 2 * NS + 5;    // both Q tiles are in shared memory (256 softmax threads)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + L::kNumBars) + 1;
+  const uint32_t q_smem = smem_u32(smem);  // Q_A, then Q_B
+  const uint32_t stage_smem = q_smem + L::kStageOffset;
 
   griddep_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kvh = blockIdx.x % a.hkv;
-  const int4* rec = reinterpret_cast<const int4*>(a.shared_units + blockIdx.x / a.hkv);
-  const int4 x = __ldg(rec), y = __ldg(rec + 1);
-  const int mb = x.x, mc = x.y, pb = x.z, pe = x.w, piece = y.x, tseq = y.y;
+  // the CTA's pair of units: 2 * pair (tile A) and 2 * pair + 1 (tile B) share the page range, the table row
+  // and the kind; a B without members leaves the CTA one tile
+  const int4* rec = reinterpret_cast<const int4*>(a.shared_units + 2 * (blockIdx.x / a.hkv));
+  const int4 xa = __ldg(rec), ya = __ldg(rec + 1), xb = __ldg(rec + 2), yb = __ldg(rec + 3);
+  const int pb = xa.z, pe = xa.w, tseq = ya.y;
   // kind 0: a shared prefix, members mb .. mb + mc - 1 (one decode token each), every key visible.
   // kind 1: a query tile of sequence tseq: mc consecutive tokens from token mb, causal keys.
-  const bool tile_unit = (y.z & 0xff) == 1;
-  const int tile_pieces = y.z >> 8, tile_part_base = y.w;
-  // key position of the tile's first token (kind 1): context length - new tokens + offset in the row
-  const int first_pos = tile_unit ? __ldg(a.seq_lens + tseq) - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) +
-                                        (mb - __ldg(a.qo + tseq))
-                                  : 0;
+  const bool tile_unit = (ya.z & 0xff) == 1;
+  bool two = xb.y > 0;
+  if (two && (xb.z != pb || xb.w != pe || yb.y != tseq || (yb.z & 0xff) != (ya.z & 0xff) || yb.x != ya.x)) {
+    two = false;  // a pair the planner would not make: tile B is left out and the plan flagged
+    if (threadIdx.x == 0) flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+  }
   const int npages = pe - pb;
   const int ntiles = (npages + kTcTilePages - 1) / kTcTilePages;
   const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(full + s, kTcProducerWarps);
       mbar_init(empty + s, 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full + b, 1);
-      mbar_init(p_full + b, 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(s_full + x, 1);
+      mbar_init(p_full + x, 128);
     }
-    mbar_init(o_done, 1);
     mbar_init(final_bar, 1);
-    mbar_init(q_ready, 128);
+    mbar_init(q_ready, 256);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -273,10 +297,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     };
     int bid = load_bid(0);
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j % kTcStages;
-      if (j >= kTcStages) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
+      const int s = j % NS;
+      if (j >= NS) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
         int ok = 1;
-        if (lane == 0) ok = tc_wait(empty + s, ((j / kTcStages) + 1) & 1, abort_flag, a.err) ? 1 : 0;
+        if (lane == 0) ok = tc_wait(empty + s, ((j / NS) + 1) & 1, abort_flag, a.err) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
       }
       const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
@@ -302,109 +326,148 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (one thread)
+    // Per tile j: O_A += P_A(j) . V_j, S_A(j+1) = Q_A . K_{j+1}^T, commit s_full[A]; then the same for B,
+    // with the stage released (empty) once both P . V of tile j are issued.  While softmax A works on its
+    // scores the tensor core runs B's products, and the other way round.  Issued MMAs execute in order, so
+    // S_x(j+1) overwrites the TMEM columns holding P_x(j) only after P_x(j) . V_j has read them.
     if (lane == 0) {
-      const bool have_q = tc_wait(q_ready, 0, abort_flag, a.err);
-      for (int j = 0; have_q && j <= ntiles && !*abort_flag; ++j) {
-        if (j < ntiles) {
-          const int s = j % kTcStages, b = j & 1;
-          if (!tc_wait(full + s, (j / kTcStages) & 1, abort_flag, a.err)) break;
+      auto issue_s = [&](int x, int j) {  // S_x = Q_x . K_j^T (K = Dh in steps of 16)
+        const uint32_t kb = stage_smem + (j % NS) * L::kStageBytes, qx = q_smem + x * L::kQBytes;
+#pragma unroll
+        for (int ks = 0; ks < DH / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
+          umma_ss(tmem + col_s(x), sw128_desc(qx + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
+                  ks > 0 ? 1u : 0u);
+        }
+      };
+      auto issue_pv = [&](int x, int j) {  // O_x += P_x . V_j, one k-step of 16 keys per loaded page
+        const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
+        const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+        for (int ks = 0; ks < live_pages; ++ks)
+          umma_ts(tmem + col_o<DH>(x), tmem + col_s(x) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
+                  kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+      };
+      bool ok = ntiles > 0 && tc_wait(q_ready, 0, abort_flag, a.err) && tc_wait(full, 0, abort_flag, a.err);
+      if (ok) {
+        fence_proxy_async_smem();
+        tc_fence_after();
+        issue_s(0, 0);
+        umma_commit(s_full);
+        if (two) {
+          issue_s(1, 0);
+          umma_commit(s_full + 1);
+        }
+      }
+      for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
+        const bool more = j + 1 < ntiles;
+        if (!tc_wait(p_full, j & 1, abort_flag, a.err)) break;
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!tc_wait(full + (j + 1) % NS, ((j + 1) / NS) & 1, abort_flag, a.err)) break;
           fence_proxy_async_smem();
           tc_fence_after();
-          const uint32_t kb = stage_smem + s * L::kStageBytes;
-#pragma unroll
-          for (int ks = 0; ks < DH / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
-            umma_ss(tmem + col_s(b), sw128_desc(q_smem + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
-                    ks > 0 ? 1u : 0u);
-          }
-          umma_commit(s_full + b);
+          issue_s(0, j + 1);
         }
-        if (j >= 1) {
-          const int jj = j - 1, b = jj & 1, s = jj % kTcStages;
-          if (!tc_wait(p_full + b, (jj >> 1) & 1, abort_flag, a.err)) break;
+        umma_commit(s_full);
+        if (two) {
+          if (!tc_wait(p_full + 1, j & 1, abort_flag, a.err)) break;
           tc_fence_after();
-          const uint32_t vb = stage_smem + s * L::kStageBytes + L::kTileBytes;
-          const int live_pages = min(kTcTilePages, npages - jj * kTcTilePages);  // one k-step per page
-          for (int ks = 0; ks < live_pages; ++ks)
-            umma_ts(tmem + kColO, tmem + col_p(b) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
-                    kIdescO, (jj > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(empty + s);
-          umma_commit(o_done);
+          issue_pv(1, j);
+          umma_commit(empty + j % NS);
+          if (more) issue_s(1, j + 1);
+          umma_commit(s_full + 1);
+        } else {
+          umma_commit(empty + j % NS);
         }
       }
       umma_commit(final_bar);  // every MMA issued above has completed when this arrives
       if (!tc_drain(final_bar, 0)) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
     }
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax warpgroup: one query column each
+  } else {
+    // ------------------------------------------------------------ softmax warpgroups: warps 4-7 take tile A,
+    // warps 8-11 tile B; one thread = one query column = one TMEM lane
+    const int x = warp >= 8 ? 1 : 0;
+    const int row = threadIdx.x - 128 * (1 + x);
+    const int mb = x ? xb.x : xa.x, mc = x ? xb.y : xa.y, piece = x ? yb.x : ya.x;
+    const int tile_pieces = (x ? yb.z : ya.z) >> 8, tile_part_base = x ? yb.w : ya.w;
     // the Q rows first, straight into the swizzled K-major A tile (zero for absent columns); the producers
     // are already fetching the first K/V tiles, and only the MMA issuer waits for q_ready
     {
-      const int c = threadIdx.x - 128;
-      const int m = c / a.group;
-      const bool live = m < mc;
+      const int m = row / a.group;
+      const bool live = m < mc && (x == 0 || two);
       const uint4* src = nullptr;
       if (live) {
         const int tok = tile_unit ? mb + m : __ldg(&a.members[mb + m].q0);
-        const int head = kvh * a.group + c % a.group;
+        const int head = kvh * a.group + row % a.group;
         src = reinterpret_cast<const uint4*>(
             a.q + (static_cast<int64_t>(tok) * a.q_st + static_cast<int64_t>(head) * a.q_sh) * 2);
       }
+      uint8_t* qx = smem + x * L::kQBytes;
 #pragma unroll
       for (int ch = 0; ch < CH; ++ch) {
         const uint4 v = live ? __ldg(src + ch) : make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(smem + sw_chunk(c, ch)) = v;
+        *reinterpret_cast<uint4*>(qx + sw_chunk(row, ch)) = v;
       }
       fence_proxy_async_smem();  // generic-proxy stores, read by the tensor core (async proxy)
     }
     mbar_arrive(q_ready);
-    const int row = threadIdx.x - 128;
-    const uint32_t lanes = static_cast<uint32_t>((warp - 4) * 32) << 16;
-    const int key_lim = first_pos + row / a.group + 1;  // kind 1: exclusive causal key limit of this column
+    const bool active = x == 0 || two;
+    const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_cols = tmem + lanes + col_s(x), o_cols = tmem + lanes + col_o<DH>(x);
+    // kind 1: key position of the tile's first token, and this column's exclusive causal key limit
+    const int first_pos = tile_unit ? __ldg(a.seq_lens + tseq) - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) +
+                                          (mb - __ldg(a.qo + tseq))
+                                    : 0;
+    const int key_lim = first_pos + row / a.group + 1;
     const int seq_len = tile_unit ? __ldg(a.seq_lens + tseq) : INT_MAX;
-    float m_used = -__builtin_huge_valf(), l = 0.f;
+    float m_used = kNegInfF, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
+    for (int j = 0; active && j < ntiles; ++j) {
       // keys of this tile: full pages up to the unit's end, minus pages with an out-of-range block id
-      // (lane p checks page p; loaded before the wait so the round trip overlaps it)
+      // (lane p checks page p; loaded before the wait so the round trip overlaps it), minus (kind 1) keys
+      // past the column's causal limit: key k of the tile is live iff k < valid_end and its page is good
       const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
       int my_bid = 0;
       if (lane < live_pages) my_bid = __ldg(table + pb + j * kTcTilePages + lane);
-      if (!tc_wait(s_full + b, (j >> 1) & 1, abort_flag, a.err)) {
+      if (!tc_wait(s_full + x, j & 1, abort_flag, a.err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sr[kTcTileTokens];
-#pragma unroll
-      for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_ld32(tmem + lanes + col_s(b) + 32 * i, sr + 32 * i);
       const uint32_t bad = __ballot_sync(0xffffffffu, lane < live_pages && (my_bid < 0 || my_bid >= a.num_blocks));
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < kTcTileTokens / 32; ++i) tmem_pin32(sr + 32 * i);
-      // raw scores stay in sr; masked keys become -inf (only on a partial tile or a bad page)
-      if (live_pages < kTcTilePages || bad) {
-#pragma unroll
-        for (int k = 0; k < kTcTileTokens; ++k) {
-          const int p = k / kBlockSize;
-          if (p >= live_pages || ((bad >> p) & 1u)) sr[k] = __float_as_uint(-__builtin_huge_valf());
-        }
-      }
       const int tile_key0 = (pb + j * kTcTilePages) * kBlockSize;  // key position of element 0
-      if (tile_unit) {
-        // causal: this column sees keys < key_lim (elements from key_lim - tile_key0 on are masked)
-        const int rel = key_lim - tile_key0;
-        if (rel < kTcTileTokens) {
+      const int valid_end = tile_unit ? min(live_pages * kBlockSize, key_lim - tile_key0) : live_pages * kBlockSize;
+      const bool masked = valid_end < kTcTileTokens || bad != 0u;
+      // pass 1: the row max of the raw scores, 32 columns per TMEM load (8 independent max chains)
+      float mx8[8];
 #pragma unroll
-          for (int k = 0; k < kTcTileTokens; ++k)
-            if (k >= rel) sr[k] = __float_as_uint(-__builtin_huge_valf());
+      for (int i = 0; i < 8; ++i) mx8[i] = kNegInfF;
+#pragma unroll 1
+      for (int c = 0; c < kTcTileTokens / 32; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(s_cols + 32 * c, sr);
+        tmem_wait_ld();
+        tmem_pin32(sr);
+        if (masked) {  // only a tile with a partial page range, a bad page or a causal edge
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int key = 32 * c + k;
+            if (key >= valid_end || ((bad >> (key / kBlockSize)) & 1u)) sr[k] = __float_as_uint(kNegInfF);
+          }
         }
-        // V rows of slots past the sequence's end (its last page) are junk: 0 x NaN would poison P . V,
-        // so they are zeroed in shared memory before the tile goes to the tensor core
+#pragma unroll
+        for (int k = 0; k < 32; ++k) mx8[k % 8] = fmaxf(mx8[k % 8], __uint_as_float(sr[k]));
+      }
+      const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      if (tile_unit && x == 0) {
+        // V rows of slots past the sequence's end (its last page) are junk: 0 x NaN would poison P . V, so
+        // they are zeroed in shared memory before the tile goes to the tensor core (tile A's threads do it
+        // before they release P_A; the MMA issues P_B . V after P_A . V)
         const int r0 = max(0, seq_len - tile_key0), r1 = live_pages * kBlockSize;
         if (r0 < r1) {
-          const uint32_t vb = stage_smem + (j % kTcStages) * L::kStageBytes + L::kTileBytes;
+          const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
           constexpr int kRowItems = (DH / 64) * 8;  // 16-byte chunks of one row, both halves
           for (int e = row; e < (r1 - r0) * kRowItems; e += 128) {
             const int r = r0 + e / kRowItems, h = (e % kRowItems) / 8, c = e % 8;
@@ -413,62 +476,63 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
           fence_proxy_async_smem();
         }
       }
-      // 8 independent max chains (one serial chain of 128 dependent FMNMX was the softmax's critical path)
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
-#pragma unroll
-      for (int k = 8; k < kTcTileTokens; ++k) mx8[k % 8] = fmaxf(mx8[k % 8], __uint_as_float(sr[k]));
-      const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx = mraw * a.sl2;  // the scale is positive: max commutes with it
       const bool need = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? fmaxf(m_used, mx) : m_used;
-        if (j > 0) {
+        if (j > 0) {  // P_x(j-1) . V has completed: s_full[x] of this tile was committed after it
           const float alpha = m_new == m_used ? 1.f : fast_exp2(m_used - m_new);
-          if (!tc_wait(o_done, (j - 1) & 1, abort_flag, a.err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
 #pragma unroll
           for (int i = 0; i < DH / 32; ++i) {
             uint32_t orow[32];
-            tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
+            tmem_ld32(o_cols + 32 * i, orow);
             tmem_wait_ld();
             tmem_pin32(orow);
 #pragma unroll
             for (int k = 0; k < 32; ++k) orow[k] = __float_as_uint(__uint_as_float(orow[k]) * alpha);
-            tmem_st32(tmem + lanes + kColO + 32 * i, orow);
+            tmem_st32(o_cols + 32 * i, orow);
           }
           tmem_wait_st();
           l *= alpha;
         }
         m_used = m_new;
       }
-      const float nbase = m_used == -__builtin_huge_valf() ? 0.f : -m_used;
-      const float sl2 = a.sl2;
-      uint32_t pk[kTcTileTokens / 2];
-      // p = 2^(s * scale * log2 e - m): the scale-and-subtract and the row sums run on packed pairs of fp32
-      // (fma.rn.f32x2 / add.f32x2, each lane rounded as fmaf / fadd), halving those instructions; the
-      // exponentials stay on the special-function unit.  4 pair sums = 8 independent sum chains.
+      // pass 2: p = 2^(s * scale * log2 e - m) packed to 16 bits over the first 64 columns of S_x (chunk c's
+      // 16 packed columns land behind the 32 score columns already read).  The scale-and-subtract and the
+      // row sums run on packed pairs of fp32 (fma.rn.f32x2 / add.f32x2, each lane rounded as fmaf / fadd);
+      // the exponentials stay on the special-function unit.  4 pair sums = 8 independent sum chains.
+      const float nbase = m_used == kNegInfF ? 0.f : -m_used;
       uint64_t sl2v, nbv, s4[4];
-      asm("mov.b64 %0, {%1, %1};" : "=l"(sl2v) : "f"(sl2));
+      asm("mov.b64 %0, {%1, %1};" : "=l"(sl2v) : "f"(a.sl2));
       asm("mov.b64 %0, {%1, %1};" : "=l"(nbv) : "f"(nbase));
 #pragma unroll
       for (int i = 0; i < 4; ++i) s4[i] = 0ull;  // +0.0f in both halves
+#pragma unroll 1
+      for (int c = 0; c < kTcTileTokens / 32; ++c) {
+        uint32_t sr[32], pk[16];
+        tmem_ld32(s_cols + 32 * c, sr);
+        tmem_wait_ld();
+        tmem_pin32(sr);
+        if (masked) {
 #pragma unroll
-      for (int k = 0; k < kTcTileTokens; k += 2) {
-        uint64_t sv, xv, pv;
-        asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "r"(sr[k]), "r"(sr[k + 1]));
-        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(xv) : "l"(sv), "l"(sl2v), "l"(nbv));
-        float x0, x1;
-        asm("mov.b64 {%0, %1}, %2;" : "=f"(x0), "=f"(x1) : "l"(xv));
-        const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
-        asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "f"(p0), "f"(p1));
-        asm("add.f32x2 %0, %0, %1;" : "+l"(s4[(k / 2) % 4]) : "l"(pv));
-        pk[k / 2] = pack2<DT>(p0, p1);
+          for (int k = 0; k < 32; ++k) {
+            const int key = 32 * c + k;
+            if (key >= valid_end || ((bad >> (key / kBlockSize)) & 1u)) sr[k] = __float_as_uint(kNegInfF);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 32; k += 2) {
+          uint64_t sv, xv, pv;
+          asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "r"(sr[k]), "r"(sr[k + 1]));
+          asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(xv) : "l"(sv), "l"(sl2v), "l"(nbv));
+          float x0, x1;
+          asm("mov.b64 {%0, %1}, %2;" : "=f"(x0), "=f"(x1) : "l"(xv));
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          asm("mov.b64 %0, {%1, %2};" : "=l"(pv) : "f"(p0), "f"(p1));
+          asm("add.f32x2 %0, %0, %1;" : "+l"(s4[(k / 2) % 4]) : "l"(pv));
+          pk[k / 2] = pack2<DT>(p0, p1);
+        }
+        tmem_st16(s_cols + 16 * c, pk);
       }
       float sum = 0.f;
 #pragma unroll
@@ -478,17 +542,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         sum += lo + hi;
       }
       l += sum;
-      tmem_st32(tmem + lanes + col_p(b), pk);
-      tmem_st32(tmem + lanes + col_p(b) + 32, pk + 32);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full + b);
+      mbar_arrive(p_full + x);
     }
-    // O is complete when final_bar (committed once, after every MMA) arrives.  Not o_done's parity
-    // (ntiles - 1) & 1: here only P . V of tile ntiles - 3 is known complete (it precedes the last S commit),
-    // and while P . V of tile ntiles - 2 is still running that parity names the phase before the current
-    // one, which a parity wait takes as complete.
-    if (ok && ntiles > 0 && tc_wait(final_bar, 0, abort_flag, a.err) && !*abort_flag) {
+    // O is complete when final_bar (committed once, after every MMA) arrives
+    if (active && ok && ntiles > 0 && tc_wait(final_bar, 0, abort_flag, a.err) && !*abort_flag) {
       tc_fence_after();
       const int m = row / a.group;
       const int head = kvh * a.group + row % a.group;
@@ -509,7 +568,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
 #pragma unroll
       for (int i = 0; i < DH / 32; ++i) {
         uint32_t orow[32];
-        tmem_ld32(tmem + lanes + kColO + 32 * i, orow);
+        tmem_ld32(o_cols + 32 * i, orow);
         tmem_wait_ld();
         tmem_pin32(orow);
         if (live && final_rows) {
@@ -528,7 +587,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
                                  __uint_as_float(orow[4 * k + 2]) * inv, __uint_as_float(orow[4 * k + 3]) * inv);
         }
       }
-      if (live && !final_rows) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -__builtin_huge_valf();
+      if (live && !final_rows) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : kNegInfF;
     }
   }
 
@@ -600,7 +659,8 @@ cudaError_t launch_tc(const AttnArgs& a, int64_t units, cudaStream_t s) {
   e = pool_tensor_map(&tk, a.k_cache, DT, a.num_blocks, a.hkv, DH);
   if (e == cudaSuccess) e = pool_tensor_map(&tv, a.v_cache, DT, a.num_blocks, a.hkv, DH);
   if (e != cudaSuccess) return e;
-  return launch_k(k, dim3(static_cast<unsigned>(units * a.hkv)), dim3(kTcThreads), bytes, s, a, tk, tv);
+  // one CTA per pair of units (2i, 2i + 1) and KV head
+  return launch_k(k, dim3(static_cast<unsigned>(units / 2 * a.hkv)), dim3(kTcThreads), bytes, s, a, tk, tv);
 }
 
 }  // namespace

@@ -269,8 +269,9 @@ def test_planner_finds_shared_prefixes(mlb):
     pieces = sorted({(int(x[2]), int(x[3]), int(x[4])) for x in su})
     assert pieces[0][0] == 0 and pieces[-1][1] == 40 and all(a[1] == b[0] for a, b in zip(pieces, pieces[1:]))
     npieces = len(pieces)
+    assert_pairs(su)
     for mb, mc, pb, pe, piece, tseq, *_ in su.tolist():
-        assert 0 < mc <= 128 // 4 and tseq in range(20)  # one unit: at most 128 query columns
+        assert 0 <= mc <= 128 // 4 and tseq in range(20)  # one unit: at most 128 query columns (0: empty partner)
         assert (pe - pb) % 8 == 0 or pe == 40  # pieces are whole 8-page (128-key) tiles but the last
     per_member = {m: 0 for m in range(len(members))}
     for mb, mc, *_ in su.tolist():
@@ -292,6 +293,17 @@ def test_planner_finds_shared_prefixes(mlb):
     assert plain.num_shared_units == 0
 
 
+def assert_pairs(su: np.ndarray) -> None:
+    """Shared units come in pairs (2i, 2i + 1) over the same pages, table row, piece and kind, ordered largest
+    first as whole pairs; a pair's second unit may be empty, its first never is."""
+    assert su.shape[0] % 2 == 0
+    a, b = su[0::2], su[1::2]
+    assert (a[:, 2:6] == b[:, 2:6]).all() and ((a[:, 6] & 0xFF) == (b[:, 6] & 0xFF)).all()
+    assert (a[:, 1] > 0).all() and (b[:, 1] >= 0).all()
+    sizes = a[:, 3] - a[:, 2]
+    assert (np.diff(sizes) <= 0).all()
+
+
 def _prefix_step(suffix_lo: int, suffix_hi: int, rows: int = 128, prefix_pages: int = 512, seed: int = 0):
     """BASELINE config 4's shape: `rows` decode rows sharing `prefix_pages` full pages, own suffixes."""
     r = random.Random(seed)
@@ -309,6 +321,9 @@ def _prefix_step(suffix_lo: int, suffix_hi: int, rows: int = 128, prefix_pages: 
     return list(range(rows + 1)), lens, host
 
 
+EXPECTED_SHARED_CTAS = {"config4": 64, "tiny": 128, "long": 32}  # CTAs = pairs x KV heads x pieces
+
+
 def test_planner_balances_shared_ctas_against_private_work(mlb):
     """The shared-prefix kernel runs beside the per-sequence kernel, one CTA per SM: the planner gives it the
     share of the SMs that balances the two (config 4: 3 pieces x 4 row blocks x 8 KV heads = 96 CTAs, the
@@ -319,11 +334,12 @@ def test_planner_balances_shared_ctas_against_private_work(mlb):
         qo, lens, host = _prefix_step(lo, hi)
         p = mlb.plan_attention(qo, lens, host.shape[1], 32, 8, "cpu", num_sms=148, block_tables_host=host)
         su = p.shared_host
-        ctas[name] = p.num_shared_units * 8
+        assert_pairs(su)
+        ctas[name] = p.num_shared_units // 2 * 8  # one CTA per pair of units and KV head
         pieces = sorted({(int(x[2]), int(x[3])) for x in su})
         assert pieces[0][0] == 0 and pieces[-1][1] == 512 and all(a[1] == b[0] for a, b in zip(pieces, pieces[1:]))
         assert ctas[name] <= 148
-    assert ctas == {"config4": 96, "tiny": 128, "long": 32}
+    assert ctas == EXPECTED_SHARED_CTAS
 
 
 @pytest.mark.parametrize("h,hkv", [(32, 8), (8, 8), (16, 2), (12, 4)])
@@ -343,18 +359,27 @@ def test_planner_makes_query_tiles_for_prefill_rows(mlb, h, hkv):
     host = np.arange(len(steps) * width, dtype=np.int32).reshape(len(steps), width)
     p = mlb.plan_attention(qo, lens, width, h, hkv, "cpu", block_tables_host=host)
     su = p.shared_host
+    assert_pairs(su)
     kind1 = [u for u in su.tolist() if (u[6] & 0xFF) == 1]
     prefill = {s for s, (c, n) in enumerate(steps) if n >= 16}
     assert {u[5] for u in kind1} == prefill
     assert not any(u[0] in prefill for u in p.units_host.tolist()), "prefill rows get no 8-column units"
     covered = {}
+    pair_pages = {}
+    for i in range(0, len(kind1), 2):  # a pair covers the keys its later tile's last token sees
+        (fa, na, *_), (fb, nb, _, _, _, seq, *_) = kind1[i], kind1[i + 1]
+        c = steps[seq][0]
+        pair_pages[(seq, fa - qo[seq])] = -(-(c + fa - qo[seq] + na + nb) // 16)
     for first, ntok, pb, pe, piece, seq, kp, base in kind1:
+        if ntok == 0:
+            continue  # an empty partner
         c, n = steps[seq]
         assert 1 <= ntok <= tile and qo[seq] <= first and first + ntok <= qo[seq + 1]
         t0 = first - qo[seq]
-        pages = -(-(c + t0 + ntok) // 16)  # keys the tile's last token sees
+        lead = t0 - t0 % (2 * tile)
+        pages = pair_pages[(seq, lead)]
         pieces = kp >> 8
-        covered.setdefault((seq, t0), []).append((pb, pe, piece, pieces, base, ntok))
+        covered.setdefault((seq, t0), []).append((pb, pe, piece, pieces, base, ntok, pages))
         assert 0 <= pb < pe <= pages
         if pieces == 1:
             assert piece == -1 and (pb, pe) == (0, pages)
@@ -368,8 +393,8 @@ def test_planner_makes_query_tiles_for_prefill_rows(mlb, h, hkv):
     for (seq, t0), parts in covered.items():
         parts.sort()
         c, n = steps[seq]
-        ntok = parts[0][5]
-        assert parts[0][0] == 0 and parts[-1][1] == -(-(c + t0 + ntok) // 16)
+        assert parts[0][0] == 0 and parts[-1][1] == parts[0][6]
+        assert parts[-1][1] >= -(-(c + t0 + parts[0][5]) // 16)  # at least the keys the tile's last token sees
         assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
     for s in prefill:  # every token of a prefill row is in exactly one tile
         n = steps[s][1]

@@ -77,6 +77,13 @@ def test_host_view_of_the_reference_metadata(mlb, name, seqs):
     assert private == ours.append_private == (name != "clash")
 
 
+def test_package_field_list_is_the_reference_interface(mlb):
+    md = importlib.import_module(mlb.__name__ + ".attention.metadata")
+    assert list(md.REFERENCE_FIELDS) == FIELDS["metadata_fields"]
+    assert all(hasattr(mlb.AttentionMetadata, f) or f in mlb.AttentionMetadata.__dataclass_fields__
+               for f in md.REFERENCE_FIELDS)
+
+
 def reference_shaped(meta) -> types.SimpleNamespace:
     """An object with exactly the reference's AttentionMetadata fields, taken from this package's build."""
     return types.SimpleNamespace(**{f: getattr(meta, f) for f in FIELDS["metadata_fields"]})
