@@ -65,7 +65,10 @@ constexpr int kSharedColumns = 128;  // query columns (member rows x group) per 
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
 // SM time of one key tile (128 keys) of a tensor-core CTA, which carries a pair of 128-column query tiles,
 // in page-heads streamed by the per-sequence kernel (head_dim 128; ~0.1 us per 8 KB page-head)
-constexpr int kTilePageHeads = 19;
+#ifndef MLB_TILE_PAGE_HEADS
+#define MLB_TILE_PAGE_HEADS 19
+#endif
+constexpr int kTilePageHeads = MLB_TILE_PAGE_HEADS;
 constexpr int kMinSharedSmPct = 25;  // the shared-prefix kernel gets at least this share of the SMs
 constexpr int kMinShareSeqs = 4;     // a shared prefix is planned once only for this many decode rows ...
 constexpr int kMinSharePages = 8;    // ... sharing at least this many full pages

@@ -22,10 +22,11 @@
 //   P read from TMEM (A operand) and V as an MN-major B operand (one k-step of 16 keys per loaded page, so
 //   pages past the unit's end are never read), then S_x(j+1) = Q_x . K_{j+1}^T, committed to s_full[x]; the
 //   stage is released (empty) once both products of tile j are issued.
-// - warps 4-7 (tile A) and 8-11 (tile B), one thread = one query column = one TMEM lane: pass 1 reads the S
-//   row from TMEM 32 columns at a time for the masked running max (exp2 domain); pass 2 reads it again and
-//   writes P = 2^(s - m), packed to 16 bits, over the first 64 columns of the same S buffer; row sums in
-//   fp32.  Two passes keep a thread under 168 registers (384 threads on one SM).  O is rescaled (TMEM load /
+// - warps 4-7 (tile A) and 8-11 (tile B), one thread = one query column = one TMEM lane: the whole S row
+//   comes out of TMEM in one go (4 loads, one wait) for the masked max (exp2 domain), and P = 2^(s - m),
+//   packed to 16 bits, goes back over the first 64 columns of the same S buffer; row sums in fp32.  The 128
+//   scores per thread need more than the 168 registers 384 threads get at launch: warps 0-3 give theirs up
+//   (setmaxnreg.dec to 56) and the softmax warps take them (setmaxnreg.inc to 224).  O is rescaled (TMEM load /
 //   scale / store) only when a row's max grows by more than 8 (a factor 256 of headroom keeps P and the
 //   sums finite), which after the first tiles is rare; s_full[x] of tile j is committed after P_x(j-1) . V,
 //   so O_x is quiet then.  At the end (the "final" barrier, committed behind the last MMA) every column's
@@ -55,6 +56,10 @@ constexpr int kTcTileTokens = 128;  // keys per tile = N of S = Q . K^T
 constexpr int kTcTilePages = kTcTileTokens / kBlockSize;
 constexpr int kTcProducerWarps = 3;  // warps 0, 2, 3
 constexpr uint32_t kTmemCols = 512;
+// registers per thread: at launch (384 threads on one SM), after the split for warps 0-3 and for the softmax
+constexpr int kRegsLaunch = 168, kRegsLow = 56, kRegsHigh = 224;
+static_assert(128 * (kRegsLaunch - kRegsLow) == 256 * (kRegsHigh - kRegsLaunch), "the split must balance");
+static_assert(kRegsLaunch * kTcThreads <= 65536, "one CTA per SM");
 // TMEM columns: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B after it; P_x (16-bit pairs) over the
 // first 64 columns of S_x
 __device__ __forceinline__ uint32_t col_s(int x) { return x ? 128u : 0u; }
@@ -279,112 +284,120 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 || warp == 2 || warp == 3) {
-    // ------------------------------------------------------------ producers (warps 0, 2, 3): TMA boxes
-    // Producer warp w (index pw 0..2) owns pages pw, pw + 3, pw + 6 of each tile, one per lane: the lane
-    // loads its page's block id one tile ahead (the table round trip overlaps the previous tile) and
-    // issues the page's 2 x Dh/64 boxes; the warp's lane 0 declares the warp's bytes on the stage barrier
-    // (3 arrivals per phase).  Three warps issue a tile's boxes in parallel.
-    constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
-    constexpr int kHalves = DH / 64;
-    const int pw = warp == 0 ? 0 : warp - 1;
-    const int page_in_tile = pw + kTcProducerWarps * lane;
-    const bool mine = lane < (kTcTilePages - pw + kTcProducerWarps - 1) / kTcProducerWarps;
-    const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
-    auto load_bid = [&](int j) {
-      const int page = j * kTcTilePages + page_in_tile;
-      return mine && page < npages ? __ldg(table + pb + page) : 0;
-    };
-    int bid = load_bid(0);
-    for (int j = 0; j < ntiles; ++j) {
-      const int s = j % NS;
-      if (j >= NS) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
-        int ok = 1;
-        if (lane == 0) ok = tc_wait(empty + s, ((j / NS) + 1) & 1, abort_flag, a.err) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-      }
-      const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
-      const int my_pages = live_pages > pw ? (live_pages - pw + kTcProducerWarps - 1) / kTcProducerWarps : 0;
-      const uint32_t kbase = stage_smem + s * L::kStageBytes, vbase = kbase + L::kTileBytes;
-      if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(my_pages) * 2 * kHalves * kBoxBytes);
-      __syncwarp();
-      const int next = load_bid(j + 1);
-      if (lane < my_pages) {
-        int slot = oob_slot;
-        if (bid >= 0 && bid < a.num_blocks)
-          slot = bid * kBlockSize;
-        else
-          flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-#pragma unroll
-        for (int h = 0; h < kHalves; ++h) {
-          const uint32_t off = h * (kTcTileTokens * 128) + page_in_tile * (kBlockSize * 128);
-          tma_load_3d(kbase + off, &tk, h * 64, kvh, slot, full + s);
-          tma_load_3d(vbase + off, &tv, h * 64, kvh, slot, full + s);
-        }
-      }
-      bid = next;
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (one thread)
-    // Per tile j: O_A += P_A(j) . V_j, S_A(j+1) = Q_A . K_{j+1}^T, commit s_full[A]; then the same for B,
-    // with the stage released (empty) once both P . V of tile j are issued.  While softmax A works on its
-    // scores the tensor core runs B's products, and the other way round.  Issued MMAs execute in order, so
-    // S_x(j+1) overwrites the TMEM columns holding P_x(j) only after P_x(j) . V_j has read them.
-    if (lane == 0) {
-      auto issue_s = [&](int x, int j) {  // S_x = Q_x . K_j^T (K = Dh in steps of 16)
-        const uint32_t kb = stage_smem + (j % NS) * L::kStageBytes, qx = q_smem + x * L::kQBytes;
-#pragma unroll
-        for (int ks = 0; ks < DH / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
-          umma_ss(tmem + col_s(x), sw128_desc(qx + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
-                  ks > 0 ? 1u : 0u);
-        }
+  // Register split: the producer / MMA warpgroup (warps 0-3) drops to kRegsLow, the two softmax warpgroups
+  // take what it frees (kRegsHigh each).  The launch gives every thread kRegsLaunch (checked on the host
+  // against the compiled kernel before any launch), so 128 x (launch - low) = 256 x (high - launch) exactly.
+  if (warp < 4) {
+    // warpgroup 0 gives up registers, all four warps at the same instruction
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
+    if (warp != 1) {
+      // ------------------------------------------------------------ producers (warps 0, 2, 3): TMA boxes
+      // Producer warp w (index pw 0..2) owns pages pw, pw + 3, pw + 6 of each tile, one per lane: the lane
+      // loads its page's block id one tile ahead (the table round trip overlaps the previous tile) and
+      // issues the page's 2 x Dh/64 boxes; the warp's lane 0 declares the warp's bytes on the stage barrier
+      // (3 arrivals per phase).  Three warps issue a tile's boxes in parallel.
+      constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
+      constexpr int kHalves = DH / 64;
+      const int pw = warp == 0 ? 0 : warp - 1;
+      const int page_in_tile = pw + kTcProducerWarps * lane;
+      const bool mine = lane < (kTcTilePages - pw + kTcProducerWarps - 1) / kTcProducerWarps;
+      const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
+      auto load_bid = [&](int j) {
+        const int page = j * kTcTilePages + page_in_tile;
+        return mine && page < npages ? __ldg(table + pb + page) : 0;
       };
-      auto issue_pv = [&](int x, int j) {  // O_x += P_x . V_j, one k-step of 16 keys per loaded page
-        const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
+      int bid = load_bid(0);
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j % NS;
+        if (j >= NS) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
+          int ok = 1;
+          if (lane == 0) ok = tc_wait(empty + s, ((j / NS) + 1) & 1, abort_flag, a.err) ? 1 : 0;
+          if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
         const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
-        for (int ks = 0; ks < live_pages; ++ks)
-          umma_ts(tmem + col_o<DH>(x), tmem + col_s(x) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
-                  kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
-      };
-      bool ok = ntiles > 0 && tc_wait(q_ready, 0, abort_flag, a.err) && tc_wait(full, 0, abort_flag, a.err);
-      if (ok) {
-        fence_proxy_async_smem();
-        tc_fence_after();
-        issue_s(0, 0);
-        umma_commit(s_full);
-        if (two) {
-          issue_s(1, 0);
-          umma_commit(s_full + 1);
+        const int my_pages = live_pages > pw ? (live_pages - pw + kTcProducerWarps - 1) / kTcProducerWarps : 0;
+        const uint32_t kbase = stage_smem + s * L::kStageBytes, vbase = kbase + L::kTileBytes;
+        if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(my_pages) * 2 * kHalves * kBoxBytes);
+        __syncwarp();
+        const int next = load_bid(j + 1);
+        if (lane < my_pages) {
+          int slot = oob_slot;
+          if (bid >= 0 && bid < a.num_blocks)
+            slot = bid * kBlockSize;
+          else
+            flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+  #pragma unroll
+          for (int h = 0; h < kHalves; ++h) {
+            const uint32_t off = h * (kTcTileTokens * 128) + page_in_tile * (kBlockSize * 128);
+            tma_load_3d(kbase + off, &tk, h * 64, kvh, slot, full + s);
+            tma_load_3d(vbase + off, &tv, h * 64, kvh, slot, full + s);
+          }
         }
+        bid = next;
       }
-      for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
-        const bool more = j + 1 < ntiles;
-        if (!tc_wait(p_full, j & 1, abort_flag, a.err)) break;
-        tc_fence_after();
-        issue_pv(0, j);
-        if (more) {
-          if (!tc_wait(full + (j + 1) % NS, ((j + 1) / NS) & 1, abort_flag, a.err)) break;
+    } else {
+      // ------------------------------------------------------------ MMA issuer (one thread)
+      // Per tile j: O_A += P_A(j) . V_j, S_A(j+1) = Q_A . K_{j+1}^T, commit s_full[A]; then the same for B,
+      // with the stage released (empty) once both P . V of tile j are issued.  While softmax A works on its
+      // scores the tensor core runs B's products, and the other way round.  Issued MMAs execute in order, so
+      // S_x(j+1) overwrites the TMEM columns holding P_x(j) only after P_x(j) . V_j has read them.
+      if (lane == 0) {
+        auto issue_s = [&](int x, int j) {  // S_x = Q_x . K_j^T (K = Dh in steps of 16)
+          const uint32_t kb = stage_smem + (j % NS) * L::kStageBytes, qx = q_smem + x * L::kQBytes;
+  #pragma unroll
+          for (int ks = 0; ks < DH / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
+            umma_ss(tmem + col_s(x), sw128_desc(qx + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
+                    ks > 0 ? 1u : 0u);
+          }
+        };
+        auto issue_pv = [&](int x, int j) {  // O_x += P_x . V_j, one k-step of 16 keys per loaded page
+          const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
+          const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+          for (int ks = 0; ks < live_pages; ++ks)
+            umma_ts(tmem + col_o<DH>(x), tmem + col_s(x) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
+                    kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
+        };
+        bool ok = ntiles > 0 && tc_wait(q_ready, 0, abort_flag, a.err) && tc_wait(full, 0, abort_flag, a.err);
+        if (ok) {
           fence_proxy_async_smem();
           tc_fence_after();
-          issue_s(0, j + 1);
+          issue_s(0, 0);
+          umma_commit(s_full);
+          if (two) {
+            issue_s(1, 0);
+            umma_commit(s_full + 1);
+          }
         }
-        umma_commit(s_full);
-        if (two) {
-          if (!tc_wait(p_full + 1, j & 1, abort_flag, a.err)) break;
+        for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
+          const bool more = j + 1 < ntiles;
+          if (!tc_wait(p_full, j & 1, abort_flag, a.err)) break;
           tc_fence_after();
-          issue_pv(1, j);
-          umma_commit(empty + j % NS);
-          if (more) issue_s(1, j + 1);
-          umma_commit(s_full + 1);
-        } else {
-          umma_commit(empty + j % NS);
+          issue_pv(0, j);
+          if (more) {
+            if (!tc_wait(full + (j + 1) % NS, ((j + 1) / NS) & 1, abort_flag, a.err)) break;
+            fence_proxy_async_smem();
+            tc_fence_after();
+            issue_s(0, j + 1);
+          }
+          umma_commit(s_full);
+          if (two) {
+            if (!tc_wait(p_full + 1, j & 1, abort_flag, a.err)) break;
+            tc_fence_after();
+            issue_pv(1, j);
+            umma_commit(empty + j % NS);
+            if (more) issue_s(1, j + 1);
+            umma_commit(s_full + 1);
+          } else {
+            umma_commit(empty + j % NS);
+          }
         }
+        umma_commit(final_bar);  // every MMA issued above has completed when this arrives
+        if (!tc_drain(final_bar, 0)) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
       }
-      umma_commit(final_bar);  // every MMA issued above has completed when this arrives
-      if (!tc_drain(final_bar, 0)) flag_error(a.err, MLB_DEV_WAIT_TIMEOUT);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsHigh));
     // ------------------------------------------------------------ softmax warpgroups: warps 4-7 take tile A,
     // warps 8-11 tile B; one thread = one query column = one TMEM lane
     const int x = warp >= 8 ? 1 : 0;
@@ -439,26 +452,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const int tile_key0 = (pb + j * kTcTilePages) * kBlockSize;  // key position of element 0
       const int valid_end = tile_unit ? min(live_pages * kBlockSize, key_lim - tile_key0) : live_pages * kBlockSize;
       const bool masked = valid_end < kTcTileTokens || bad != 0u;
-      // pass 1: the row max of the raw scores, 32 columns per TMEM load (8 independent max chains)
+      // the whole S row: 4 TMEM loads in flight, one wait (the softmax warps hold 224 registers)
+      uint32_t sr[kTcTileTokens];
+#pragma unroll
+      for (int c = 0; c < kTcTileTokens / 32; ++c) tmem_ld32(s_cols + 32 * c, sr + 32 * c);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < kTcTileTokens / 32; ++c) tmem_pin32(sr + 32 * c);
+      if (masked) {  // only a tile with a partial page range, a bad page or a causal edge
+#pragma unroll
+        for (int k = 0; k < kTcTileTokens; ++k)
+          if (k >= valid_end || ((bad >> (k / kBlockSize)) & 1u)) sr[k] = __float_as_uint(kNegInfF);
+      }
+      // 8 independent max chains (one serial chain of 128 dependent FMNMX would be the critical path)
       float mx8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = kNegInfF;
-#pragma unroll 1
-      for (int c = 0; c < kTcTileTokens / 32; ++c) {
-        uint32_t sr[32];
-        tmem_ld32(s_cols + 32 * c, sr);
-        tmem_wait_ld();
-        tmem_pin32(sr);
-        if (masked) {  // only a tile with a partial page range, a bad page or a causal edge
+      for (int i = 0; i < 8; ++i) mx8[i] = __uint_as_float(sr[i]);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int key = 32 * c + k;
-            if (key >= valid_end || ((bad >> (key / kBlockSize)) & 1u)) sr[k] = __float_as_uint(kNegInfF);
-          }
-        }
-#pragma unroll
-        for (int k = 0; k < 32; ++k) mx8[k % 8] = fmaxf(mx8[k % 8], __uint_as_float(sr[k]));
-      }
+      for (int k = 8; k < kTcTileTokens; ++k) mx8[k % 8] = fmaxf(mx8[k % 8], __uint_as_float(sr[k]));
       const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       if (tile_unit && x == 0) {
@@ -497,33 +508,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         }
         m_used = m_new;
       }
-      // pass 2: p = 2^(s * scale * log2 e - m) packed to 16 bits over the first 64 columns of S_x (chunk c's
-      // 16 packed columns land behind the 32 score columns already read).  The scale-and-subtract and the
-      // row sums run on packed pairs of fp32 (fma.rn.f32x2 / add.f32x2, each lane rounded as fmaf / fadd);
-      // the exponentials stay on the special-function unit.  4 pair sums = 8 independent sum chains.
+      // p = 2^(s * scale * log2 e - m) packed to 16 bits over the first 64 columns of S_x (the row is in
+      // registers already), in two halves of 32 packed columns.  The scale-and-subtract and the row sums run
+      // on packed pairs of fp32 (fma.rn.f32x2 / add.f32x2, each lane rounded as fmaf / fadd); the
+      // exponentials stay on the special-function unit.  4 pair sums = 8 independent sum chains.
       const float nbase = m_used == kNegInfF ? 0.f : -m_used;
       uint64_t sl2v, nbv, s4[4];
       asm("mov.b64 %0, {%1, %1};" : "=l"(sl2v) : "f"(a.sl2));
       asm("mov.b64 %0, {%1, %1};" : "=l"(nbv) : "f"(nbase));
 #pragma unroll
       for (int i = 0; i < 4; ++i) s4[i] = 0ull;  // +0.0f in both halves
-#pragma unroll 1
-      for (int c = 0; c < kTcTileTokens / 32; ++c) {
-        uint32_t sr[32], pk[16];
-        tmem_ld32(s_cols + 32 * c, sr);
-        tmem_wait_ld();
-        tmem_pin32(sr);
-        if (masked) {
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int key = 32 * c + k;
-            if (key >= valid_end || ((bad >> (key / kBlockSize)) & 1u)) sr[k] = __float_as_uint(kNegInfF);
-          }
-        }
+      for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
 #pragma unroll
-        for (int k = 0; k < 32; k += 2) {
+        for (int k = 0; k < 64; k += 2) {
           uint64_t sv, xv, pv;
-          asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "r"(sr[k]), "r"(sr[k + 1]));
+          asm("mov.b64 %0, {%1, %2};" : "=l"(sv) : "r"(sr[64 * h + k]), "r"(sr[64 * h + k + 1]));
           asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(xv) : "l"(sv), "l"(sl2v), "l"(nbv));
           float x0, x1;
           asm("mov.b64 {%0, %1}, %2;" : "=f"(x0), "=f"(x1) : "l"(xv));
@@ -532,7 +533,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
           asm("add.f32x2 %0, %0, %1;" : "+l"(s4[(k / 2) % 4]) : "l"(pv));
           pk[k / 2] = pack2<DT>(p0, p1);
         }
-        tmem_st16(s_cols + 16 * c, pk);
+        tmem_st32(s_cols + 32 * h, pk);
       }
       float sum = 0.f;
 #pragma unroll
@@ -651,6 +652,12 @@ cudaError_t launch_tc(const AttnArgs& a, int64_t units, cudaStream_t s) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (!(dev < 64 && (done >> dev) & 1ull)) {
+    // the register split inside the kernel (setmaxnreg) balances only if every thread starts with exactly
+    // kRegsLaunch registers; a build that compiled to another count is refused instead of launched
+    cudaFuncAttributes fa{};
+    e = cudaFuncGetAttributes(&fa, k);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kRegsLaunch) return cudaErrorInvalidKernelImage;
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (e != cudaSuccess) return e;
     if (dev < 64) __atomic_fetch_or(&done, 1ull << dev, __ATOMIC_RELAXED);

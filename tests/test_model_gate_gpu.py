@@ -4,9 +4,13 @@ the reference's own model) with B200Backend swapped in, as an unmodified engine 
 - fp32 pools: greedy generation through ragged paged steps (scattered blocks, pools pre-filled with junk,
   chunked prefill) gives exactly the dense greedy tokens (the reference's tests/test_paged.py:136-146).
 - bf16: the reference's G1b check (src/minillm/correctness.py:57-95, driven as tests/test_kernels.py:75-114
-  drives it): teacher-forced ragged steps (one batched prefill of ragged prompts, then 24 decode steps)
-  through B200Backend and through the reference's torch algorithm on the same GPU, with the reference as its
-  own noise baseline: mean KL, max |delta logit| and clear-lead top-1 agreement within G1b's limits.  The
+  drives it): teacher-forced ragged steps (one batched prefill of ragged prompts, then 24 decode steps) on
+  the same GPU and model.  G1b calibrates its tolerance from a trusted implementation's own spread; here the
+  truth is the reference's torch algorithm with attention in fp32, the noise is the same algorithm run the
+  way the reference runs it (SDPA in the pool dtype, bf16), and B200Backend's drift from the truth (mean
+  KL, max |delta logit|) must be within twice that noise (with G1b's floors), with top-1 agreement
+  wherever the truth's lead is clear.  (Checked against itself, as test_kernels.py does for Llama-3.1-8B,
+  only the floors would apply; they are calibrated for that model's sharp logits, not for a random one.)  The
   prefill rows of >= 16 tokens run as tensor-core query tiles; a second case has every row behind a shared
   24-block prefix, so the decode steps run the shared-prefix (cascade) kernel.
 """
@@ -74,12 +78,13 @@ def test_bf16_teacher_forced_drift_within_g1b(mlb, cuda, weights, shared):
     lens = (12, 200, 57, 1, 640, 33, 90, 8)
     seqs = [head + [rng.randrange(cfg.vocab_size) for _ in range(n + 24)] for n in lens]
     prompt_lens = [len(s) - 24 for s in seqs]
-    ref = teacher_forced(mlb, model, TorchPagedBackend(), seqs, prompt_lens, 24, shared=shared)
+    truth = teacher_forced(mlb, model, TorchPagedBackend(torch.float32), seqs, prompt_lens, 24, shared=shared)
+    ref_bf16 = teacher_forced(mlb, model, TorchPagedBackend(), seqs, prompt_lens, 24, shared=shared)
     ours_backend = _Recording(mlb)
     ours = teacher_forced(mlb, model, ours_backend, seqs, prompt_lens, 24, shared=shared)
-    noise, got = drift(ref, ref), drift(ref, ours)
-    print(f"\nG1b tiny llama bf16 ({'shared prefix' if shared else 'ragged'}): {got} (positions {got['positions']})")
-    assert g1b_passed(noise, got), got
+    noise, got = drift(truth, ref_bf16), drift(truth, ours)
+    print(f"\nG1b tiny llama bf16 ({'shared prefix' if shared else 'ragged'}): ours {got}, noise {noise}")
+    assert g1b_passed(noise, got), (got, noise)
     assert "fused_append" in ours_backend.seen
     assert "query_tiles" in ours_backend.seen  # the prefill rows of >= 16 tokens
     if shared:

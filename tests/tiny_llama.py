@@ -139,6 +139,9 @@ class TorchPagedBackend:
 
     name = "torch_paged"
 
+    def __init__(self, compute_dtype: torch.dtype | None = None) -> None:
+        self.compute_dtype = compute_dtype  # None: SDPA in the pool dtype, as the reference runs it
+
     def forward(self, q, k, v, k_cache, v_cache, meta):
         bs = k_cache.shape[1]
         k_cache.view(-1, *k_cache.shape[2:]).index_copy_(0, meta.slot_mapping, k.to(k_cache.dtype))
@@ -150,10 +153,11 @@ class TorchPagedBackend:
             a, b, length = qo[s], qo[s + 1], lens[s]
             n = b - a
             pages = -(-length // bs)
-            kk = k_cache[tables[s, :pages]].reshape(-1, *k_cache.shape[2:])[:length].transpose(0, 1)  # [Hkv, L, Dh]
-            vv = v_cache[tables[s, :pages]].reshape(-1, *v_cache.shape[2:])[:length].transpose(0, 1)
+            dt = self.compute_dtype or k_cache.dtype
+            kk = k_cache[tables[s, :pages]].reshape(-1, *k_cache.shape[2:])[:length].transpose(0, 1).to(dt)  # [Hkv, L, Dh]
+            vv = v_cache[tables[s, :pages]].reshape(-1, *v_cache.shape[2:])[:length].transpose(0, 1).to(dt)
             mask = torch.ones(n, length, dtype=torch.bool, device=q.device).tril(diagonal=length - n)
-            o = F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None].to(k_cache.dtype), kk[None], vv[None],
+            o = F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None].to(dt), kk[None], vv[None],
                                                attn_mask=mask, enable_gqa=True)
             out[a:b] = o[0].transpose(0, 1).to(q.dtype)
         return out
