@@ -63,8 +63,9 @@ constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (sh
 constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best)
 constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
-// SM time of one key tile (128 keys) of a tensor-core CTA, which carries a pair of 128-column query tiles,
-// in page-heads streamed by the per-sequence kernel (head_dim 128; ~0.1 us per 8 KB page-head)
+// SM time of one shared-prefix tile (128 query columns x 128 keys, a single-tile tensor-core CTA) in
+// page-heads streamed by the per-sequence kernel (head_dim 128; measured on config 4: ~2 us per tile per SM
+// against ~0.1 us per 8 KB page-head)
 #ifndef MLB_TILE_PAGE_HEADS
 #define MLB_TILE_PAGE_HEADS 19
 #endif
@@ -325,13 +326,13 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   // The shared-prefix kernel runs beside the per-sequence kernel, one CTA per SM: it gets the share of the
   // SMs that balances the two kernels' estimated SM time (all of them when no per-sequence work is left)
   int64_t tc_work = 0;
-  // a tensor-core CTA takes a pair of member blocks (two query tiles over the same pages)
-  auto pairs_of = [&](const ShareSet& set) {
-    const int64_t blocks = (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
-    return (blocks + 1) / 2;
+  // a tensor-core CTA takes one member block of a shared prefix (its single-tile pipeline double-buffers S,
+  // which measured faster there than two blocks per CTA)
+  auto blocks_of = [&](const ShareSet& set) {
+    return (static_cast<int64_t>(set.seqs.size()) + per_cta - 1) / per_cta;
   };
   for (const ShareSet& set : sets)
-    tc_work += pairs_of(set) * num_kv_heads * ((set.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit) *
+    tc_work += blocks_of(set) * num_kv_heads * ((set.pages + kMinPagesPerUnit - 1) / kMinPagesPerUnit) *
                kTilePageHeads;
   const int64_t priv_work = rest * num_kv_heads;
   const int64_t share_pct =
@@ -344,7 +345,7 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
     // as many pieces as keep every CTA in one wave of that share, each a whole number of 8-page (128-key)
     // tiles
     const int64_t target = std::max<int64_t>(1, static_cast<int64_t>(num_sms) * kSharedCtasPerSm * share_pct / 100);
-    int64_t pieces = std::max<int64_t>(1, target / (pairs_of(set) * num_kv_heads));
+    int64_t pieces = std::max<int64_t>(1, target / (blocks_of(set) * num_kv_heads));
     pieces = std::min<int64_t>(pieces, std::max(1, set.pages / kMinPagesPerUnit));
     int per = static_cast<int>((set.pages + pieces - 1) / pieces);
     per = (per + kMinPagesPerUnit - 1) / kMinPagesPerUnit * kMinPagesPerUnit;
@@ -444,7 +445,7 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
     return (x.page_end - x.page_begin) > (y.page_end - y.page_begin);
   });
 
-  // shared-prefix units: per piece, the member blocks in pairs (an odd last block gets an empty partner);
+  // shared-prefix units: per piece, one member block per pair with an empty partner (a single-tile CTA);
   // every pair of units (2i, 2i + 1) covers the same pages of the same table row, and pairs are ordered
   // largest first as whole pairs
   std::vector<std::array<mlb_shared_unit, 2>> pairs;
@@ -456,12 +457,12 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
       mems.push_back({s, qo_indptr[s], static_cast<int32_t>(base[seq_group[s]]), 0});
     const int nm = static_cast<int>(set.seqs.size());
     for (int piece = 0; piece < set_plans[k].pieces; ++piece)
-      for (int m = 0; m < nm; m += 2 * per_cta) {
+      for (int m = 0; m < nm; m += per_cta) {
         std::array<mlb_shared_unit, 2> pair{};
         for (int h = 0; h < 2; ++h) {
           mlb_shared_unit& u = pair[h];
-          u.member_begin = first + std::min(nm, m + h * per_cta);
-          u.member_count = std::max(0, std::min(per_cta, nm - m - h * per_cta));
+          u.member_begin = first + m;
+          u.member_count = h == 0 ? std::min(per_cta, nm - m) : 0;
           u.page_begin = piece * set_plans[k].per;
           u.page_end = std::min(set.pages, (piece + 1) * set_plans[k].per);
           u.piece = piece;

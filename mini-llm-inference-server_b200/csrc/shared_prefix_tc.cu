@@ -71,14 +71,18 @@ constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
 template <int DH>
 struct TcLayout {
-  static constexpr int kStages = DH == 128 ? 2 : 4;  // K + V stages that fit beside the two Q tiles
+  // K and V tiles in separate rings beside the two Q tiles: a K tile is free once both S products of its
+  // key tile are done, well before the V tile (both P . V products), so K runs further ahead
+  static constexpr int kKStages = DH == 128 ? 3 : 4;
+  static constexpr int kVStages = DH == 128 ? 2 : 4;
   static constexpr int kTileBytes = kTcTileTokens * DH * 2;  // one K or V tile, [DH/64][128][64] swizzled
   static constexpr int kQBytes = kTcRows * DH * 2;           // one query tile
-  static constexpr int kStageBytes = 2 * kTileBytes;
-  static constexpr int kStageOffset = 2 * kQBytes;
-  static constexpr int kBarOffset = kStageOffset + kStages * kStageBytes;
-  // barriers: full[S], empty[S], s_full[2], p_full[2], final, q_ready; then the TMEM base and the abort flag
-  static constexpr int kNumBars = 2 * kStages + 6;
+  static constexpr int kKOffset = 2 * kQBytes;
+  static constexpr int kVOffset = kKOffset + kKStages * kTileBytes;
+  static constexpr int kBarOffset = kVOffset + kVStages * kTileBytes;
+  // barriers: kfull[KS], kempty[KS], vfull[VS], vempty[VS], s_full[2], p_full[2], final, q_ready, o_done;
+  // then the TMEM base and the abort flag
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 7;
   static constexpr int kBytes = kBarOffset + 8 * kNumBars + 16;
   static constexpr int kLaunchBytes = kBytes + 1024;  // slack to align the base to 1024 (swizzle atoms)
 };
@@ -219,7 +223,7 @@ template <int DT, int DH>
 __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArgs a, const __grid_constant__ CUtensorMap tk,
                                                                           const __grid_constant__ CUtensorMap tv) {
   using L = TcLayout<DH>;
-  constexpr int NS = L::kStages;
+  constexpr int NK = L::kKStages, NV = L::kVStages;
   constexpr int CH = DH * 2 / 16;  // 16-byte chunks per row
   constexpr uint32_t kFmt = DT == MLB_BF16 ? 1u : 0u;
   constexpr uint32_t kIdescS = f16_idesc(kFmt, false, kTcRows, kTcTileTokens);
@@ -228,16 +232,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
-  uint64_t* full = bars;                   // [NS] a stage's K and V tiles have landed
-  uint64_t* empty = bars + NS;             // [NS] every MMA reading the stage has completed
-  uint64_t* s_full = bars + 2 * NS;        // [2] S_x of the next tile (and P_x . V of the one before) complete
-  uint64_t* p_full = bars + 2 * NS + 2;    // [2] P_x written into TMEM (128 softmax threads of tile x)
-  uint64_t* final_bar = bars + 2 * NS + 4;  // every MMA of the CTA has completed
-  uint64_t* q_ready = bars + 2 * NS + 5;    // both Q tiles are in shared memory (256 softmax threads)
+  uint64_t* kfull = bars;                   // [NK] a K stage has landed
+  uint64_t* kempty = bars + NK;             // [NK] both S products reading the K stage have completed
+  uint64_t* vfull = bars + 2 * NK;          // [NV] a V stage has landed
+  uint64_t* vempty = bars + 2 * NK + NV;    // [NV] both P . V products reading the V stage have completed
+  uint64_t* s_full = bars + 2 * (NK + NV);  // [2] S_x of the next tile (and P_x . V of the one before) complete
+  uint64_t* p_full = s_full + 2;            // [2] P_x written into TMEM (128 softmax threads of tile x)
+  uint64_t* final_bar = s_full + 4;         // every MMA of the CTA has completed
+  uint64_t* q_ready = s_full + 5;           // both Q tiles are in shared memory (256 softmax threads)
+  uint64_t* o_done = s_full + 6;            // single-tile CTA: the P . V products of a tile have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + L::kNumBars) + 1;
   const uint32_t q_smem = smem_u32(smem);  // Q_A, then Q_B
-  const uint32_t stage_smem = q_smem + L::kStageOffset;
+  const uint32_t k_smem = q_smem + L::kKOffset, v_smem = q_smem + L::kVOffset;
 
   griddep_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -260,9 +267,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   const int32_t* table = a.bt + static_cast<int64_t>(tseq) * a.bt_stride;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(full + s, kTcProducerWarps);
-      mbar_init(empty + s, 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(kfull + s, kTcProducerWarps);
+      mbar_init(kempty + s, 1);
+    }
+    for (int s = 0; s < NV; ++s) {
+      mbar_init(vfull + s, kTcProducerWarps);
+      mbar_init(vempty + s, 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(s_full + x, 1);
@@ -270,6 +281,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     }
     mbar_init(final_bar, 1);
     mbar_init(q_ready, 256);
+    mbar_init(o_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -307,89 +319,130 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         return mine && page < npages ? __ldg(table + pb + page) : 0;
       };
       int bid = load_bid(0);
+      // the warp waits for a ring slot on lane 0 and follows it (uniform exit on a timeout)
+      auto slot_free = [&](uint64_t* bar, uint32_t parity) {
+        int ok = 1;
+        if (lane == 0) ok = tc_wait(bar, parity, abort_flag, a.err) ? 1 : 0;
+        return __shfl_sync(0xffffffffu, ok, 0) != 0;
+      };
       for (int j = 0; j < ntiles; ++j) {
-        const int s = j % NS;
-        if (j >= NS) {  // lane 0 waits for the stage, the warp follows it (uniform exit on a timeout)
-          int ok = 1;
-          if (lane == 0) ok = tc_wait(empty + s, ((j / NS) + 1) & 1, abort_flag, a.err) ? 1 : 0;
-          if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        }
+        const int sk = j % NK, sv = j % NV;
         const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
         const int my_pages = live_pages > pw ? (live_pages - pw + kTcProducerWarps - 1) / kTcProducerWarps : 0;
-        const uint32_t kbase = stage_smem + s * L::kStageBytes, vbase = kbase + L::kTileBytes;
-        if (lane == 0) mbar_arrive_expect_tx(full + s, static_cast<uint32_t>(my_pages) * 2 * kHalves * kBoxBytes);
-        __syncwarp();
+        const uint32_t bytes = static_cast<uint32_t>(my_pages) * kHalves * kBoxBytes;
         const int next = load_bid(j + 1);
+        int slot = oob_slot;
         if (lane < my_pages) {
-          int slot = oob_slot;
           if (bid >= 0 && bid < a.num_blocks)
             slot = bid * kBlockSize;
           else
             flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-  #pragma unroll
-          for (int h = 0; h < kHalves; ++h) {
-            const uint32_t off = h * (kTcTileTokens * 128) + page_in_tile * (kBlockSize * 128);
-            tma_load_3d(kbase + off, &tk, h * 64, kvh, slot, full + s);
-            tma_load_3d(vbase + off, &tv, h * 64, kvh, slot, full + s);
-          }
+        }
+        const uint32_t off = page_in_tile * (kBlockSize * 128);
+        if (j >= NK && !slot_free(kempty + sk, ((j / NK) + 1) & 1)) break;
+        if (lane == 0) mbar_arrive_expect_tx(kfull + sk, bytes);
+        __syncwarp();
+        if (lane < my_pages) {
+#pragma unroll
+          for (int h = 0; h < kHalves; ++h)
+            tma_load_3d(k_smem + sk * L::kTileBytes + h * (kTcTileTokens * 128) + off, &tk, h * 64, kvh, slot,
+                        kfull + sk);
+        }
+        if (j >= NV && !slot_free(vempty + sv, ((j / NV) + 1) & 1)) break;
+        if (lane == 0) mbar_arrive_expect_tx(vfull + sv, bytes);
+        __syncwarp();
+        if (lane < my_pages) {
+#pragma unroll
+          for (int h = 0; h < kHalves; ++h)
+            tma_load_3d(v_smem + sv * L::kTileBytes + h * (kTcTileTokens * 128) + off, &tv, h * 64, kvh, slot,
+                        vfull + sv);
         }
         bid = next;
       }
     } else {
       // ------------------------------------------------------------ MMA issuer (one thread)
-      // Per tile j: O_A += P_A(j) . V_j, S_A(j+1) = Q_A . K_{j+1}^T, commit s_full[A]; then the same for B,
-      // with the stage released (empty) once both P . V of tile j are issued.  While softmax A works on its
-      // scores the tensor core runs B's products, and the other way round.  Issued MMAs execute in order, so
-      // S_x(j+1) overwrites the TMEM columns holding P_x(j) only after P_x(j) . V_j has read them.
+      // Paired CTA, per tile j: O_A += P_A(j) . V_j, S_A(j+1) = Q_A . K_{j+1}^T, commit s_full[A]; then the
+      // same for B; a K stage is released once both S products of its tile are issued, a V stage once both
+      // P . V products are.  While softmax A works on its scores the tensor core runs B's products, and the
+      // other way round.  Issued MMAs execute in order, so S_x(j+1) overwrites the TMEM columns holding
+      // P_x(j) only after P_x(j) . V_j has read them.
+      // Single-tile CTA: S is double-buffered in TMEM (tile j in buffer j % 2, the columns tile B would use),
+      // so S(j+1) is issued before O += P(j) . V_j and the tensor core computes the next scores while the
+      // softmax works; o_done tells the softmax when the P . V products before its tile have completed.
       if (lane == 0) {
-        auto issue_s = [&](int x, int j) {  // S_x = Q_x . K_j^T (K = Dh in steps of 16)
-          const uint32_t kb = stage_smem + (j % NS) * L::kStageBytes, qx = q_smem + x * L::kQBytes;
-  #pragma unroll
+        auto issue_s = [&](uint32_t s_col, int x, int j) {  // S = Q_x . K_j^T (K = Dh in steps of 16)
+          const uint32_t kb = k_smem + (j % NK) * L::kTileBytes, qx = q_smem + x * L::kQBytes;
+#pragma unroll
           for (int ks = 0; ks < DH / 16; ++ks) {
             const uint32_t off = (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32;
-            umma_ss(tmem + col_s(x), sw128_desc(qx + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
+            umma_ss(tmem + s_col, sw128_desc(qx + off, 16, 1024), sw128_desc(kb + off, 16, 1024), kIdescS,
                     ks > 0 ? 1u : 0u);
           }
         };
-        auto issue_pv = [&](int x, int j) {  // O_x += P_x . V_j, one k-step of 16 keys per loaded page
-          const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
+        auto issue_pv = [&](uint32_t o_col, uint32_t p_col, int j) {  // O += P . V_j, one k-step per loaded page
+          const uint32_t vb = v_smem + (j % NV) * L::kTileBytes;
           const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
           for (int ks = 0; ks < live_pages; ++ks)
-            umma_ts(tmem + col_o<DH>(x), tmem + col_s(x) + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
+            umma_ts(tmem + o_col, tmem + p_col + ks * 8, sw128_desc(vb + ks * 16 * 128, kTcRows * 128, 1024),
                     kIdescO, (j > 0 || ks > 0) ? 1u : 0u);
         };
-        bool ok = ntiles > 0 && tc_wait(q_ready, 0, abort_flag, a.err) && tc_wait(full, 0, abort_flag, a.err);
-        if (ok) {
+        auto wait_k = [&](int j) {
+          if (!tc_wait(kfull + j % NK, (j / NK) & 1, abort_flag, a.err)) return false;
           fence_proxy_async_smem();
           tc_fence_after();
-          issue_s(0, 0);
-          umma_commit(s_full);
-          if (two) {
-            issue_s(1, 0);
-            umma_commit(s_full + 1);
-          }
-        }
-        for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
-          const bool more = j + 1 < ntiles;
-          if (!tc_wait(p_full, j & 1, abort_flag, a.err)) break;
+          return true;
+        };
+        auto wait_v = [&](int j) {
+          if (!tc_wait(vfull + j % NV, (j / NV) & 1, abort_flag, a.err)) return false;
+          fence_proxy_async_smem();
           tc_fence_after();
-          issue_pv(0, j);
-          if (more) {
-            if (!tc_wait(full + (j + 1) % NS, ((j + 1) / NS) & 1, abort_flag, a.err)) break;
-            fence_proxy_async_smem();
-            tc_fence_after();
-            issue_s(0, j + 1);
+          return true;
+        };
+        bool ok = ntiles > 0 && tc_wait(q_ready, 0, abort_flag, a.err);
+        if (two) {
+          if (ok && wait_k(0)) {
+            issue_s(col_s(0), 0, 0);
+            umma_commit(s_full);
+            issue_s(col_s(1), 1, 0);
+            umma_commit(s_full + 1);
+            umma_commit(kempty);  // K tile 0 is free once both its S products are done
+          } else {
+            ok = false;
           }
-          umma_commit(s_full);
-          if (two) {
+          for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
+            const bool more = j + 1 < ntiles;
+            if (!tc_wait(p_full, j & 1, abort_flag, a.err) || !wait_v(j)) break;
+            issue_pv(col_o<DH>(0), col_s(0), j);
+            if (more) {
+              if (!wait_k(j + 1)) break;
+              issue_s(col_s(0), 0, j + 1);
+            }
+            umma_commit(s_full);
             if (!tc_wait(p_full + 1, j & 1, abort_flag, a.err)) break;
             tc_fence_after();
-            issue_pv(1, j);
-            umma_commit(empty + j % NS);
-            if (more) issue_s(1, j + 1);
+            issue_pv(col_o<DH>(1), col_s(1), j);
+            umma_commit(vempty + j % NV);
+            if (more) {
+              issue_s(col_s(1), 1, j + 1);
+              umma_commit(kempty + (j + 1) % NK);
+            }
             umma_commit(s_full + 1);
-          } else {
-            umma_commit(empty + j % NS);
+          }
+        } else {
+          for (int j = 0; ok && j <= ntiles && !*abort_flag; ++j) {
+            if (j < ntiles) {
+              if (!wait_k(j)) break;
+              issue_s(col_s(j & 1), 0, j);
+              umma_commit(s_full + (j & 1));
+              umma_commit(kempty + j % NK);
+            }
+            if (j >= 1) {
+              const int jj = j - 1;
+              if (!tc_wait(p_full + (jj & 1), (jj >> 1) & 1, abort_flag, a.err) || !wait_v(jj)) break;
+              issue_pv(col_o<DH>(0), col_s(jj & 1), jj);
+              umma_commit(vempty + jj % NV);
+              umma_commit(o_done);
+            }
           }
         }
         umma_commit(final_bar);  // every MMA issued above has completed when this arrives
@@ -427,7 +480,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     mbar_arrive(q_ready);
     const bool active = x == 0 || two;
     const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t s_cols = tmem + lanes + col_s(x), o_cols = tmem + lanes + col_o<DH>(x);
+    const uint32_t o_cols = tmem + lanes + col_o<DH>(x);
     // kind 1: key position of the tile's first token, and this column's exclusive causal key limit
     const int first_pos = tile_unit ? __ldg(a.seq_lens + tseq) - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) +
                                           (mb - __ldg(a.qo + tseq))
@@ -436,6 +489,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     const int seq_len = tile_unit ? __ldg(a.seq_lens + tseq) : INT_MAX;
     float m_used = kNegInfF, l = 0.f;
     bool ok = true;
+    // a wait before warp-collective TMEM loads / stores: every lane gets the same answer, so a timeout seen
+    // by some lanes never splits the warp at a tcgen05 .sync.aligned instruction
+    auto wait_warp = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, tc_wait(bar, parity, abort_flag, a.err) ? 1 : 0) != 0;
+    };
     for (int j = 0; active && j < ntiles; ++j) {
       // keys of this tile: full pages up to the unit's end, minus pages with an out-of-range block id
       // (lane p checks page p; loaded before the wait so the round trip overlaps it), minus (kind 1) keys
@@ -443,7 +501,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
       int my_bid = 0;
       if (lane < live_pages) my_bid = __ldg(table + pb + j * kTcTilePages + lane);
-      if (!tc_wait(s_full + x, j & 1, abort_flag, a.err)) {
+      // S buffer of this tile: the tile's own (paired) or tile j's of the two (single, double-buffered)
+      const int buf = two ? x : (j & 1);
+      const uint32_t s_cols = tmem + lanes + col_s(buf);
+      if (!wait_warp(s_full + buf, two ? (j & 1) : ((j >> 1) & 1))) {
         ok = false;
         break;
       }
@@ -478,7 +539,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
         // before they release P_A; the MMA issues P_B . V after P_A . V)
         const int r0 = max(0, seq_len - tile_key0), r1 = live_pages * kBlockSize;
         if (r0 < r1) {
-          const uint32_t vb = stage_smem + (j % NS) * L::kStageBytes + L::kTileBytes;
+          // the V tile has its own barrier: its rows must have landed before they are cleared
+          if (!wait_warp(vfull + j % NV, (j / NV) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t vb = v_smem + (j % NV) * L::kTileBytes;
           constexpr int kRowItems = (DH / 64) * 8;  // 16-byte chunks of one row, both halves
           for (int e = row; e < (r1 - r0) * kRowItems; e += 128) {
             const int r = r0 + e / kRowItems, h = (e % kRowItems) / 8, c = e % 8;
@@ -491,7 +557,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const bool need = mx > m_used + 8.f;
       if (__any_sync(0xffffffffu, need)) {
         const float m_new = need ? fmaxf(m_used, mx) : m_used;
-        if (j > 0) {  // P_x(j-1) . V has completed: s_full[x] of this tile was committed after it
+        if (j > 0) {  // paired: P_x(j-1) . V has completed (s_full[x] of this tile was committed after it)
+          if (!two && !wait_warp(o_done, (j - 1) & 1)) {  // single: wait for it
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const float alpha = m_new == m_used ? 1.f : fast_exp2(m_used - m_new);
 #pragma unroll
           for (int i = 0; i < DH / 32; ++i) {
@@ -545,10 +616,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       l += sum;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full + x);
+      mbar_arrive(p_full + buf);
     }
     // O is complete when final_bar (committed once, after every MMA) arrives
-    if (active && ok && ntiles > 0 && tc_wait(final_bar, 0, abort_flag, a.err) && !*abort_flag) {
+    if (active && ok && ntiles > 0 && wait_warp(final_bar, 0) && !*abort_flag) {
       tc_fence_after();
       const int m = row / a.group;
       const int head = kvh * a.group + row % a.group;

@@ -321,7 +321,7 @@ def _prefix_step(suffix_lo: int, suffix_hi: int, rows: int = 128, prefix_pages: 
     return list(range(rows + 1)), lens, host
 
 
-EXPECTED_SHARED_CTAS = {"config4": 64, "tiny": 128, "long": 32}  # CTAs = pairs x KV heads x pieces
+EXPECTED_SHARED_CTAS = {"config4": 96, "tiny": 128, "long": 32}  # CTAs = blocks x KV heads x pieces
 
 
 def test_planner_balances_shared_ctas_against_private_work(mlb):
