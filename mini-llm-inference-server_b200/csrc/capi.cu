@@ -60,7 +60,10 @@ bool aligned(const void* p, int a) { return (reinterpret_cast<uintptr_t>(p) % a)
 
 constexpr int kMinPagesPerUnit = 8;  // below this a unit's pipeline start-up dominates
 constexpr int kCtasPerSm = 3;        // resident paged-attention CTAs per SM (shared memory bound)
-constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best)
+constexpr int kWaveTenths = 13;      // the auto split aims for 1.3 waves of resident CTAs (measured best) ...
+constexpr int kEqualWaveHundredths = 155;  // ... 1.55 waves when every row's pages are the same length ...
+constexpr int kSmallWorkPages = 64;        // ... and 0.55 waves when the step has under 64 page-heads per
+constexpr int kSmallWaveHundredths = 55;   //     CTA slot (per-CTA start and split-K rows then dominate)
 constexpr int kSharedColumns = 128;  // query columns (member rows x group) per shared-prefix unit: MMA M
 constexpr int kSharedCtasPerSm = 1;  // resident shared-prefix CTAs per SM (the tcgen05 kernel's smem/TMEM)
 // SM time of one shared-prefix tile (128 query columns x 128 keys, a single-tile tensor-core CTA) in
@@ -355,10 +358,36 @@ int mlb_plan_attention(const int32_t* qo_indptr, const int32_t* seq_lens, int nu
   }
 
   // ---- regular units over each group's pages [start, pages)
+  // Split size (pages per unit).  Measured on B200 with every layer's launch back to back, one rank of
+  // KV-head sharding emulated on one GPU (1 / 2 / 4 / 8 KV heads):
+  // - rows of varied length (config 2, 64 rows): 1.3 waves of resident CTAs is best while the work is large
+  //   (8 heads: 101 us; 1.5 waves 105, 2.2 waves 108), but with under 64 page-heads per CTA slot fewer,
+  //   longer units win (1 head: 0.5 waves 19.8 us against 24.3 at 1.3; 2 heads: 32.8 against 37.2);
+  // - rows of one length (config 5, 29 x 8192 pages): a last wave under half full costs a whole unit time
+  //   (4 heads: 1.31 waves 1358 us, 1.05 waves 1444, 1.57 waves 1190 = 1/2 of the 8-head time), so every row
+  //   gets the same number of units and they fill ~1.55 waves.
   int64_t chunk = pages_per_unit;
   if (chunk <= 0) {
-    const int64_t target_ctas = static_cast<int64_t>(num_sms) * kCtasPerSm * kWaveTenths / 10;
-    chunk = std::max<int64_t>(kMinPagesPerUnit, (rest * num_kv_heads + target_ctas - 1) / target_ctas);
+    const int64_t slots = static_cast<int64_t>(num_sms) * kCtasPerSm;
+    const int64_t work = rest * num_kv_heads;  // page-heads left to the per-sequence kernel
+    int64_t gmin = INT64_MAX, gmax = 0, ngroups = 0;
+    for (const Group& g : groups) {
+      const int64_t own = g.pages - g.start;
+      if (own <= 0) continue;
+      gmin = std::min(gmin, own);
+      gmax = std::max(gmax, own);
+      ++ngroups;
+    }
+    if (ngroups > 0 && gmax - gmin <= gmax / 64 && gmax >= 2 * kMinPagesPerUnit) {
+      const int64_t want = (slots * kEqualWaveHundredths + 99) / 100;  // CTAs
+      int64_t k = (want + ngroups * num_kv_heads - 1) / (ngroups * num_kv_heads);  // units per row
+      k = std::max<int64_t>(1, std::min<int64_t>(k, gmax / kMinPagesPerUnit));
+      chunk = (gmax + k - 1) / k;
+    } else {
+      const int64_t hundredths = work < slots * kSmallWorkPages ? kSmallWaveHundredths : kWaveTenths * 10;
+      const int64_t target_ctas = std::max<int64_t>(1, slots * hundredths / 100);
+      chunk = std::max<int64_t>(kMinPagesPerUnit, (work + target_ctas - 1) / target_ctas);
+    }
   }
   std::vector<mlb_work_unit> out;
   out.reserve(groups.size());

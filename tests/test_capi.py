@@ -238,6 +238,31 @@ def test_planner_auto_split_targets_waves_of_ctas(mlb):
     assert p.num_partial_rows > 0
 
 
+@pytest.mark.parametrize("hkv", [1, 2, 4, 8])
+def test_planner_fills_about_one_and_a_half_waves_with_equal_rows(mlb, hkv):
+    """Rows of one length (29 x 8192 pages, one rank of KV-head sharding at 8 / 4 / 2 / 1
+    heads): every row gets the same number of units and the CTAs fill ~1.55 waves of 3 per SM, so the last
+    wave is more than half full (a thin last wave measured up to 20% slower)."""
+    steps = [(131071, 1)] * 29
+    p, _, _ = plan(mlb, steps, h=4 * hkv, hkv=hkv)
+    per_row = np.bincount(p.units_host[:, 0], minlength=29)
+    assert len(set(per_row.tolist())) == 1
+    waves = p.num_units * hkv / (148 * 3)
+    assert 1.5 <= waves <= 1.7
+
+
+def test_planner_uses_fewer_longer_units_when_the_step_is_small(mlb):
+    """Under 64 page-heads per CTA slot (config 2's 64 rows at one or two KV heads per GPU) the split aims at
+    ~0.55 waves: per-CTA start-up and split-K rows cost more than the parallelism buys."""
+    r = random.Random(0)
+    steps = [(r.randint(512, 4096) - 1, 1) for _ in range(64)]
+    for hkv in (1, 2):
+        p, _, _ = plan(mlb, steps, h=4 * hkv, hkv=hkv)
+        assert 0.45 <= p.num_units * hkv / (148 * 3) <= 0.8
+    p8, _, _ = plan(mlb, steps, h=32, hkv=8)
+    assert p8.num_units * 8 / (148 * 3) >= 1.3  # a large step keeps >= 1.3 waves
+
+
 def test_planner_finds_shared_prefixes(mlb):
     """Decode rows whose tables start with the same blocks get shared-prefix units over those pages; their
     own units start after the prefix, and the pieces line up with the partial rows."""
