@@ -7,9 +7,14 @@ Several GPUs (config 2): rank r of N owns KV heads [8r/N, 8(r+1)/N) of every seq
 batch is 64 x N sequences (weak scaling: each rank reads one GPU's worth of KV bytes, as serving with N
 GPUs runs N times the batch); --scaling strong keeps batch 64 and splits its heads.
 
-The default (config 2) is the headline line.  --config 3/4/5 print the same kind of line for BASELINE's
-mixed continuous-batching step, prefix-sharing step (copy-on-write) and long-context eviction step
-(compaction), each described in its builder below.
+The default (config 2) is the headline line.  At N=1 it also carries `configs` (4, 5:
+the mixed continuous-batching step, the prefix-sharing step with copy-on-write, the long-context eviction
+step with compaction, each described in its builder below), `flashinfer_decode` (the reference's CUDA
+backend timed on the same pages) and `e2e_reference_metadata` (the end-to-end loop handing the backend an
+object with only the reference's AttentionMetadata fields).  At N>1 it carries `strong`: KV-head sharding
+of a fixed workload (config 2 at batch 64 and config 5) with each rank's attention time and the per-layer
+gather + barrier time.  Every sub-object ends with a spot check of sampled rows against a plain torch fp32
+attention over the same pages.  --config 3/4/5 print a line of their own for one workload.
 
 Workload (config 2): bf16, 32 query heads, 8 KV heads, head_dim 128, block_size 16, batch 64, context
 lengths U[512, 4096] (seeded), block tables a seeded shuffle of a pool sized 1.25x the blocks needed,
