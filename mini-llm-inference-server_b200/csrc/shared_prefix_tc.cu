@@ -6,33 +6,35 @@
 // multi-token row (kind 1, causal keys).  That is a small FlashAttention forward: S = Q . K^T over the pages,
 // online softmax, O = P . V, with M = 128 query columns (the TMEM lanes) and 128 keys (8 pages) per tile.
 //
-// One CTA takes a PAIR of units over the same pages (the planner makes them: two member blocks of one
-// prefix piece, or two neighbouring tiles of one row over the later tile's keys), so every K / V tile is
-// loaded once for 256 query columns and two softmax warpgroups work side by side: while one exponentiates
-// its tile's scores, the tensor core runs the other tile's products.
+// A CTA takes a PAIR of units over the same pages (the planner makes them: two neighbouring query tiles of
+// one row over the later tile's keys), so every K / V tile is loaded once for 256 query columns and two
+// softmax warpgroups work side by side, or a SINGLE unit (a shared prefix's member block), whose scores are
+// triple-buffered in TMEM so the tensor core computes the next two tiles' scores while the softmax works.
 //
-// Roles in one CTA of 384 threads (1 CTA per SM: two Q tiles + 2 (Dh 128) or 4 (Dh 64) K/V stages of shared
-// memory, all 512 TMEM columns):
-// - warps 0, 2, 3: the producers (one lane per page).  Each page of a tile is 2 x Dh/64 TMA boxes (tensor
-//   maps over the K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle), landing in the K-major
-//   layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts the bytes (expect_tx).
-//   A block id out of range gets a slot coordinate past the pool's end: TMA fills zeros there and the
-//   softmax masks the page.  No multicast.
-// - warp 1, one thread: the MMA issuer.  Per tile j and query tile x (A, then B): O_x += P_x(j) . V_j with
-//   P read from TMEM (A operand) and V as an MN-major B operand (one k-step of 16 keys per loaded page, so
-//   pages past the unit's end are never read), then S_x(j+1) = Q_x . K_{j+1}^T, committed to s_full[x]; the
-//   stage is released (empty) once both products of tile j are issued.
+// Roles in one CTA of 384 threads (1 CTA per SM: two Q tiles + 3 K and 2 V stages (Dh 128) or 4 + 4 (Dh 64)
+// of shared memory, all 512 TMEM columns):
+// - warp 0 fills the K ring and warp 2 the V ring (one lane per page; warp 3 idles).  Each page of a tile is
+//   Dh/64 TMA boxes (tensor maps over the K and V pools: {64 dims, 1 KV head, 16 slots}, 128-byte swizzle),
+//   landing in the K-major layout the MMA reads ([Dh/64][128 rows][64]); the stage's "full" barrier counts
+//   the bytes (expect_tx).  With a warp per ring a K tile never waits behind a V slot.  A block id out of
+//   range gets a slot coordinate past the pool's end: TMA fills zeros there and the softmax masks the page.
+//   No multicast.
+// - warp 1, one thread: the MMA issuer.  Paired, per tile j and query tile x (A, then B): O_x += P_x(j) . V_j
+//   with P read from TMEM (A operand) and V as an MN-major B operand (one k-step of 16 keys per loaded page,
+//   so pages past the unit's end are never read), then S_x(j+1) = Q_x . K_{j+1}^T, committed to s_full[x].
+//   Single: S(0), S(1), then per tile j: O += P(j) . V_j and S(j+2) into the buffer P(j-1) held.
 // - warps 4-7 (tile A) and 8-11 (tile B), one thread = one query column = one TMEM lane: the whole S row
 //   comes out of TMEM in one go (4 loads, one wait) for the masked max (exp2 domain), and P = 2^(s - m),
 //   packed to 16 bits, goes back over the first 64 columns of the same S buffer; row sums in fp32.  The 128
 //   scores per thread need more than the 168 registers 384 threads get at launch: warps 0-3 give theirs up
 //   (setmaxnreg.dec to 56) and the softmax warps take them (setmaxnreg.inc to 224).  O is rescaled (TMEM load /
 //   scale / store) only when a row's max grows by more than 8 (a factor 256 of headroom keeps P and the
-//   sums finite), which after the first tiles is rare; s_full[x] of tile j is committed after P_x(j-1) . V,
-//   so O_x is quiet then.  At the end (the "final" barrier, committed behind the last MMA) every column's
-//   normalised O row and log2-sum-exp go to its split-K partial row, merged by the reduction (an unsplit
-//   query tile stores its final rows).
-// TMEM columns: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B [256 + Dh, 256 + 2 Dh).
+//   sums finite), which after the first tiles is rare; the rescale first waits for the P . V products
+//   before it.  At the end (the "final" barrier, committed behind the last MMA) every column's normalised O
+//   row and log2-sum-exp go to its split-K partial row, merged by the reduction (an unsplit query tile
+//   stores its final rows).
+// TMEM columns, paired: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B [256 + Dh, 256 + 2 Dh);
+// single: S buffers [0,128), [128,256), [256,384), O [384, 384 + Dh).
 //
 // Every wait is bounded (time and polls); on expiry the CTA raises MLB_DEV_WAIT_TIMEOUT, drains its own
 // copies and MMAs, frees TMEM and returns.
@@ -54,7 +56,6 @@ constexpr int kTcThreads = 384;     // 12 warps: 3 producers, the MMA issuer, tw
 constexpr int kTcRows = 128;        // query columns per tile = MMA M = TMEM lanes
 constexpr int kTcTileTokens = 128;  // keys per tile = N of S = Q . K^T
 constexpr int kTcTilePages = kTcTileTokens / kBlockSize;
-constexpr int kTcProducerWarps = 3;  // warps 0, 2, 3
 constexpr uint32_t kTmemCols = 512;
 // registers per thread: at launch (384 threads on one SM), after the split for warps 0-3 and for the softmax
 constexpr int kRegsLaunch = 168, kRegsLow = 56, kRegsHigh = 224;
@@ -63,6 +64,8 @@ static_assert(kRegsLaunch * kTcThreads <= 65536, "one CTA per SM");
 // TMEM columns: S_A [0,128), S_B [128,256), O_A [256, 256 + Dh), O_B after it; P_x (16-bit pairs) over the
 // first 64 columns of S_x
 __device__ __forceinline__ uint32_t col_s(int x) { return x ? 128u : 0u; }
+// a single-tile CTA: S buffers b = 0, 1, 2 at [128 b, 128 b + 128), O at [384, 384 + Dh)
+constexpr uint32_t kSingleO = 384;
 template <int DH>
 __device__ __forceinline__ uint32_t col_o(int x) {
   return 256u + (x ? static_cast<uint32_t>(DH) : 0u);
@@ -80,9 +83,9 @@ struct TcLayout {
   static constexpr int kKOffset = 2 * kQBytes;
   static constexpr int kVOffset = kKOffset + kKStages * kTileBytes;
   static constexpr int kBarOffset = kVOffset + kVStages * kTileBytes;
-  // barriers: kfull[KS], kempty[KS], vfull[VS], vempty[VS], s_full[2], p_full[2], final, q_ready, o_done;
+  // barriers: kfull[KS], kempty[KS], vfull[VS], vempty[VS], s_full[3], p_full[3], final, q_ready, o_done;
   // then the TMEM base and the abort flag
-  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 7;
+  static constexpr int kNumBars = 2 * kKStages + 2 * kVStages + 9;
   static constexpr int kBytes = kBarOffset + 8 * kNumBars + 16;
   static constexpr int kLaunchBytes = kBytes + 1024;  // slack to align the base to 1024 (swizzle atoms)
 };
@@ -236,11 +239,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
   uint64_t* kempty = bars + NK;             // [NK] both S products reading the K stage have completed
   uint64_t* vfull = bars + 2 * NK;          // [NV] a V stage has landed
   uint64_t* vempty = bars + 2 * NK + NV;    // [NV] both P . V products reading the V stage have completed
-  uint64_t* s_full = bars + 2 * (NK + NV);  // [2] S_x of the next tile (and P_x . V of the one before) complete
-  uint64_t* p_full = s_full + 2;            // [2] P_x written into TMEM (128 softmax threads of tile x)
-  uint64_t* final_bar = s_full + 4;         // every MMA of the CTA has completed
-  uint64_t* q_ready = s_full + 5;           // both Q tiles are in shared memory (256 softmax threads)
-  uint64_t* o_done = s_full + 6;            // single-tile CTA: the P . V products of a tile have completed
+  uint64_t* s_full = bars + 2 * (NK + NV);  // [3] an S buffer holds its tile's scores (paired: S_x, x < 2)
+  uint64_t* p_full = s_full + 3;            // [3] P written over that buffer (128 softmax threads)
+  uint64_t* final_bar = s_full + 6;         // every MMA of the CTA has completed
+  uint64_t* q_ready = s_full + 7;           // both Q tiles are in shared memory (256 softmax threads)
+  uint64_t* o_done = s_full + 8;            // single-tile CTA: the P . V products of a tile have completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + L::kNumBars) + 1;
   const uint32_t q_smem = smem_u32(smem);  // Q_A, then Q_B
@@ -268,16 +271,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NK; ++s) {
-      mbar_init(kfull + s, kTcProducerWarps);
+      mbar_init(kfull + s, 1);
       mbar_init(kempty + s, 1);
     }
     for (int s = 0; s < NV; ++s) {
-      mbar_init(vfull + s, kTcProducerWarps);
+      mbar_init(vfull + s, 1);
       mbar_init(vempty + s, 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      mbar_init(s_full + x, 1);
-      mbar_init(p_full + x, 128);
+    for (int b = 0; b < 3; ++b) {
+      mbar_init(s_full + b, 1);
+      mbar_init(p_full + b, 128);
     }
     mbar_init(final_bar, 1);
     mbar_init(q_ready, 256);
@@ -303,61 +306,53 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     // warpgroup 0 gives up registers, all four warps at the same instruction
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsLow));
     if (warp != 1) {
-      // ------------------------------------------------------------ producers (warps 0, 2, 3): TMA boxes
-      // Producer warp w (index pw 0..2) owns pages pw, pw + 3, pw + 6 of each tile, one per lane: the lane
-      // loads its page's block id one tile ahead (the table round trip overlaps the previous tile) and
-      // issues the page's 2 x Dh/64 boxes; the warp's lane 0 declares the warp's bytes on the stage barrier
-      // (3 arrivals per phase).  Three warps issue a tile's boxes in parallel.
-      constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
-      constexpr int kHalves = DH / 64;
-      const int pw = warp == 0 ? 0 : warp - 1;
-      const int page_in_tile = pw + kTcProducerWarps * lane;
-      const bool mine = lane < (kTcTilePages - pw + kTcProducerWarps - 1) / kTcProducerWarps;
-      const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
-      auto load_bid = [&](int j) {
-        const int page = j * kTcTilePages + page_in_tile;
-        return mine && page < npages ? __ldg(table + pb + page) : 0;
-      };
-      int bid = load_bid(0);
-      // the warp waits for a ring slot on lane 0 and follows it (uniform exit on a timeout)
-      auto slot_free = [&](uint64_t* bar, uint32_t parity) {
-        int ok = 1;
-        if (lane == 0) ok = tc_wait(bar, parity, abort_flag, a.err) ? 1 : 0;
-        return __shfl_sync(0xffffffffu, ok, 0) != 0;
-      };
-      for (int j = 0; j < ntiles; ++j) {
-        const int sk = j % NK, sv = j % NV;
-        const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
-        const int my_pages = live_pages > pw ? (live_pages - pw + kTcProducerWarps - 1) / kTcProducerWarps : 0;
-        const uint32_t bytes = static_cast<uint32_t>(my_pages) * kHalves * kBoxBytes;
-        const int next = load_bid(j + 1);
-        int slot = oob_slot;
-        if (lane < my_pages) {
-          if (bid >= 0 && bid < a.num_blocks)
-            slot = bid * kBlockSize;
-          else
-            flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-        }
-        const uint32_t off = page_in_tile * (kBlockSize * 128);
-        if (j >= NK && !slot_free(kempty + sk, ((j / NK) + 1) & 1)) break;
-        if (lane == 0) mbar_arrive_expect_tx(kfull + sk, bytes);
-        __syncwarp();
-        if (lane < my_pages) {
+      // ------------------------------------------------------------ producers: warp 0 fills the K ring,
+      // warp 2 the V ring (warp 3 has no role), so a K tile never queues behind a V slot: the K ring runs up
+      // to kKStages tiles ahead of the scores while V stages wait for their P . V products.  Lane p loads
+      // page p's block id one tile ahead (the table round trip overlaps the previous tile) and issues the
+      // page's Dh/64 boxes; lane 0 declares the tile's bytes on the stage barrier (one arrival per phase).
+      if (warp != 3) {
+        constexpr uint32_t kBoxBytes = 64 * 2 * kBlockSize;  // {64 dims, 1 head, 16 slots}
+        constexpr int kHalves = DH / 64;
+        const bool is_v = warp == 2;
+        const int stages = is_v ? NV : NK;
+        uint64_t* full = is_v ? vfull : kfull;
+        uint64_t* empty = is_v ? vempty : kempty;
+        const uint32_t ring = is_v ? v_smem : k_smem;
+        const CUtensorMap* map = is_v ? &tv : &tk;
+        const int oob_slot = static_cast<int>(a.num_blocks * kBlockSize);  // past the end: zero fill
+        auto load_bid = [&](int j) {
+          const int page = j * kTcTilePages + lane;
+          return lane < kTcTilePages && page < npages ? __ldg(table + pb + page) : 0;
+        };
+        int bid = load_bid(0);
+        for (int j = 0; j < ntiles; ++j) {
+          const int st = j % stages;
+          const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
+          const uint32_t bytes = static_cast<uint32_t>(live_pages) * kHalves * kBoxBytes;
+          const int next = load_bid(j + 1);
+          int slot = oob_slot;
+          if (lane < live_pages) {
+            if (bid >= 0 && bid < a.num_blocks)
+              slot = bid * kBlockSize;
+            else
+              flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+          }
+          if (j >= stages) {  // the warp waits for the ring slot on lane 0 and follows it (uniform exit)
+            int ok = 1;
+            if (lane == 0) ok = tc_wait(empty + st, ((j / stages) + 1) & 1, abort_flag, a.err) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok, 0) == 0) break;
+          }
+          if (lane == 0) mbar_arrive_expect_tx(full + st, bytes);
+          __syncwarp();
+          if (lane < live_pages) {
 #pragma unroll
-          for (int h = 0; h < kHalves; ++h)
-            tma_load_3d(k_smem + sk * L::kTileBytes + h * (kTcTileTokens * 128) + off, &tk, h * 64, kvh, slot,
-                        kfull + sk);
+            for (int h = 0; h < kHalves; ++h)
+              tma_load_3d(ring + st * L::kTileBytes + h * (kTcTileTokens * 128) + lane * (kBlockSize * 128), map,
+                          h * 64, kvh, slot, full + st);
+          }
+          bid = next;
         }
-        if (j >= NV && !slot_free(vempty + sv, ((j / NV) + 1) & 1)) break;
-        if (lane == 0) mbar_arrive_expect_tx(vfull + sv, bytes);
-        __syncwarp();
-        if (lane < my_pages) {
-#pragma unroll
-          for (int h = 0; h < kHalves; ++h)
-            tma_load_3d(v_smem + sv * L::kTileBytes + h * (kTcTileTokens * 128) + off, &tv, h * 64, kvh, slot,
-                        vfull + sv);
-        }
-        bid = next;
       }
     } else {
       // ------------------------------------------------------------ MMA issuer (one thread)
@@ -366,9 +361,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       // P . V products are.  While softmax A works on its scores the tensor core runs B's products, and the
       // other way round.  Issued MMAs execute in order, so S_x(j+1) overwrites the TMEM columns holding
       // P_x(j) only after P_x(j) . V_j has read them.
-      // Single-tile CTA: S is double-buffered in TMEM (tile j in buffer j % 2, the columns tile B would use),
-      // so S(j+1) is issued before O += P(j) . V_j and the tensor core computes the next scores while the
-      // softmax works; o_done tells the softmax when the P . V products before its tile have completed.
+      // Single-tile CTA: S is triple-buffered in TMEM (tile j in buffer j % 3), so two tiles of scores are
+      // issued ahead of the softmax and P(j) . V_j -> S(j+2) runs while it works on tile j+1 (with two
+      // buffers, S(j+1) queued behind P(j-1) . V and the softmax waited for it about a quarter of every
+      // tile); o_done tells the softmax when the P . V products before its tile have completed.
       if (lane == 0) {
         auto issue_s = [&](uint32_t s_col, int x, int j) {  // S = Q_x . K_j^T (K = Dh in steps of 16)
           const uint32_t kb = k_smem + (j % NK) * L::kTileBytes, qx = q_smem + x * L::kQBytes;
@@ -429,19 +425,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
             umma_commit(s_full + 1);
           }
         } else {
-          for (int j = 0; ok && j <= ntiles && !*abort_flag; ++j) {
-            if (j < ntiles) {
-              if (!wait_k(j)) break;
-              issue_s(col_s(j & 1), 0, j);
-              umma_commit(s_full + (j & 1));
-              umma_commit(kempty + j % NK);
+          // single tile, S triple-buffered (buffer j % 3 at column 128 (j % 3), O after them): S(0) and S(1)
+          // first, then per tile j: O += P(j) . V_j once P(j) is in, and S(j + 2) into the buffer P(j - 1)
+          // held (its P . V was issued before it: in order).  The scores of the next two tiles are computed
+          // while the softmax works, so P(j) . V -> S(j + 2) is off the softmax's path.
+          for (int j = 0; ok && j < ntiles && j < 2; ++j) {
+            if (!wait_k(j)) {
+              ok = false;
+              break;
             }
-            if (j >= 1) {
-              const int jj = j - 1;
-              if (!tc_wait(p_full + (jj & 1), (jj >> 1) & 1, abort_flag, a.err) || !wait_v(jj)) break;
-              issue_pv(col_o<DH>(0), col_s(jj & 1), jj);
-              umma_commit(vempty + jj % NV);
-              umma_commit(o_done);
+            issue_s(kTcRows * j, 0, j);
+            umma_commit(s_full + j);
+            umma_commit(kempty + j % NK);
+          }
+          for (int j = 0; ok && j < ntiles && !*abort_flag; ++j) {
+            const int b = j % 3;
+            if (!tc_wait(p_full + b, (j / 3) & 1, abort_flag, a.err) || !wait_v(j)) break;
+            issue_pv(kSingleO, kTcRows * b, j);
+            umma_commit(vempty + j % NV);
+            umma_commit(o_done);
+            if (j + 2 < ntiles) {
+              if (!wait_k(j + 2)) break;
+              issue_s(kTcRows * ((j + 2) % 3), 0, j + 2);
+              umma_commit(s_full + (j + 2) % 3);
+              umma_commit(kempty + (j + 2) % NK);
             }
           }
         }
@@ -480,7 +487,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     mbar_arrive(q_ready);
     const bool active = x == 0 || two;
     const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t o_cols = tmem + lanes + col_o<DH>(x);
+    const uint32_t o_cols = tmem + lanes + (two ? col_o<DH>(x) : kSingleO);
     // kind 1: key position of the tile's first token, and this column's exclusive causal key limit
     const int first_pos = tile_unit ? __ldg(a.seq_lens + tseq) - (__ldg(a.qo + tseq + 1) - __ldg(a.qo + tseq)) +
                                           (mb - __ldg(a.qo + tseq))
@@ -501,10 +508,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       const int live_pages = min(kTcTilePages, npages - j * kTcTilePages);
       int my_bid = 0;
       if (lane < live_pages) my_bid = __ldg(table + pb + j * kTcTilePages + lane);
-      // S buffer of this tile: the tile's own (paired) or tile j's of the two (single, double-buffered)
-      const int buf = two ? x : (j & 1);
-      const uint32_t s_cols = tmem + lanes + col_s(buf);
-      if (!wait_warp(s_full + buf, two ? (j & 1) : ((j >> 1) & 1))) {
+      // S buffer of this tile: the tile's own (paired) or tile j's of the three (single)
+      const int buf = two ? x : j % 3;
+      const uint32_t s_cols = tmem + lanes + kTcRows * buf;  // col_s(x) = 128 x when paired
+      if (!wait_warp(s_full + buf, two ? (j & 1) : ((j / 3) & 1))) {
         ok = false;
         break;
       }
