@@ -169,15 +169,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
-// 32 lanes x 16 consecutive 32-bit columns
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // The compiler takes a tcgen05.ld's destination registers as written by the ld itself, so arithmetic on them
 // may be scheduled above tcgen05.wait::ld (the wait's memory clobber orders memory, not registers).  This
@@ -486,6 +477,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
     }
     mbar_arrive(q_ready);
     const bool active = x == 0 || two;
+    // this column's destination: an unsplit query tile writes its final row, everything else a split-K
+    // partial row (its index read now, off the epilogue's path)
+    const int out_m = row / a.group, out_head = kvh * a.group + row % a.group;
+    const bool final_rows = tile_unit && piece < 0;
+    bool out_live = active && out_m < mc;
+    int64_t out_slot = 0;
+    if (out_live && !final_rows) {
+      const int64_t prow = tile_unit ? tile_part_base + (static_cast<int64_t>(out_m) * tile_pieces + piece) * a.tile_tokens
+                                     : __ldg(&a.members[mb + out_m].part_base) + static_cast<int64_t>(piece) * a.tile_tokens;
+      out_slot = prow * a.h + out_head;
+      if (out_slot < 0 || out_slot >= a.part_rows * a.h) {  // a plan inconsistent with the workspace
+        flag_error(a.err, MLB_DEV_BLOCK_RANGE);
+        out_live = false;
+      }
+    }
     const uint32_t lanes = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t o_cols = tmem + lanes + (two ? col_o<DH>(x) : kSingleO);
     // kind 1: key position of the tile's first token, and this column's exclusive causal key limit
@@ -625,48 +631,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) shared_prefix_tc_kernel(AttnArg
       tc_fence_before();
       mbar_arrive(p_full + buf);
     }
-    // O is complete when final_bar (committed once, after every MMA) arrives
+    // O is complete when final_bar (committed once, after every MMA) arrives; the whole O row comes out of
+    // TMEM in one go (Dh / 32 loads, one wait), and the row's destination was worked out before the tiles
     if (active && ok && ntiles > 0 && wait_warp(final_bar, 0) && !*abort_flag) {
       tc_fence_after();
-      const int m = row / a.group;
-      const int head = kvh * a.group + row % a.group;
-      bool live = m < mc;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      // an unsplit query tile writes its final rows; everything else writes a split-K partial row
-      const bool final_rows = tile_unit && piece < 0;
-      int64_t slot = 0;
-      if (live && !final_rows) {
-        const int64_t prow = tile_unit ? tile_part_base + (static_cast<int64_t>(m) * tile_pieces + piece) * a.tile_tokens
-                                       : __ldg(&a.members[mb + m].part_base) + static_cast<int64_t>(piece) * a.tile_tokens;
-        slot = prow * a.h + head;
-        if (slot < 0 || slot >= a.part_rows * a.h) {  // a plan inconsistent with the workspace
-          flag_error(a.err, MLB_DEV_BLOCK_RANGE);
-          live = false;
+      uint32_t orow[DH];
+#pragma unroll
+      for (int i = 0; i < DH / 32; ++i) tmem_ld32(o_cols + 32 * i, orow + 32 * i);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < DH / 32; ++i) tmem_pin32(orow + 32 * i);
+      if (out_live && final_rows) {
+#pragma unroll
+        for (int k = 0; k < DH / 8; ++k) {
+          float v8[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v8[e] = __uint_as_float(orow[8 * k + e]) * inv;
+          store_out_n<DT, 8>(a.out, a.out_vec != 0, mb + out_m, out_head, 8 * k, v8);
         }
+      } else if (out_live) {
+        float4* dst = reinterpret_cast<float4*>(a.part_o + out_slot * DH);
+#pragma unroll
+        for (int k = 0; k < DH / 4; ++k)
+          dst[k] = make_float4(__uint_as_float(orow[4 * k]) * inv, __uint_as_float(orow[4 * k + 1]) * inv,
+                               __uint_as_float(orow[4 * k + 2]) * inv, __uint_as_float(orow[4 * k + 3]) * inv);
+        a.part_lse[out_slot] = l > 0.f ? m_used + log2f(l) : kNegInfF;
       }
-#pragma unroll
-      for (int i = 0; i < DH / 32; ++i) {
-        uint32_t orow[32];
-        tmem_ld32(o_cols + 32 * i, orow);
-        tmem_wait_ld();
-        tmem_pin32(orow);
-        if (live && final_rows) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            float v8[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v8[e] = __uint_as_float(orow[8 * k + e]) * inv;
-            store_out_n<DT, 8>(a.out, a.out_vec != 0, mb + m, head, 32 * i + 8 * k, v8);
-          }
-        } else if (live) {
-          float4* dst = reinterpret_cast<float4*>(a.part_o + slot * DH + 32 * i);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            dst[k] = make_float4(__uint_as_float(orow[4 * k]) * inv, __uint_as_float(orow[4 * k + 1]) * inv,
-                                 __uint_as_float(orow[4 * k + 2]) * inv, __uint_as_float(orow[4 * k + 3]) * inv);
-        }
-      }
-      if (live && !final_rows) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : kNegInfF;
     }
   }
 
