@@ -438,9 +438,10 @@ class Rig:
     @property
     def launches_per_layer(self) -> int:
         # [append,] attention (+ shared-prefix attention), split-K reduction (p2p: always, carrying the gather)
-        # [+ p2p barrier]
+        # [+ p2p barrier after plain stores]
         return ((1 if self.fused else 2) + (1 if self.plan.num_shared_units else 0)
-                + (1 if self.plan.num_partial_rows or self.p2p else 0) + (1 if self.p2p else 0))
+                + (1 if self.plan.num_partial_rows or self.p2p else 0)
+                + (1 if self.p2p and not self.peers.use_packets(self.n_q) else 0))
 
 
 def make_rig(args, mlb, sharding, wl: Workload, dev, rank: int, world: int, layers: int) -> Rig:
@@ -489,7 +490,7 @@ def make_rig(args, mlb, sharding, wl: Workload, dev, rank: int, world: int, laye
              and ops.can_fuse_append(plan, k_pools[0], k_l, v_l))
     return Rig(wl, layers, rank, world, dev, hkv_l, h_l, qs, ks, k_pools, v_pools, q, q_l, k_l, v_l, meta_att,
                meta_app, plan, ops.Workspace(), torch.empty(n_q, h_l, DH, device=dev, dtype=torch.bfloat16), p2p,
-               sharding.PeerOutputs(n_q, H, DH, torch.bfloat16, dev) if p2p else None,
+               sharding.PeerOutputs(n_q, H, DH, torch.bfloat16, dev, exchange=args.exchange) if p2p else None,
                torch.empty(world * n_q, h_l, DH, device=dev, dtype=torch.bfloat16) if world > 1 and not p2p else None,
                copies, ptrs, src, dst, fused, n_q, n_app, ops, not args.no_pdl)
 
@@ -503,10 +504,14 @@ def attend(r: Rig, l: int) -> None:
 
 
 def gather_step(r: Rig, l: int) -> None:
-    """The layer's split-K reduction and output all-gather: p2p = the reduction storing every row into every
-    rank's buffer + the flag barrier; NCCL = the local reduction + all_gather_into_tensor."""
+    """The layer's split-K reduction and output all-gather: p2p = the reduction sending every row to every
+    rank as flagged packets and receiving theirs (one launch), or storing every row into every rank's buffer
+    followed by the flag barrier; NCCL = the local reduction + all_gather_into_tensor."""
     if r.p2p:
         slot = l % r.peers.slots
+        if r.peers.use_packets(r.n_q):
+            r.ops.splitk_reduce_exchange(r.plan, r.ws, r.peers, slot, torch.bfloat16, DH, r.dev)
+            return
         r.ops.splitk_reduce_gather(r.plan, r.ws, r.peers.targets(slot, r.qs.start), r.peers.self_dest,
                                    torch.bfloat16, DH, r.dev)
         r.peers.barrier()
@@ -676,6 +681,8 @@ def workload_summary(r: Rig, t: dict, peak: float, check: float, sample: list[in
            "spot_check_passed": bool(check <= 2e-2), **{k: v for k, v in r.wl.info.items() if k != "evicted"}}
     if "gather_ms" in t:
         out["gather_barrier_us_per_layer"] = round(t["gather_ms"] * 1e3, 2)
+        if r.p2p:
+            out["gather"] = "flagged packets" if r.peers.use_packets(r.n_q) else "stores + flag barrier"
     if r.wl.name == "config 4":  # shared prefix: HBM sees each shared block once per launch, so the roofline
         unique = r.wl.unique_pages() * BS * 2 * r.hkv_l * DH * 2  # fraction counts unique bytes
         out["logical_gbs_per_rank"] = round(achieved, 1)
@@ -789,6 +796,8 @@ def run_ours(args) -> None:
     headline = {"gather_ms": t.get("gather_ms"), "copy_ms": t.get("copy_ms")}
     launches = r.launches_per_layer * layers * args.steps + (args.steps if r.copies else 0)
     fused, plan, n_q, n_app, copies = r.fused, r.plan, r.n_q, r.n_app, r.copies
+    gather_mode = (("flagged packets" if r.peers.use_packets(r.n_q) else "stores + flag barrier") if r.p2p
+                   else "NCCL all-gather")
     release(r)
     del r
 
@@ -829,7 +838,9 @@ def run_ours(args) -> None:
                        "query_tokens": n_q, "appended_tokens": n_app, "sum_ctx": int(np.sum(ctx)),
                        "pool_blocks": wl.num_blocks,
                        "parallelism": (f"kv-head shard x{world}, output gather: "
-                                       + ("kernel NVLink stores + flag barrier" if p2p else "NCCL all-gather"))
+                                       + ((f"kernel NVLink stores, exchange={args.exchange} (flagged packets up to "
+                                           f"{sharding.PACKET_BYTES_PER_PEER >> 10} KB per peer, else stores + flag "
+                                           "barrier)") if p2p else "NCCL all-gather"))
                                       if world > 1 else "single GPU",
                        "l2": "no flush: every layer's pool reads exceed the 126 MB L2",
                        "host_binding": (f"each rank pinned to its GPU's NVML-local CPUs ({len(cpus)} on rank 0)"
@@ -862,6 +873,7 @@ def run_ours(args) -> None:
             line["roofline"]["traffic_note"] = ("DRAM traffic is captured with ncu on one GPU (config 2, N=1); not "
                                                 "captured per rank at N>1")
             line["gather_barrier_us_per_layer"] = round(headline["gather_ms"] * 1e3, 2)
+            line["gather"] = gather_mode
         if args.config == 4:
             unique = wl.unique_pages() * BS * 2 * (HKV // world) * DH * 2
             line["roofline"]["unique_bytes"] = unique
@@ -943,7 +955,7 @@ def run_e2e(args, mlb, sharding, wl: Workload, q, k, v, k_pools, v_pools, dev, w
     inner_backend = mlb.B200Backend(pages_per_unit=args.pages_per_unit)
     # p2p: one gathered-output slot per layer and step, two steps' worth: step n writes slots of parity n % 2
     backend = (sharding.KVHeadShardedBackend(inner_backend, transport=args.transport,
-                                             slots=2 * layers if p2p_ring else 2)
+                                             slots=2 * layers if p2p_ring else 2, exchange=args.exchange)
                if world > 1 else inner_backend)
     # outputs come back in 4 shrinking chunks (a side-stream copy per layer costs ~60 us of host time: 32 per
     # step made the step host-bound)
@@ -1137,6 +1149,9 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="config 2 sequences per GPU-set (see --scaling)")
     ap.add_argument("--transport", choices=["p2p", "nccl"], default="p2p",
                     help="N>1: output all-gather by the kernels' own NVLink stores + a flag barrier (p2p), or NCCL")
+    ap.add_argument("--exchange", choices=["auto", "packets", "barrier"], default="auto",
+                    help="p2p: rows to the peers as flagged packets in the reduction's launch (packets), plain "
+                         "stores followed by a flag-barrier launch (barrier), or by the step's size (auto)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="N>1, config 2: weak = batch x N sequences (each rank keeps one GPU's KV bytes); "
                          "strong = the same batch split by KV heads (configs 3-5 are always strong)")

@@ -48,7 +48,7 @@ enum {
 MLB_API const char* mlb_last_error(void);
 
 /* ABI version (bumped on any signature change). */
-MLB_API int mlb_abi_version(void);  /* 9 */
+MLB_API int mlb_abi_version(void);  /* 10 */
 
 /*
  * Programmatic dependent launch (process-wide, default on): every kernel is launched with programmatic
@@ -360,6 +360,29 @@ MLB_API int mlb_splitk_reduce_gather(const float* partial_o, const float* partia
                       const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,
                       int64_t num_tokens, int num_heads, int head_dim, int out_dtype,
                       const mlb_out_targets* out_targets, int self_dest, void* stream);
+
+/*
+ * The same all-gather without the barrier: one launch that finishes this rank's rows, sends them to every
+ * peer and waits for the peers' rows.  Each 32-bit word of a row goes to a peer as one 8-byte packet
+ * {word, epoch} (single-copy-atomic store), so a row is complete when its packets carry the current
+ * epoch: no system-scope fence and no flag round trip, at twice the NVLink bytes of
+ * mlb_splitk_reduce_gather.  Call it after mlb_paged_attention left this rank's unsplit rows in `out`
+ * (this rank's gathered [num_tokens, world * num_heads, head_dim] buffer, element strides, rows 4-byte
+ * aligned), heads [rank * num_heads, (rank + 1) * num_heads).  packets: 2 x world addresses,
+ * packets[a * world + p] = rank p's packet area a (this rank's own, the others from mlb_ipc_open), each
+ * packet_capacity x world x num_heads x (head_dim x element bytes / 4) uint64, zero when allocated.  Calls
+ * alternate between the two areas by the epoch's parity (a peer may still be reading the previous call's).
+ * state: this rank's two uint32 device words {epoch, arrivals}, zero at the start and advanced by the
+ * kernel (CUDA-graph replays stay in step).  Each wait gives up after timeout_ns (0: 2 s) and ORs MLB_DEV_WAIT_TIMEOUT into
+ * *err_word.  Every rank must make the same sequence of calls.  No reference counterpart (it replaces the
+ * NCCL all-gather of KV-head sharding).
+ */
+MLB_API int mlb_splitk_reduce_exchange(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                      const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile,
+                      int64_t num_tokens, int num_heads, int head_dim, int out_dtype, void* out,
+                      int64_t out_stride_tok, int64_t out_stride_head, void* const* packets,
+                      int64_t packet_capacity, int rank, int world, uint32_t* state, int64_t timeout_ns,
+                      int32_t* err_word, void* stream);
 
 #ifdef __cplusplus
 }

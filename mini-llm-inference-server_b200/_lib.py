@@ -22,8 +22,8 @@ EXPORTS = ("mlb_last_error", "mlb_abi_version", "mlb_kv_append", "mlb_plan_atten
            "mlb_splitk_reduce", "mlb_block_copy", "mlb_paged_attention_noalloc", "mlb_ipc_alloc", "mlb_ipc_open",
            "mlb_ipc_close", "mlb_ipc_free", "mlb_peer_barrier", "mlb_set_programmatic_launch",
            "mlb_splitk_reduce_gather", "mlb_set_tensor_core_prefix", "mlb_paged_attention_append",
-           "mlb_build_metadata", "mlb_set_concurrent_prefix")
-ABI_VERSION = 9
+           "mlb_build_metadata", "mlb_set_concurrent_prefix", "mlb_splitk_reduce_exchange")
+ABI_VERSION = 10
 NOALLOC_SCRATCH_BYTES = 8 << 20  # MLB_NOALLOC_SCRATCH_BYTES
 MAX_OUT_DESTS = 8  # MLB_MAX_OUT_DESTS
 IPC_HANDLE_BYTES = 64  # MLB_IPC_HANDLE_BYTES
@@ -108,6 +108,9 @@ _SIGNATURES = {
     "mlb_peer_barrier": (c_int, [POINTER(c_void_p), c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
     "mlb_splitk_reduce_gather": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
                                          c_int, c_int, POINTER(OutTargets), c_int, c_void_p]),
+    "mlb_splitk_reduce_exchange": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int64, c_int,
+                                           c_int, c_int, c_void_p, c_int64, c_int64, POINTER(c_void_p), c_int64,
+                                           c_int, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

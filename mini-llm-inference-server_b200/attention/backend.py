@@ -26,7 +26,7 @@ import torch.nn.functional as F
 
 from .. import _lib
 from ..ops import (AttentionPlan, Workspace, attention_partials, can_fuse_append, kv_append, paged_attention,
-                   plan_attention, splitk_reduce_gather)
+                   plan_attention, splitk_reduce_exchange, splitk_reduce_gather)
 from .base import AttentionBackend
 from .metadata import host_view
 
@@ -109,8 +109,8 @@ class B200Backend(AttentionBackend):
     def forward(self, q, k, v, k_cache, v_cache, meta, out_targets=None, peer_gather=None):
         """out_targets (optional, `ops.out_targets`): store the output rows there and return None.
         peer_gather (optional, `(PeerOutputs, slot, head_offset)`, used by KV-head sharding): put every row
-        in every rank's gathered buffer of that slot (the reduction carries the all-gather), then the
-        peers' barrier."""
+        in every rank's gathered buffer of that slot (the reduction carries the all-gather: as flagged
+        packets, or plain stores followed by the peers' barrier, as the PeerOutputs was built)."""
         if k_cache.shape[1] != meta.block_size:
             raise ValueError(f"pool block size {k_cache.shape[1]} != metadata block size {meta.block_size}")
         err = self._error_word(q.device) if self.check_errors else None
@@ -126,9 +126,12 @@ class B200Backend(AttentionBackend):
             attention_partials(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan,
                                self._workspace, err=err, targets=peers.local_targets(slot, head_offset),
                                append=append)
-            splitk_reduce_gather(plan, self._workspace, peers.targets(slot, head_offset), peers.self_dest, q.dtype,
-                                 q.shape[2], q.device)
-            peers.barrier()
+            if peers.use_packets(q.shape[0]):
+                splitk_reduce_exchange(plan, self._workspace, peers, slot, q.dtype, q.shape[2], q.device)
+            else:
+                splitk_reduce_gather(plan, self._workspace, peers.targets(slot, head_offset), peers.self_dest,
+                                     q.dtype, q.shape[2], q.device)
+                peers.barrier()
             out = None
         else:
             out = paged_attention(q, k_cache, v_cache, meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr,

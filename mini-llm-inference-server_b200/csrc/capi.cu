@@ -28,6 +28,11 @@ cudaError_t launch_splitk_reduce(const float* po, const float* plse, const int32
 cudaError_t launch_splitk_reduce_gather(const float* po, const float* plse, const int32_t* rrows,
                                         const int32_t* rchunks, int tpt, int64_t ntok, int h, int dh,
                                         const mlb_out_targets& out, int self, int out_dtype, cudaStream_t s);
+cudaError_t launch_splitk_reduce_exchange(const float* po, const float* plse, const int32_t* rrows,
+                                          const int32_t* rchunks, int tpt, int64_t ntok, int h, int dh, int out_dtype,
+                                          void* out, int64_t out_st, int64_t out_sh, void* const* packets, int rank,
+                                          int world, uint32_t* state, int64_t timeout_ns, int32_t* err, int num_sms,
+                                          cudaStream_t s);
 cudaError_t launch_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes,
                               const int32_t* src, const int32_t* dst, int64_t num_pairs, int32_t* err, int num_sms,
                               cudaStream_t s);
@@ -236,7 +241,7 @@ extern "C" {
 
 const char* mlb_last_error(void) { return g_last_error.c_str(); }
 
-int mlb_abi_version(void) { return 9; }
+int mlb_abi_version(void) { return 10; }
 
 int mlb_set_programmatic_launch(int enable) {
   return mlb::g_programmatic_launch.exchange(enable ? 1 : 0, std::memory_order_relaxed);
@@ -723,6 +728,42 @@ int mlb_splitk_reduce_gather(const float* partial_o, const float* partial_lse, i
                                                       tokens_per_tile_, num_tokens, num_heads, head_dim, targets,
                                                       self_dest, out_dtype, static_cast<cudaStream_t>(stream)),
                      "splitk_reduce_gather launch");
+}
+
+int mlb_splitk_reduce_exchange(const float* partial_o, const float* partial_lse, int64_t num_partial_rows,
+                               const int32_t* reduce_rows, const int32_t* reduce_chunks, int tokens_per_tile_,
+                               int64_t num_tokens, int num_heads, int head_dim, int out_dtype, void* out,
+                               int64_t out_stride_tok, int64_t out_stride_head, void* const* packets,
+                               int64_t packet_capacity, int rank, int world, uint32_t* state, int64_t timeout_ns,
+                               int32_t* err_word, void* stream) {
+  const int eb = elt_bytes(out_dtype);
+  if (!eb) return fail(MLB_EINVAL, "splitk_reduce_exchange: unknown dtype %d", out_dtype);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return fail(MLB_EUNSUPPORTED, "splitk_reduce_exchange: head_dim %d", head_dim);
+  if (world < 1 || world > MLB_MAX_OUT_DESTS || rank < 0 || rank >= world)
+    return fail(MLB_EINVAL, "splitk_reduce_exchange: rank %d of %d (1..%d ranks)", rank, world, MLB_MAX_OUT_DESTS);
+  if (num_tokens < 0 || num_heads <= 0 || tokens_per_tile_ <= 0 || num_partial_rows < 0 || timeout_ns < 0)
+    return fail(MLB_EINVAL, "splitk_reduce_exchange: bad sizes");
+  if (num_tokens > packet_capacity)
+    return fail(MLB_EINVAL, "splitk_reduce_exchange: %lld tokens > packet capacity %lld",
+                static_cast<long long>(num_tokens), static_cast<long long>(packet_capacity));
+  if (!out || !packets || !state) return fail(MLB_EINVAL, "splitk_reduce_exchange: null pointer");
+  for (int p = 0; p < 2 * world; ++p)
+    if (!packets[p]) return fail(MLB_EINVAL, "splitk_reduce_exchange: packet area %d of rank %d is null", p / world,
+                                 p % world);
+  // every lane moves head_dim / 32 elements as whole 32-bit words: rows 4-byte aligned
+  if ((reinterpret_cast<uintptr_t>(out) | static_cast<uintptr_t>(out_stride_tok * eb) |
+       static_cast<uintptr_t>(out_stride_head * eb)) & 3)
+    return fail(MLB_EUNSUPPORTED, "splitk_reduce_exchange: out rows must be 4-byte aligned");
+  if (num_tokens == 0) return MLB_OK;
+  if (num_partial_rows > 0 && (!partial_o || !partial_lse || !reduce_rows || !reduce_chunks))
+    return fail(MLB_EINVAL, "splitk_reduce_exchange: null pointer");
+  return cuda_status(mlb::launch_splitk_reduce_exchange(
+                         partial_o, partial_lse, reduce_rows, num_partial_rows > 0 ? reduce_chunks : nullptr,
+                         tokens_per_tile_, num_tokens, num_heads, head_dim, out_dtype, out, out_stride_tok,
+                         out_stride_head, packets, rank, world, state, timeout_ns > 0 ? timeout_ns : 2000000000LL,
+                         err_word, sm_count(), static_cast<cudaStream_t>(stream)),
+                     "splitk_reduce_exchange launch");
 }
 
 int mlb_block_copy(void* const* pools, int num_pools, int64_t num_blocks, int64_t block_bytes, const int32_t* src,

@@ -810,6 +810,132 @@ __global__ void __launch_bounds__(256) splitk_reduce_gather_kernel(const float* 
   }
 }
 
+// The split-K reduction carrying the output all-gather as flagged packets, with no barrier kernel after
+// it.  Every 32-bit word of a row travels to each peer as one 64-bit packet {word, epoch}, stored with
+// one single-copy-atomic 8-byte store, so a receiver that reads the packet with the current epoch holds
+// that word: no fence, no flag round trip.  Phase 1 (send): one warp per (token, head of this rank),
+// grid-stride: finish the row (reduce a split token, or read the unsplit row the attention kernel left
+// in this rank's own buffer) and store its packets into every peer's packet area.  Phase 2 (receive): the
+// same warp waits (bounded) for the packets of the same (token, head index) from every peer in this
+// rank's area and writes those rows into its own buffer.  The grid is at most one CTA per SM, so every
+// CTA is resident and all ranks' warps make progress.  The epoch (state[0]) is read by every CTA first
+// and advanced by the last CTA to finish (state[1] counts arrivals).  Calls alternate between two packet
+// areas by the epoch's parity: a peer may still be reading the area of the call before (a rank finishes a
+// call once it holds every peer's rows, not once every peer holds its), never the one of two calls back.
+struct ExchangeArgs {
+  const float* po;
+  const float* plse;
+  const int32_t* rrows;
+  const int32_t* rchunks;
+  int tpt, h, rank, world;
+  int64_t ntok;
+  char* out;  // this rank's gathered rows [ntok, world * h, DH] (element strides below)
+  int64_t out_st, out_sh;
+  uint64_t* packets[2][MLB_MAX_OUT_DESTS];  // area a of rank p: [ntok][world][h][row words]
+  uint32_t* state;                       // this rank's {epoch, arrivals}
+  int64_t timeout_ns;
+  int32_t* err;
+};
+
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int DH, int OUT_DT>
+__global__ void __launch_bounds__(256) splitk_reduce_exchange_kernel(const ExchangeArgs x) {
+  constexpr int EB = Elt<OUT_DT>::bytes;
+  constexpr int DPL = DH / 32;       // output elements per lane
+  constexpr int WPL = DPL * EB / 4;  // 32-bit words per lane
+  constexpr int WPR = 32 * WPL;      // words per row
+  griddep_begin();
+  const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(x.state) + 1u;
+  const int area = static_cast<int>(e & 1u);
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t items = x.ntok * x.h;
+  auto row_at = [&](int64_t tok, int head) {
+    return x.out + (tok * x.out_st + static_cast<int64_t>(head) * x.out_sh + lane * DPL) * EB;
+  };
+  for (int64_t it = warp0; it < items; it += nwarps) {
+    const int64_t tok = it / x.h;
+    const int hl = static_cast<int>(it % x.h);
+    char* row = row_at(tok, x.rank * x.h + hl);
+    uint32_t w[WPL];
+    const int nc = x.rchunks ? x.rchunks[tok] : 1;
+    if (nc > 1) {
+      float acc[DPL];
+      reduce_token_head<DH>(x.po, x.plse, x.rrows[tok], nc, x.tpt, x.h, hl, lane, acc);
+      if constexpr (OUT_DT == MLB_F32) {
+#pragma unroll
+        for (int k = 0; k < DPL; ++k) w[k] = __float_as_uint(acc[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < DPL / 2; ++k) {
+          const uint32_t lo = OUT_DT == MLB_BF16 ? f32_to_bf16_bits(acc[2 * k]) : f32_to_f16_bits(acc[2 * k]);
+          const uint32_t hi = OUT_DT == MLB_BF16 ? f32_to_bf16_bits(acc[2 * k + 1]) : f32_to_f16_bits(acc[2 * k + 1]);
+          w[k] = lo | (hi << 16);
+        }
+      }
+      store_bytes<DPL * EB>(row, w);
+    } else {
+      load_bytes<DPL * EB>(row, w);
+    }
+    const int64_t at = ((tok * x.world + x.rank) * x.h + hl) * WPR + lane * WPL;
+#pragma unroll
+    for (int p = 0; p < MLB_MAX_OUT_DESTS; ++p) {
+      if (p >= x.world || p == x.rank) continue;
+#pragma unroll
+      for (int i = 0; i < WPL; ++i)
+        st_relaxed_sys_u64(x.packets[area][p] + at + i, (static_cast<uint64_t>(e) << 32) | w[i]);
+    }
+  }
+  // receive: one deadline for the whole phase, so a missing peer costs one timeout, not one per row
+  const uint64_t* mine = nullptr;
+#pragma unroll
+  for (int p = 0; p < MLB_MAX_OUT_DESTS; ++p)
+    if (p == x.rank) mine = x.packets[area][p];
+  const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(x.timeout_ns);
+  bool late = false;
+  for (int64_t it = warp0; it < items && !late; it += nwarps) {
+    const int64_t tok = it / x.h;
+    const int hl = static_cast<int>(it % x.h);
+    for (int p = 0; p < x.world && !late; ++p) {
+      if (p == x.rank) continue;
+      const uint64_t* src = mine + ((tok * x.world + p) * x.h + hl) * WPR + lane * WPL;
+      uint32_t w[WPL];
+#pragma unroll
+      for (int i = 0; i < WPL; ++i) {
+        uint64_t v = ld_relaxed_sys_u64(src + i);
+        for (uint32_t polls = 1; static_cast<uint32_t>(v >> 32) != e; ++polls) {
+          if ((polls & 63) == 0 && (globaltimer_ns() > deadline || polls >= (1u << 26))) {
+            late = true;
+            break;
+          }
+          v = ld_relaxed_sys_u64(src + i);
+        }
+        w[i] = static_cast<uint32_t>(v);
+      }
+      if (!late) store_bytes<DPL * EB>(row_at(tok, p * x.h + hl), w);
+    }
+  }
+  if (late) flag_error(x.err, MLB_DEV_WAIT_TIMEOUT);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(x.state + 1, 1u) == gridDim.x - 1) {  // every CTA has read the epoch
+      x.state[1] = 0u;
+      x.state[0] = e;
+      __threadfence();
+    }
+  }
+}
+
 // Opt in to > 48 KB of dynamic shared memory once per kernel instance and device (`done` is the
 // caller's per-instance bit set of device ordinals < 64).
 template <typename K>
@@ -918,6 +1044,41 @@ cudaError_t launch_splitk_reduce_gather(const float* po, const float* plse, cons
   MLB_REDG(128, MLB_F32) MLB_REDG(128, MLB_F16) MLB_REDG(128, MLB_BF16)
   MLB_REDG(256, MLB_F32) MLB_REDG(256, MLB_F16) MLB_REDG(256, MLB_BF16)
 #undef MLB_REDG
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_splitk_reduce_exchange(const float* po, const float* plse, const int32_t* rrows,
+                                          const int32_t* rchunks, int tpt, int64_t ntok, int h, int dh, int out_dtype,
+                                          void* out, int64_t out_st, int64_t out_sh, void* const* packets, int rank,
+                                          int world, uint32_t* state, int64_t timeout_ns, int32_t* err, int num_sms,
+                                          cudaStream_t s) {
+  ExchangeArgs x{};
+  x.po = po;
+  x.plse = plse;
+  x.rrows = rrows;
+  x.rchunks = rchunks;
+  x.tpt = tpt;
+  x.h = h;
+  x.rank = rank;
+  x.world = world;
+  x.ntok = ntok;
+  x.out = static_cast<char*>(out);
+  x.out_st = out_st;
+  x.out_sh = out_sh;
+  for (int a = 0; a < 2; ++a)
+    for (int p = 0; p < world; ++p) x.packets[a][p] = static_cast<uint64_t*>(packets[a * world + p]);
+  x.state = state;
+  x.timeout_ns = timeout_ns;
+  x.err = err;
+  // one warp per (token, head) up to one CTA per SM: every CTA resident at once
+  const int64_t ctas = (ntok * h + 7) / 8;
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(ctas, num_sms)));
+#define MLB_EXCH(D, O) \
+  if (dh == D && out_dtype == O) return launch_k(splitk_reduce_exchange_kernel<D, O>, dim3(blocks), dim3(256), 0, s, x);
+  MLB_EXCH(64, MLB_F32) MLB_EXCH(64, MLB_F16) MLB_EXCH(64, MLB_BF16)
+  MLB_EXCH(128, MLB_F32) MLB_EXCH(128, MLB_F16) MLB_EXCH(128, MLB_BF16)
+  MLB_EXCH(256, MLB_F32) MLB_EXCH(256, MLB_F16) MLB_EXCH(256, MLB_BF16)
+#undef MLB_EXCH
   return cudaErrorInvalidValue;
 }
 

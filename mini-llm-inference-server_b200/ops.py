@@ -333,6 +333,25 @@ def splitk_reduce_gather(plan: AttentionPlan, workspace: Workspace, targets: Out
     check(rc, "splitk_reduce_gather")
 
 
+def splitk_reduce_exchange(plan: AttentionPlan, workspace: Workspace, peers, slot: int, dtype: torch.dtype,
+                           head_dim: int, device: torch.device, err: torch.Tensor | None = None) -> None:
+    """The output all-gather as flagged packets (mlb_splitk_reduce_exchange): after `attention_partials` left
+    this rank's unsplit rows in its own buffer of `slot` (`peers.local_targets`), one launch finishes this
+    rank's rows, sends them to every peer and waits for theirs; no barrier follows.  `peers` is the
+    `sharding.PeerOutputs` of the step (its packet areas and state words)."""
+    po = plse = None
+    if plan.num_partial_rows:
+        po, plse = workspace.get(plan.num_partial_rows, plan.num_heads, head_dim, device)
+    rc = lib().mlb_splitk_reduce_exchange(_ptr(po), _ptr(plse), plan.num_partial_rows, plan.reduce_rows.data_ptr(),
+                                          plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, plan.num_tokens,
+                                          plan.num_heads, head_dim, DTYPE_CODE[dtype], peers.slot_address(slot),
+                                          peers.num_heads * head_dim, head_dim, peers.packet_areas(),
+                                          peers.capacity, peers.rank, peers.world, peers.state_address,
+                                          peers.timeout_ns, peers.err.data_ptr() if err is None else err.data_ptr(),
+                                          _stream(device))
+    check(rc, "splitk_reduce_exchange")
+
+
 def _strides(out: torch.Tensor | None) -> tuple[int, int]:
     return (out.stride(0), out.stride(1)) if out is not None else (0, 0)
 

@@ -1,7 +1,7 @@
 """One rank of the two-GPU check in test_peer_gpu.py (run under torchrun): KV-head-sharded forward with the
-p2p output gather equals the NCCL all-gather bit for bit, over several forwards (both slots reused), from the
-full rows (`forward`) and from each rank's own heads (`forward_local`), and matches the fp32 oracle within
-the bf16 tolerance."""
+p2p output gather (flagged packets, and plain stores + barrier) equals the NCCL all-gather bit for bit, over
+several forwards (both slots and both packet areas reused), from the full rows (`forward`) and from each
+rank's own heads (`forward_local`), and matches the fp32 oracle within the bf16 tolerance."""
 
 from __future__ import annotations
 
@@ -28,7 +28,8 @@ def main() -> None:
     dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=60))
     mlb = import_module("mini-llm-inference-server_b200")
     sharding = import_module("mini-llm-inference-server_b200.sharding")
-    p2p = sharding.KVHeadShardedBackend(transport="p2p")
+    p2p = sharding.KVHeadShardedBackend(transport="p2p", exchange="packets")
+    p2b = sharding.KVHeadShardedBackend(transport="p2p", exchange="barrier")
     nccl = sharding.KVHeadShardedBackend(transport="nccl")
     for case in (cases.mixed_step(4, 32, 8, 128), cases.llama_decode(21, 6, 512, 4096), cases.boundaries(6, 32, 8, 64)):
         dtype = torch.bfloat16
@@ -43,14 +44,17 @@ def main() -> None:
             want = nccl.forward(t["q"], t["k"], t["v"], pools[2], pools[3], meta)
             assert torch.equal(got, want), f"rank {rank}: p2p gather differs from NCCL ({case.name})"
             assert_close(got, expected, dtype)
+            got = p2b.forward(t["q"], t["k"], t["v"], pools[0], pools[1], meta)
+            assert torch.equal(got, want), f"rank {rank}: p2p gather with barrier differs from NCCL ({case.name})"
             # the same step from this rank's own heads only (forward_local), both transports
             loc = p2p.forward_local(t["q"][:, qs].contiguous(), t["k"][:, ks].contiguous(),
                                     t["v"][:, ks].contiguous(), pools[0], pools[1], meta).clone()
             assert torch.equal(loc, want), f"rank {rank}: p2p forward_local differs ({case.name})"
             loc = nccl.forward_local(t["q"][:, qs], t["k"][:, ks], t["v"][:, ks], pools[2], pools[3], meta)
             assert torch.equal(loc, want), f"rank {rank}: NCCL forward_local differs ({case.name})"
-    p2p.peers.raise_errors()
-    p2p.close()
+    for b in (p2p, p2b):
+        b.peers.raise_errors()
+        b.close()
     dist.barrier()
     dist.destroy_process_group()
     print(f"rank {rank}: peer gather ok", flush=True)

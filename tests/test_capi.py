@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(L):
     for name in declared:
         assert hasattr(lib, name), name
     assert declared == set(L.EXPORTS)
-    assert lib.mlb_abi_version() == L.ABI_VERSION == 9
+    assert lib.mlb_abi_version() == L.ABI_VERSION == 10
 
 
 def test_plan_record_layouts_match_header(L):

@@ -1,8 +1,9 @@
 """The output gather of KV-head sharding on the GPU: attention rows stored into several destinations
 (mlb_out_targets) equal the plain output bit for bit in each; the reduction carrying the gather fills
-every destination; `PeerOutputs` over a one-rank group (IPC allocation, slot views, barrier); the flag
-barrier advances its device epoch under CUDA-graph replay, and its bounded wait runs out and reports
-MLB_DEV_WAIT_TIMEOUT when a peer never arrives (a flag nothing sets).
+every destination; `PeerOutputs` over a one-rank group (IPC allocation, slot views, barrier, the packet
+exchange); the flag barrier and the packet exchange advance their device epochs under CUDA-graph replay,
+and their bounded waits run out and report MLB_DEV_WAIT_TIMEOUT when a peer never arrives (a flag or a
+packet nothing writes).
 With two or more GPUs visible, `peer_worker.py` runs under torchrun and checks the p2p gather against the
 NCCL all-gather and the oracle."""
 
@@ -150,6 +151,85 @@ def test_peer_outputs_single_rank(mlb, cuda):
     finally:
         if own_group:
             dist.destroy_process_group()
+
+
+def _exchange(L, dt, plan, ws, out, n_heads, dh, areas, capacity, rank, world, state, timeout_ns, err):
+    po = plse = None
+    if plan.num_partial_rows:
+        po, plse = ws.get(plan.num_partial_rows, plan.num_heads, dh, out.device)
+    arr = (ctypes.c_void_p * len(areas))(*[a.data_ptr() for a in areas])
+    L.check(L.lib().mlb_splitk_reduce_exchange(
+        0 if po is None else po.data_ptr(), 0 if plse is None else plse.data_ptr(), plan.num_partial_rows,
+        plan.reduce_rows.data_ptr(), plan.reduce_chunks.data_ptr(), plan.tokens_per_tile, plan.num_tokens,
+        plan.num_heads, dh, dt, out.data_ptr(), out.stride(0), out.stride(1), arr, capacity, rank, world,
+        state.data_ptr(), timeout_ns, err.data_ptr(), torch.cuda.current_stream().cuda_stream), "splitk_reduce_exchange")
+
+
+def test_exchange_single_rank_finishes_rows_and_advances_its_epoch(mlb, cuda):
+    """One rank: the exchange has no peer to send to or wait for; it finishes the split rows into the own
+    buffer (bit-equal to the plain output) and advances its epoch once per call, also under graph replay."""
+    L = mlb._lib
+    case = cases.boundaries(6, 32, 8, 128)
+    t, meta, plan = _setup(mlb, case, torch.bfloat16, cuda, ppu=2)
+    assert plan.num_partial_rows > 0
+    ws = mlb.Workspace()
+    args = (t["q"], t["k_pool"], t["v_pool"], meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan, ws)
+    ref = mlb.paged_attention(*args)
+    n, h, dh = ref.shape
+    out = torch.full((n, h, dh), float("nan"), dtype=torch.bfloat16, device=cuda)
+    areas = [torch.zeros(n * h * dh * 2 * 2 // 8, dtype=torch.int64, device=cuda) for _ in range(2)]
+    state = torch.zeros(2, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    tg = mlb.ops.out_targets([out.data_ptr()], 0, h * dh, dh)
+
+    def step():
+        mlb.ops.attention_partials(*args, targets=tg)
+        _exchange(L, L.MLB_BF16, plan, ws, out, h, dh, areas, n, 0, 1, state, 0, err)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    assert torch.equal(bits(out), bits(ref)) and state.tolist() == [3, 0] and err.item() == 0
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step()
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    for _ in range(4):
+        g.replay()
+    torch.cuda.synchronize()
+    assert state.tolist() == [11, 0] and err.item() == 0
+    assert torch.equal(bits(out), bits(ref))
+
+
+def test_exchange_wait_runs_out_when_a_peer_never_sends(mlb, cuda):
+    """Rank 0 of 2 with every packet area local: rank 0's packets land in "rank 1's" area with epoch 1 (area
+    1 = the epoch's parity), nothing ever writes rank 1's packets into rank 0's area, so the wait gives up
+    after its limit (50 ms here) and says so in the error word; the epoch still advances."""
+    L = mlb._lib
+    case = cases.llama_decode(5, 3, 20, 120)
+    t, meta, plan = _setup(mlb, case, torch.bfloat16, cuda, ppu=0)
+    ws = mlb.Workspace()
+    args = (t["q"], t["k_pool"], t["v_pool"], meta.block_tables_i32, meta.seq_lens_i32, meta.qo_indptr, plan, ws)
+    n, h, dh = t["q"].shape
+    out = torch.zeros((n, 2 * h, dh), dtype=torch.bfloat16, device=cuda)
+    words = dh * 2 // 4  # 32-bit words per row
+    areas = [torch.zeros(n * 2 * h * words, dtype=torch.int64, device=cuda) for _ in range(4)]  # [area][rank]
+    state = torch.zeros(2, dtype=torch.int32, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    mlb.ops.attention_partials(*args, targets=mlb.ops.out_targets([out.data_ptr()], 0, 2 * h * dh, dh))
+    _exchange(L, L.MLB_BF16, plan, ws, out, h, dh, areas, n, 0, 2, state, 50_000_000, err)
+    torch.cuda.synchronize()
+    assert err.item() & L.DEV_WAIT_TIMEOUT
+    assert state.tolist() == [1, 0]
+    sent = areas[1 * 2 + 1].view(n, 2, h, words)  # area 1 of rank 1: rank 0's rows at sender index 0
+    assert (sent[:, 0] >> 32 == 1).all() and (sent[:, 1] == 0).all()
+    mine = out[:, :h].contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF  # rank 0's finished rows
+    assert torch.equal(sent[:, 0] & 0xFFFFFFFF, mine)
+    assert (areas[0] == 0).all() and (areas[1] == 0).all() and (areas[2] == 0).all()
 
 
 def _free_port() -> int:
