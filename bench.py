@@ -1055,12 +1055,14 @@ def run_e2e(args, mlb, sharding, wl: Workload, q, k, v, k_pools, v_pools, dev, w
     # three timed windows of `steps` steps each, the median reported: the eager path is the host's pace
     # when the host stalls (other jobs on the machine), and one stall must not stand for the path
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    windows = []
+    windows, host_loop = [], []
     state["host_ms"] = 0.0
     for _ in range(3):
         s.record()
+        t_loop = time.perf_counter()
         for _ in range(args.steps):
             step()
+        host_loop.append((time.perf_counter() - t_loop) * 1e3 / args.steps)
         compute.wait_stream(copier)  # the window ends when the last step's outputs are on the host
         e.record()
         torch.cuda.synchronize()
@@ -1078,6 +1080,7 @@ def run_e2e(args, mlb, sharding, wl: Workload, q, k, v, k_pools, v_pools, dev, w
     return {"value": round(total / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
             "window_ms_per_step": [round(w, 4) for w in windows],
             "host_build_plan_ms_per_step": round(host_build_ms, 3),
+            "host_issue_ms_per_step": round(max_over_ranks(statistics.median(host_loop), world, dev), 3),
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "metadata": ("reference-shaped object (the reference's AttentionMetadata fields only): host tables "
                          "derived by the backend" if reference_meta else "AttentionMetadata.build_arrays"),
