@@ -97,3 +97,31 @@ def test_a_rank_that_dies_fails_the_others_fast(tmp_path):
     with pytest.raises(mp.ProcessExitedException):
         mp.start_processes(_worker, args=(2, _free_port(), "die", path), nprocs=2, start_method="spawn")
     assert not os.path.exists(path)
+
+
+def test_exchange_auto_rule_and_argument_checks():
+    """exchange="auto" sends a step as flagged packets up to PACKET_BYTES_PER_PEER bytes of rows per peer
+    and as stores + barrier above (config 2 at 2 GPUs: 64 rows of 16 heads x 128 dims x 2 B = 256 KB ->
+    packets, 128 rows -> barrier); a fixed mode ignores the size; a bad mode is refused."""
+    from importlib import import_module
+
+    sharding = import_module(PACKAGE + ".sharding")
+    p = object.__new__(sharding.PeerOutputs)  # the rule alone: no IPC allocation
+    p._row_bytes = 16 * 128 * 2
+    p.exchange = "auto"
+    assert sharding.PACKET_BYTES_PER_PEER == 384 << 10
+    assert p.use_packets(64) and not p.use_packets(128)
+    p.exchange = "packets"
+    assert p.use_packets(1 << 20)
+    p.exchange = "barrier"
+    assert not p.use_packets(1)
+    own = not dist.is_initialized()
+    if own:
+        dist.init_process_group("gloo", store=dist.HashStore(), rank=0, world_size=1)
+    try:
+        with pytest.raises(ValueError, match="exchange"):
+            sharding.KVHeadShardedBackend(transport="p2p", exchange="fast")
+        assert sharding.KVHeadShardedBackend(transport="p2p").exchange == "auto"
+    finally:
+        if own:
+            dist.destroy_process_group()
