@@ -89,7 +89,7 @@ class PeerOutputs:
         self._epoch_off = self._flags_off + 128
         self._state_off = self._epoch_off + 128  # the packet exchange's {epoch, arrivals}
         self._packets_off = self._state_off + 128
-        # per slot: [capacity][world][H / world][Dh x elt / 4] packets of 8 bytes
+        # per packet area (two): [capacity][world][H / world][Dh x elt / 4] packets of 8 bytes
         self.packet_bytes = (-(-capacity * num_heads * head_dim * elt * 2 // 256) * 256) if exchange != "barrier" else 0
         self._row_bytes = num_heads // self.world * head_dim * elt  # one token's rows of this rank's heads
         total = self._packets_off + 2 * self.packet_bytes
