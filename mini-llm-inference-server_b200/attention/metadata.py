@@ -91,11 +91,15 @@ class AttentionMetadata:
 
     @classmethod
     def build_arrays(cls, num_cached: np.ndarray, num_new: np.ndarray, block_ids: np.ndarray,
-                     num_blocks: np.ndarray, block_size: int, device: torch.device | str) -> AttentionMetadata:
+                     num_blocks: np.ndarray, block_size: int, device: torch.device | str,
+                     expand_on: torch.cuda.Stream | None = None) -> AttentionMetadata:
         """`build` for an engine that keeps its block tables in arrays: num_cached / num_new / num_blocks are
         per sequence, block_ids every sequence's ids back to back (num_blocks[i] of them for sequence i).
         Skips turning Python lists of ids into an array, the bulk of `build`'s host time at large batches
-        (512 sequences, 75K ids: ~2 ms of the ~5 ms)."""
+        (512 sequences, 75K ids: ~2 ms of the ~5 ms).
+        expand_on (CUDA): the upload stays on the current stream, the expansion kernel runs on this stream
+        once the upload is in (an engine that uploads a step ahead on a side stream can expand on its compute
+        stream just before the step's first layer, instead of beside whatever that stream is running)."""
         device = torch.device(device)
         cached = np.ascontiguousarray(num_cached, dtype=np.int64)
         new = np.ascontiguousarray(num_new, dtype=np.int64)
@@ -138,7 +142,14 @@ class AttentionMetadata:
             upload = _to_device(np.concatenate([ids, ids_indptr, starts, ends, kv_indptr, last_len]), device)
             d64 = torch.empty(2 * n + s * width + s, dtype=torch.int64, device=device)
             d32 = torch.empty(s * width + 4 * s + 2 + int(kv_indptr[-1]), dtype=torch.int32, device=device)
-            ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
+            if expand_on is None:
+                ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
+            else:
+                expand_on.wait_stream(torch.cuda.current_stream(device))
+                for t in (upload, d64, d32):  # used on that stream too: not reused before it is done
+                    t.record_stream(expand_on)
+                with torch.cuda.stream(expand_on):
+                    ops.build_metadata(upload, ids.size, s, n, int(kv_indptr[-1]), width, block_size, d64, d32)
         else:
             table = np.zeros((s, width), dtype=np.int64)
             table[mask] = ids

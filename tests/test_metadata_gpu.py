@@ -73,3 +73,22 @@ def test_device_build_at_config_sizes(mlb, cuda):
     for wl in (bench.config2(), bench.config3()):
         for rows in {id(wl.attend_rows): wl.attend_rows, id(wl.append_rows): wl.append_rows}.values():
             _same(mlb, [mlb.SeqStep(c, n, b) for c, n, b in rows], 16, cuda)
+
+
+def test_build_arrays_expands_on_another_stream(mlb, cuda):
+    """build_arrays(expand_on=s): the upload on the current stream, the expansion kernel on s after it; every
+    field equals the build without it (config 3's rows: ragged tables, multi-token rows)."""
+    import bench
+
+    rows = bench.config3(attend_chunks=True).attend_rows
+    arrays = (np.array([c for c, _, _ in rows], dtype=np.int64), np.array([n for _, n, _ in rows], dtype=np.int64),
+              np.concatenate([np.asarray(b, dtype=np.int64) for _, _, b in rows]),
+              np.array([len(b) for _, _, b in rows], dtype=np.int64))
+    plain = mlb.AttentionMetadata.build_arrays(*arrays, 16, cuda)
+    side = torch.cuda.Stream(cuda)
+    loader = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(loader):
+        other = mlb.AttentionMetadata.build_arrays(*arrays, 16, cuda, expand_on=side)
+    side.synchronize()
+    for f in TENSORS:
+        assert torch.equal(getattr(plain, f).cpu(), getattr(other, f).cpu()), f
